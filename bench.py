@@ -1,0 +1,406 @@
+"""Batch-one Qwen3 decode benchmark on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config qwen3-8b] [--context 4096]
+
+Workload (N=1): the Qwen3-8B shape (seeded random-init bf16 weights, drawn on
+the GPU), batch 1, decoding at a 4096-token context: the KV cache holds 4096
+seeded random positions (the decode step's work does not depend on their
+values), then K timed greedy steps each attend over 4096+i positions. One
+step = the captured decode graph (embed -> 36 layers -> final norm -> LM head
+-> argmax, position += 1). Weights (15.1 GB) are far larger than L2, so every
+step streams them from HBM.
+
+* value      device-timed tok/s (CUDA events around K graph replays), max over ranks
+* e2e        the same K steps through the engine's state API with host buffers:
+             per step a pinned host->device token copy, the replay, a
+             device->host token copy and a stream sync (what generate() does)
+* roofline   dominant kernel (gate/up + SwiGLU GEMV) timed live with CUDA
+             events over all layers' weights, algorithmic bytes / duration
+* step_roofline  whole-step algorithmic bytes (weights + KV) / step time
+* cpu_baseline   the reference's eager path (Transformers Qwen3ForCausalLM,
+             bf16, DynamicCache) decoding at the same shape on the host cores
+* --impl reference  times only that CPU path (rank 0; other ranks exit 0)
+
+Multi-GPU (N>1, launched by torchrun): each rank runs an independent replica
+(the weak-scaling baseline; tensor parallelism is not in this build yet).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "batch-1 decode tok/s and % of HBM roofline (1/2/4/8 B200) vs reference CPU"
+
+
+def load_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        self.path = None
+        try:
+            props = torch.cuda.get_device_properties(device_index)
+            ident = str(getattr(props, "uuid", ""))
+            self.ident = ident if ident.startswith("GPU-") else (f"GPU-{ident}" if ident else str(device_index))
+        except Exception:
+            self.ident = str(device_index)
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(prefix="qb_clocks_", suffix=".csv")
+            os.close(fd)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.ident, f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.fh.close()
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 8:
+                    rows.append(parts)
+        os.unlink(self.path)
+        sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
+        mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = sorted({n for r in rows for n, v in zip(names, r[4:8]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows),
+                "power_w_max": max((float(r[2]) for r in rows if r[2].replace(".", "").isdigit()), default=None)}
+
+
+# ------------------------------------------------------------------ CPU arm
+def cpu_reference_decode(cfg, context: int, budget_s: float, max_steps: int = 64):
+    """Time the reference's eager path (HF Qwen3ForCausalLM, bf16, SDPA,
+    DynamicCache greedy loop) at this shape on the host cores: a KV cache of
+    ``context`` random positions, then greedy steps until ``budget_s``."""
+    from transformers import DynamicCache
+
+    from oracle import hf_eager
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    t0 = time.perf_counter()
+    model = hf_eager.build_hf_model(cfg, None)
+    gen = torch.Generator().manual_seed(0)
+    block = (torch.randn(1 << 20, generator=gen) * 0.02).to(torch.bfloat16)
+    with torch.no_grad():
+        for p in model.parameters():
+            flat = p.data.view(-1)
+            for s in range(0, flat.numel(), block.numel()):
+                n = min(block.numel(), flat.numel() - s)
+                flat[s:s + n].copy_(block[:n])
+        for name, p in model.named_parameters():
+            if "norm" in name:
+                p.data.fill_(1.0)
+    cache = DynamicCache()
+    shape = (1, cfg.n_kv_heads, context, cfg.head_dim)
+    for layer in range(cfg.n_layers):
+        k = torch.randn(shape, generator=gen).to(torch.bfloat16)
+        v = torch.randn(shape, generator=gen).to(torch.bfloat16)
+        cache.update(k, v, layer)
+    setup = time.perf_counter() - t0
+    tok = torch.tensor([[1]])
+    steps, times = 0, []
+    with torch.inference_mode():
+        t_start = time.perf_counter()
+        while steps < max_steps:
+            ts = time.perf_counter()
+            res = model(input_ids=tok, past_key_values=cache, use_cache=True, logits_to_keep=1)
+            cache = res.past_key_values
+            tok = res.logits[:, -1:].float().argmax(-1)
+            times.append(time.perf_counter() - ts)
+            steps += 1
+            if time.perf_counter() - t_start > budget_s and steps >= 2:
+                break
+    total = sum(times)
+    return {"value": steps / total, "unit": "tok/s", "cores": torch.get_num_threads(), "kind": "reference",
+            "sample": (f"Transformers {__import__('transformers').__version__} Qwen3ForCausalLM eager bf16 "
+                       f"(the reference's eager path, dryft/OPTIMIZATION_GUIDE.md:316-368), {cfg.name} shape, "
+                       f"{steps} greedy DynamicCache steps at context {context}..{context + steps - 1}, "
+                       f"median {1000 * statistics.median(times):.1f} ms/token; setup {setup:.0f}s untimed"),
+            "median_ms_per_token": 1000 * statistics.median(times)}
+
+
+# ------------------------------------------------------------------ GPU arm
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device(f"cuda:{local}"))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def time_dominant_kernel(engine, reps_per_layer=2):
+    """Gate/up + SwiGLU GEMV (about half of a step's bytes) launched alone over
+    every layer's weights in turn, timed with CUDA events on the launching
+    stream. Returns (average seconds per launch, algorithmic bytes per launch)."""
+    from hackthenorth_b200 import ops
+
+    cfg = engine.cfg
+    layers = engine.weights.layers
+    x = torch.randn(cfg.hidden, device=engine.device).to(torch.bfloat16)
+    for lw in layers[:3]:
+        ops.norm_projection(x, lw["post_norm"], lw["gu"], cfg.rms_eps, swiglu=True)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    n = 0
+    for _ in range(reps_per_layer):
+        for lw in layers:
+            ops.norm_projection(x, lw["post_norm"], lw["gu"], cfg.rms_eps, swiglu=True)
+            n += 1
+    e1.record(stream)
+    torch.cuda.synchronize()
+    sec = e0.elapsed_time(e1) / 1000.0 / n
+    nbytes = 2 * cfg.ffn * cfg.hidden * 2 + cfg.hidden * 2 * 2 + cfg.ffn * 2
+    return sec, nbytes
+
+
+def run_ours(args):
+    from hackthenorth_b200 import build as qbuild
+    from hackthenorth_b200.config import get_config
+    from hackthenorth_b200.engine import Engine
+
+    world, rank, local = dist_setup(args.gpus)
+    qbuild.build()
+    cfg = get_config(args.config)
+    dev = torch.device(f"cuda:{local}")
+    peak_gbs, peak_kind = load_peaks()
+    engine = Engine.from_random(cfg, seed=0, device=str(dev), init_device=str(dev))
+    torch.cuda.empty_cache()
+    ctx = args.context
+    total_steps = args.warmup + args.steps
+    state = engine.new_state(ctx, total_steps + 2, capacity=ctx + 2 * total_steps + 8)
+    gen = torch.Generator(device=dev).manual_seed(2)
+    for t in (state.keys, state.values):
+        for l in range(cfg.n_layers):
+            t[l, :, :ctx].normal_(generator=gen)
+    state.token.fill_(1)
+    state.position.fill_(ctx)
+    state.capture()
+    stream = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        state.step()
+    state.check()
+    state.position.fill_(ctx)
+    torch.cuda.synchronize()
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        state.step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    dev_s = e0.elapsed_time(e1) / 1000.0
+    clk = clocks.stop()
+    state.check()
+
+    # e2e: the same steps with host buffers (pinned H2D of the token, replay,
+    # D2H of the result, sync) — the per-token loop of generate().
+    state.position.fill_(ctx)
+    host_in = torch.tensor([1], dtype=torch.int64).pin_memory()
+    host_out = torch.empty(1, dtype=torch.int64).pin_memory()
+    torch.cuda.synchronize()
+    barrier(world)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(args.steps):
+        state.token.copy_(host_in, non_blocking=True)
+        state.step()
+        host_out.copy_(state.token, non_blocking=True)
+        stream.synchronize()
+        host_in.copy_(host_out)
+    f1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_s = f0.elapsed_time(f1) / 1000.0
+    state.check()
+
+    kern_s, kern_bytes = time_dominant_kernel(engine)
+
+    t_dev = max_over_ranks(dev_s, world)
+    t_e2e = max_over_ranks(e2e_s, world)
+    ms_step = 1000.0 * t_dev / args.steps
+    value = world * args.steps / t_dev
+    mean_ctx = ctx + (args.steps - 1) / 2.0
+    step_bytes = cfg.step_bytes(int(round(mean_ctx)))
+    achieved = kern_bytes / kern_s / 1e9
+    launches_per_step = 5 * cfg.n_layers + 1
+    out = {
+        "metric": METRIC,
+        "value": round(value, 3),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded random-init weights N(0,0.02); KV cache of seeded N(0,1) positions)",
+        "config": {"workload": f"{cfg.name}-shaped batch-1 greedy decode at context {ctx}",
+                   "model": cfg.name, "global_batch": world, "seq_len": ctx, "context": ctx,
+                   "parallelism": "none" if world == 1 else f"replicas x{world}",
+                   "l2": "inputs larger than L2 (weights stream %.1f GB per step)" % (cfg.weight_bytes_per_token() / 1e9)},
+        "roofline": {"bound": "hbm", "kernel": "gemv_kernel<EPI_SWIGLU> (post-norm + gate/up + SwiGLU)",
+                     "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
+                     "frac": round(achieved / peak_gbs, 4), "peak_source": peak_kind,
+                     "bytes_per_launch": kern_bytes, "us_per_launch": round(kern_s * 1e6, 2),
+                     "traffic": None},
+        "step_roofline": {"bytes_per_step": step_bytes, "achieved": round(step_bytes / (t_dev / args.steps) / 1e9, 1),
+                          "peak": peak_gbs, "unit": "GB/s",
+                          "frac": round(step_bytes / (t_dev / args.steps) / 1e9 / peak_gbs, 4),
+                          "roofline_tok_s": round(peak_gbs * 1e9 / step_bytes, 1)},
+        "e2e": {"value": round(world * args.steps / t_e2e, 3), "unit": "tok/s",
+                "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
+                "d2h_bytes_per_step": host_out.numel() * host_out.element_size()},
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clk,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        del state, engine
+        torch.cuda.empty_cache()
+        out["cpu_baseline"] = cpu_reference_decode(cfg, ctx, budget_s=args.cpu_budget)
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from hackthenorth_b200.config import get_config
+
+    cfg = get_config(args.config)
+    budget = max(10.0, min(120.0, 2.0 * args.steps))
+    cb = cpu_reference_decode(cfg, args.context, budget_s=budget, max_steps=args.warmup + args.steps)
+    out = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": round(cb["value"], 4),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(cb["median_ms_per_token"], 2),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": f"{cfg.name}-shaped batch-1 greedy decode at context {args.context}",
+                   "model": cfg.name, "global_batch": 1, "seq_len": args.context, "context": args.context,
+                   "parallelism": "none (host CPU)"},
+        "cpu_baseline": cb,
+        "e2e": {"value": round(cb["value"], 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out), flush=True)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--config", default="qwen3-8b")
+    ap.add_argument("--context", type=int, default=4096)
+    ap.add_argument("--cpu-budget", type=float, default=20.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,695 @@
+// qb.cu — C ABI of the B200 batch-one Qwen3 decode engine (see include/qb.h).
+//
+// One decode step is 5 launches per layer plus the head:
+//   gemv<STORE>     RMSNorm + QKV           (layer 0 also gathers the embedding)
+//   attn<PRO>       q/k norm + RoPE + KV append + split-KV attention + merge
+//   gemv<RESIDUAL>  o-proj + residual
+//   gemv<SWIGLU>    RMSNorm + gate/up + SiLU * up
+//   gemv<RESIDUAL>  down + residual
+//   gemv<ARGMAX>    final RMSNorm + LM head + greedy argmax, position += 1
+// every launch carries the programmatic-stream-serialization attribute, so in
+// a stream or a captured graph each kernel starts streaming its weights while
+// its predecessor drains.
+#include "../../include/qb.h"
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemv.cuh"
+
+using namespace qb;
+
+namespace {
+
+thread_local std::string g_last_error = "";
+
+// Per-CTA shared-memory budget of the GEMV: two CTAs of consecutive kernels
+// fit on one SM (228 KB), which is what lets PDL overlap them.
+constexpr size_t kGemvSmemBudget = 113 * 1024;
+constexpr int kMaxGemvStages = 8;
+constexpr size_t kOpScratchBytes = 16u << 20;
+
+// Op-level scratch layout (bytes).
+constexpr size_t kScrErr = 0;
+constexpr size_t kScrCounters = 256;       // unsigned[192]
+constexpr size_t kScrHeadVal = 1024;       // float[1024]
+constexpr size_t kScrHeadIdx = 5120;       // int[1024]
+constexpr size_t kScrAttnLse = 9216;       // float[16384]
+constexpr size_t kScrAttnO = 9216 + 65536; // float[...] up to the end
+constexpr int kMaxAttnCtas = 512;
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+int set_err(std::string* dst, int code, const std::string& msg) {
+  if (dst) *dst = msg;
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(std::string* dst, cudaError_t e, const char* what) {
+  return set_err(dst, QB_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+int sm_count_of(int device) {
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0) n = 148;
+  return n;
+}
+
+int current_sm_count() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return sm_count_of(dev);
+}
+
+bool pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("QB_PDL");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                      Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// ---------------------------------------------------------------- GEMV launch
+struct GemvPlan {
+  int grid, stages, max_rows;
+  size_t smem;
+};
+
+bool plan_gemv(int epi, int K, int rows, int sm_count, GemvPlan* p) {
+  const int rpu = gemv_rows_per_unit(epi);
+  const int units = rows / rpu;
+  if (units <= 0) return false;
+  p->grid = units < sm_count ? units : sm_count;
+  p->max_rows = ((units + p->grid - 1) / p->grid) * rpu;
+  const size_t fixed = gemv_smem_bytes(K, 0, p->max_rows);
+  int stages = 0;
+  if (fixed < kGemvSmemBudget) stages = (int)((kGemvSmemBudget - fixed) / (kGemvStageBytes + 16));
+  if (stages > kMaxGemvStages) stages = kMaxGemvStages;
+  if (stages < 2) stages = 2;
+  p->stages = stages;
+  p->smem = gemv_smem_bytes(K, stages, p->max_rows);
+  return p->smem <= 227 * 1024;
+}
+
+template <int EPI>
+cudaError_t launch_gemv(GemvArgs a, int sm_count, cudaStream_t st) {
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+    attr_done = true;
+  }
+  GemvPlan p;
+  if (!plan_gemv(EPI, a.K, a.rows, sm_count, &p)) return cudaErrorInvalidValue;
+  a.stages = p.stages;
+  a.max_rows = p.max_rows;
+  return launch_ex(gemv_kernel<EPI>, dim3(p.grid), dim3(kGemvThreads), p.smem, st, a);
+}
+
+GemvArgs gemv_args(const void* w, int K, int rows, const void* x, void* out, int* err) {
+  GemvArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.w = static_cast<const bf16*>(w);
+  a.K = K;
+  a.rows = rows;
+  a.x = static_cast<const bf16*>(x);
+  a.out = static_cast<bf16*>(out);
+  a.err = err;
+  return a;
+}
+
+// ----------------------------------------------------------- attention launch
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// Tensor map over one layer's cache viewed as [Hkv*cap rows][128 dims] bf16,
+// box [16 rows][64 dims], 128-byte swizzle; out-of-range rows read as zero.
+bool make_kv_map(CUtensorMap* m, const void* base, int hkv, int cap) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)kAttnD, (cuuint64_t)hkv * (cuuint64_t)cap};
+  cuuint64_t strides[1] = {(cuuint64_t)kAttnD * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)kAttnKeys};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int attn_splits_for(int hkv, int sm_count) {
+  int s = sm_count / hkv;
+  if (s < 1) s = 1;
+  return s;
+}
+
+template <int MT, bool PRO>
+cudaError_t launch_attn_t(const CUtensorMap& tk, const CUtensorMap& tv, const AttnArgs& a, cudaStream_t st) {
+  static bool attr_done = false;
+  const size_t smem = attn_smem_bytes(MT);
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(attn_kernel<MT, PRO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr_done = true;
+  }
+  return launch_ex(attn_kernel<MT, PRO>, dim3(a.Hkv * a.splits), dim3(kAttnThreads), smem, st, tk, tv, a);
+}
+
+cudaError_t launch_attn(const CUtensorMap& tk, const CUtensorMap& tv, const AttnArgs& a, bool pro, cudaStream_t st) {
+  const int rows = (a.Hq / a.Hkv) * a.Q;
+  if (pro) return launch_attn_t<1, true>(tk, tv, a, st);
+  if (rows <= 16) return launch_attn_t<1, false>(tk, tv, a, st);
+  return launch_attn_t<2, false>(tk, tv, a, st);
+}
+
+bool ptr_ok(const void* p) { return p != nullptr && (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+
+// =================================================================== context
+struct qb_ctx {
+  qb_config cfg;
+  int device = 0;
+  int tp_rank = 0, tp_size = 1;
+  int sm_count = 148;
+  std::vector<qb_layer_weights> layers;
+  const bf16* embed = nullptr;
+  const bf16* final_norm = nullptr;
+  const bf16* lm_head = nullptr;
+  bool weights_bound = false;
+  bool state_bound = false;
+  bf16* kc = nullptr;
+  bf16* vc = nullptr;
+  int cap = 0;
+  const bf16* cos = nullptr;
+  const bf16* sin = nullptr;
+  uint8_t* ws = nullptr;
+  size_t ws_bytes = 0;
+  int* err = nullptr;
+  unsigned* counters = nullptr;
+  float* head_val = nullptr;
+  int* head_idx = nullptr;
+  bf16 *xa = nullptr, *xb = nullptr, *qkv = nullptr, *attn = nullptr, *act = nullptr;
+  float* part_o = nullptr;
+  float* part_lse = nullptr;
+  int splits = 1;
+  std::vector<CUtensorMap> tmk, tmv;
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  std::string msg;
+};
+
+namespace {
+
+struct WsLayout {
+  size_t err, counters, head_val, head_idx, xa, xb, qkv, attn, act, part_lse, part_o, total;
+};
+
+WsLayout ws_layout(const qb_ctx* c) {
+  const qb_config& g = c->cfg;
+  WsLayout L;
+  size_t o = 0;
+  L.err = o; o += 256;
+  L.counters = o; o += 1024;
+  L.head_val = o; o = align_up(o + 4 * 1024, 256);
+  L.head_idx = o; o = align_up(o + 4 * 1024, 256);
+  L.xa = o; o = align_up(o + (size_t)g.hidden * 2, 256);
+  L.xb = o; o = align_up(o + (size_t)g.hidden * 2, 256);
+  L.qkv = o; o = align_up(o + (size_t)(g.n_heads + 2 * g.n_kv_heads) * g.head_dim * 2, 256);
+  L.attn = o; o = align_up(o + (size_t)g.n_heads * g.head_dim * 2, 256);
+  L.act = o; o = align_up(o + (size_t)g.ffn * 2, 256);
+  const size_t parts = (size_t)g.n_kv_heads * c->splits * 32;
+  L.part_lse = o; o = align_up(o + parts * 4, 256);
+  L.part_o = o; o = align_up(o + parts * kAttnD * 4, 256);
+  L.total = o;
+  return L;
+}
+
+int validate_config(const qb_config* g, std::string* msg) {
+  if (!g) return set_err(msg, QB_ERR_ARG, "config is NULL");
+  if (g->head_dim != 128) return set_err(msg, QB_ERR_UNSUPPORTED, "kernels implement head_dim == 128 only");
+  if (g->n_kv_heads <= 0 || g->n_heads <= 0 || g->n_heads % g->n_kv_heads != 0)
+    return set_err(msg, QB_ERR_ARG, "n_heads must be a positive multiple of n_kv_heads");
+  if (g->n_heads / g->n_kv_heads > 16) return set_err(msg, QB_ERR_UNSUPPORTED, "GQA group above 16");
+  if (g->n_kv_heads > 64) return set_err(msg, QB_ERR_UNSUPPORTED, "more than 64 KV heads");
+  const int ks[3] = {g->hidden, g->n_heads * g->head_dim, g->ffn};
+  for (int k : ks)
+    if (k <= 0 || k % 256 != 0) return set_err(msg, QB_ERR_UNSUPPORTED, "hidden, Hq*D and ffn must be multiples of 256");
+  if (g->n_layers <= 0 || g->vocab <= 0) return set_err(msg, QB_ERR_ARG, "n_layers and vocab must be positive");
+  if (g->hidden > 16384 || g->ffn > 65536) return set_err(msg, QB_ERR_UNSUPPORTED, "hidden/ffn too large for one CTA's x row");
+  return QB_OK;
+}
+
+// One decode row through every layer. tok_in: device id; pos: device position
+// (read, then incremented by the last kernel). head=false skips the LM head
+// and lets the last down-projection increment the position (prefill rows).
+int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t* pos, void* logits, bool head,
+                    cudaStream_t st) {
+  const qb_config& g = c->cfg;
+  const int H = g.hidden, D = g.head_dim;
+  const int nqkv = (g.n_heads + 2 * g.n_kv_heads) * D;
+  cudaError_t e;
+  for (int l = 0; l < g.n_layers; ++l) {
+    const qb_layer_weights& w = c->layers[l];
+    // 1. RMSNorm + QKV (layer 0 gathers the embedding row into xa)
+    GemvArgs a = gemv_args(w.qkv, H, nqkv, l == 0 ? nullptr : c->xa, c->qkv, c->err);
+    a.gain = static_cast<const bf16*>(w.input_norm);
+    a.eps = g.rms_eps;
+    if (l == 0) {
+      a.embed = c->embed;
+      a.token = tok_in;
+      a.vocab = g.vocab;
+      a.x_copy = c->xa;
+    }
+    if ((e = launch_gemv<EPI_STORE>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "qkv launch");
+    // 2. attention with the norm/rope/append prologue
+    AttnArgs at;
+    std::memset(&at, 0, sizeof(at));
+    at.qkv = c->qkv;
+    at.q_norm = static_cast<const bf16*>(w.q_norm);
+    at.k_norm = static_cast<const bf16*>(w.k_norm);
+    at.cos = c->cos;
+    at.sin = c->sin;
+    at.eps = g.rms_eps;
+    at.pos = pos;
+    const size_t layer_off = (size_t)l * g.n_kv_heads * c->cap * D;
+    at.k_cache = c->kc + layer_off;
+    at.v_cache = c->vc + layer_off;
+    at.out = c->attn;
+    at.part_o = c->part_o;
+    at.part_lse = c->part_lse;
+    at.counters = c->counters;
+    at.err = c->err;
+    at.Hq = g.n_heads;
+    at.Hkv = g.n_kv_heads;
+    at.Q = 1;
+    at.cap = c->cap;
+    at.splits = c->splits;
+    if ((e = launch_attn(c->tmk[l], c->tmv[l], at, true, st)) != cudaSuccess)
+      return cuda_fail(&c->msg, e, "attention launch");
+    // 3. o-proj + residual: xb = xa + O . attn
+    a = gemv_args(w.o, g.n_heads * D, H, c->attn, c->xb, c->err);
+    a.residual = c->xa;
+    if ((e = launch_gemv<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "o launch");
+    // 4. RMSNorm + gate/up + SwiGLU
+    a = gemv_args(w.gate_up, H, 2 * g.ffn, c->xb, c->act, c->err);
+    a.gain = static_cast<const bf16*>(w.post_norm);
+    a.eps = g.rms_eps;
+    if ((e = launch_gemv<EPI_SWIGLU>(a, c->sm_count, st)) != cudaSuccess)
+      return cuda_fail(&c->msg, e, "gate/up launch");
+    // 5. down + residual: xa = xb + Down . act
+    a = gemv_args(w.down, g.ffn, H, c->act, c->xa, c->err);
+    a.residual = c->xb;
+    if (!head && l == g.n_layers - 1) a.pos_inc = pos;
+    if ((e = launch_gemv<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess)
+      return cuda_fail(&c->msg, e, "down launch");
+  }
+  if (head) {
+    GemvArgs a = gemv_args(c->lm_head, H, g.vocab, c->xa, nullptr, c->err);
+    a.gain = c->final_norm;
+    a.eps = g.rms_eps;
+    a.logits = static_cast<bf16*>(logits);
+    a.part_val = c->head_val;
+    a.part_idx = c->head_idx;
+    a.counter = c->counters + 64;
+    a.token_out = tok_out;
+    a.pos_inc = pos;
+    if ((e = launch_gemv<EPI_ARGMAX>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "head launch");
+  }
+  return QB_OK;
+}
+
+int require_ready(qb_ctx* c) {
+  if (!c) return set_err(nullptr, QB_ERR_ARG, "ctx is NULL");
+  if (!c->weights_bound) return set_err(&c->msg, QB_ERR_STATE, "weights not bound");
+  if (!c->state_bound) return set_err(&c->msg, QB_ERR_STATE, "state not bound");
+  return QB_OK;
+}
+
+}  // namespace
+
+// ====================================================================== C ABI
+extern "C" {
+
+const char* qb_version(void) { return "qb 0.1 sm_100a"; }
+
+const char* qb_last_error(const qb_ctx* ctx) {
+  if (ctx) return ctx->msg.c_str();
+  return g_last_error.c_str();
+}
+
+int qb_create(const qb_config* cfg, int device, int tp_rank, int tp_size, qb_ctx** out) {
+  if (!out) return set_err(nullptr, QB_ERR_ARG, "out is NULL");
+  *out = nullptr;
+  std::string msg;
+  int rc = validate_config(cfg, &msg);
+  if (rc) return rc;
+  if (tp_size != 1 || tp_rank != 0)
+    return set_err(nullptr, QB_ERR_UNSUPPORTED, "tensor-parallel contexts are created by qb_create_tp");
+  cudaError_t e = cudaSetDevice(device);
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaSetDevice");
+  qb_ctx* c = new qb_ctx();
+  c->cfg = *cfg;
+  c->device = device;
+  c->tp_rank = tp_rank;
+  c->tp_size = tp_size;
+  c->sm_count = sm_count_of(device);
+  c->splits = attn_splits_for(cfg->n_kv_heads, c->sm_count);
+  *out = c;
+  return QB_OK;
+}
+
+int qb_destroy(qb_ctx* c) {
+  if (!c) return QB_OK;
+  if (c->exec) cudaGraphExecDestroy(c->exec);
+  if (c->graph) cudaGraphDestroy(c->graph);
+  delete c;
+  return QB_OK;
+}
+
+int qb_bind_weights(qb_ctx* c, const qb_layer_weights* layers, int n_layers, const void* embed,
+                    const void* final_norm, const void* lm_head) {
+  if (!c) return set_err(nullptr, QB_ERR_ARG, "ctx is NULL");
+  if (!layers || n_layers != c->cfg.n_layers) return set_err(&c->msg, QB_ERR_ARG, "layer table does not match n_layers");
+  if (!ptr_ok(embed) || !ptr_ok(final_norm) || !ptr_ok(lm_head))
+    return set_err(&c->msg, QB_ERR_ARG, "embed/final_norm/lm_head must be 16-byte aligned device pointers");
+  for (int l = 0; l < n_layers; ++l) {
+    const qb_layer_weights& w = layers[l];
+    const void* ps[8] = {w.input_norm, w.qkv, w.q_norm, w.k_norm, w.o, w.post_norm, w.gate_up, w.down};
+    for (const void* p : ps)
+      if (!ptr_ok(p)) return set_err(&c->msg, QB_ERR_ARG, "layer weight pointers must be 16-byte aligned and non-NULL");
+  }
+  c->layers.assign(layers, layers + n_layers);
+  c->embed = static_cast<const bf16*>(embed);
+  c->final_norm = static_cast<const bf16*>(final_norm);
+  c->lm_head = static_cast<const bf16*>(lm_head);
+  c->weights_bound = true;
+  return QB_OK;
+}
+
+int qb_workspace_bytes(const qb_ctx* c, size_t* bytes) {
+  if (!c || !bytes) return set_err(nullptr, QB_ERR_ARG, "NULL argument");
+  *bytes = ws_layout(c).total;
+  return QB_OK;
+}
+
+int qb_bind_state(qb_ctx* c, void* k_cache, void* v_cache, int capacity, const void* rope_cos,
+                  const void* rope_sin, void* workspace, size_t workspace_bytes) {
+  if (!c) return set_err(nullptr, QB_ERR_ARG, "ctx is NULL");
+  if (capacity <= 0) return set_err(&c->msg, QB_ERR_ARG, "capacity must be positive");
+  if (!ptr_ok(k_cache) || !ptr_ok(v_cache) || !ptr_ok(rope_cos) || !ptr_ok(rope_sin) || !ptr_ok(workspace))
+    return set_err(&c->msg, QB_ERR_ARG, "state pointers must be 16-byte aligned and non-NULL");
+  const WsLayout L = ws_layout(c);
+  if (workspace_bytes < L.total) return set_err(&c->msg, QB_ERR_ARG, "workspace smaller than qb_workspace_bytes()");
+  cudaError_t e = cudaSetDevice(c->device);
+  if (e != cudaSuccess) return cuda_fail(&c->msg, e, "cudaSetDevice");
+  c->kc = static_cast<bf16*>(k_cache);
+  c->vc = static_cast<bf16*>(v_cache);
+  c->cap = capacity;
+  c->cos = static_cast<const bf16*>(rope_cos);
+  c->sin = static_cast<const bf16*>(rope_sin);
+  c->ws = static_cast<uint8_t*>(workspace);
+  c->ws_bytes = workspace_bytes;
+  c->err = reinterpret_cast<int*>(c->ws + L.err);
+  c->counters = reinterpret_cast<unsigned*>(c->ws + L.counters);
+  c->head_val = reinterpret_cast<float*>(c->ws + L.head_val);
+  c->head_idx = reinterpret_cast<int*>(c->ws + L.head_idx);
+  c->xa = reinterpret_cast<bf16*>(c->ws + L.xa);
+  c->xb = reinterpret_cast<bf16*>(c->ws + L.xb);
+  c->qkv = reinterpret_cast<bf16*>(c->ws + L.qkv);
+  c->attn = reinterpret_cast<bf16*>(c->ws + L.attn);
+  c->act = reinterpret_cast<bf16*>(c->ws + L.act);
+  c->part_lse = reinterpret_cast<float*>(c->ws + L.part_lse);
+  c->part_o = reinterpret_cast<float*>(c->ws + L.part_o);
+  if ((e = cudaMemset(workspace, 0, L.total)) != cudaSuccess) return cuda_fail(&c->msg, e, "workspace memset");
+  const qb_config& g = c->cfg;
+  c->tmk.assign(g.n_layers, CUtensorMap());
+  c->tmv.assign(g.n_layers, CUtensorMap());
+  for (int l = 0; l < g.n_layers; ++l) {
+    const size_t off = (size_t)l * g.n_kv_heads * capacity * g.head_dim;
+    if (!make_kv_map(&c->tmk[l], c->kc + off, g.n_kv_heads, capacity) ||
+        !make_kv_map(&c->tmv[l], c->vc + off, g.n_kv_heads, capacity))
+      return set_err(&c->msg, QB_ERR_CUDA, "cuTensorMapEncodeTiled failed for the KV cache");
+  }
+  if (c->exec) {
+    cudaGraphExecDestroy(c->exec);
+    c->exec = nullptr;
+  }
+  if (c->graph) {
+    cudaGraphDestroy(c->graph);
+    c->graph = nullptr;
+  }
+  c->state_bound = true;
+  return QB_OK;
+}
+
+int qb_decode_step(qb_ctx* c, int64_t* token, int64_t* position, void* logits_out, void* stream) {
+  int rc = require_ready(c);
+  if (rc) return rc;
+  if (!token || !position) return set_err(&c->msg, QB_ERR_ARG, "token/position are NULL");
+  return run_rows_decode(c, token, token, position, logits_out, true, static_cast<cudaStream_t>(stream));
+}
+
+int qb_prefill(qb_ctx* c, const int64_t* ids, int n, int64_t* token, int64_t* position, void* logits_out,
+               void* stream) {
+  int rc = require_ready(c);
+  if (rc) return rc;
+  if (!ids || !token || !position || n <= 0) return set_err(&c->msg, QB_ERR_ARG, "bad prefill arguments");
+  if (n > c->cap) return set_err(&c->msg, QB_ERR_CAPACITY, "prompt longer than the KV capacity");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(position, 0, sizeof(int64_t), st);
+  if (e != cudaSuccess) return cuda_fail(&c->msg, e, "position reset");
+  for (int i = 0; i < n; ++i) {
+    const bool last = (i == n - 1);
+    rc = run_rows_decode(c, ids + i, token, position, last ? logits_out : nullptr, last, st);
+    if (rc) return rc;
+  }
+  return QB_OK;
+}
+
+int qb_capture_decode(qb_ctx* c, int64_t* token, int64_t* position, void* logits_out, void* stream) {
+  int rc = require_ready(c);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (c->exec) {
+    cudaGraphExecDestroy(c->exec);
+    c->exec = nullptr;
+  }
+  if (c->graph) {
+    cudaGraphDestroy(c->graph);
+    c->graph = nullptr;
+  }
+  cudaError_t e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+  if (e != cudaSuccess) return cuda_fail(&c->msg, e, "begin capture");
+  rc = run_rows_decode(c, token, token, position, logits_out, true, st);
+  cudaGraph_t graph = nullptr;
+  e = cudaStreamEndCapture(st, &graph);
+  if (rc) {
+    if (graph) cudaGraphDestroy(graph);
+    return rc;
+  }
+  if (e != cudaSuccess) return cuda_fail(&c->msg, e, "end capture");
+  e = cudaGraphInstantiate(&c->exec, graph, 0);
+  if (e != cudaSuccess) {
+    cudaGraphDestroy(graph);
+    return cuda_fail(&c->msg, e, "graph instantiate");
+  }
+  c->graph = graph;
+  return QB_OK;
+}
+
+int qb_replay_decode(qb_ctx* c, void* stream) {
+  if (!c) return set_err(nullptr, QB_ERR_ARG, "ctx is NULL");
+  if (!c->exec) return set_err(&c->msg, QB_ERR_STATE, "no captured decode graph");
+  cudaError_t e = cudaGraphLaunch(c->exec, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(&c->msg, e, "graph launch");
+  return QB_OK;
+}
+
+static int read_device_error(int* err_word, cudaStream_t st, std::string* msg) {
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(msg, e, "stream synchronize");
+  int v = 0;
+  e = cudaMemcpy(&v, err_word, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(msg, e, "error word read");
+  if (v == 0) return QB_OK;
+  cudaMemset(err_word, 0, sizeof(int));
+  char buf[128];
+  if (v == DEV_BAD_TOKEN) return set_err(msg, QB_ERR_ARG, "token id outside the vocabulary");
+  if (v == DEV_BAD_POSITION) return set_err(msg, QB_ERR_CAPACITY, "position outside the KV capacity");
+  std::snprintf(buf, sizeof(buf), "device wait timed out (site 0x%x); kernel returned early", v);
+  return set_err(msg, QB_ERR_TIMEOUT, buf);
+}
+
+int qb_check(qb_ctx* c, void* stream) {
+  int rc = require_ready(c);
+  if (rc) return rc;
+  return read_device_error(c->err, static_cast<cudaStream_t>(stream), &c->msg);
+}
+
+// --------------------------------------------------------------- op level
+size_t qb_op_scratch_bytes(void) { return kOpScratchBytes; }
+
+int qb_op_check(void* scratch, void* stream) {
+  if (!ptr_ok(scratch)) return set_err(nullptr, QB_ERR_ARG, "scratch is NULL or misaligned");
+  return read_device_error(reinterpret_cast<int*>(static_cast<uint8_t*>(scratch) + kScrErr),
+                           static_cast<cudaStream_t>(stream), nullptr);
+}
+
+int qb_norm_projection(const void* x, const void* gain, const void* w, void* out, int K, int rows, float eps,
+                       int swiglu, void* stream) {
+  if (!ptr_ok(x) || !ptr_ok(w) || !ptr_ok(out) || (gain && !ptr_ok(gain)))
+    return set_err(nullptr, QB_ERR_ARG, "x, w, out (and gain) must be 16-byte aligned device pointers");
+  if (K <= 0 || K % 256 != 0) return set_err(nullptr, QB_ERR_UNSUPPORTED, "K must be a positive multiple of 256");
+  if (rows <= 0 || (swiglu && rows % 2 != 0)) return set_err(nullptr, QB_ERR_ARG, "packed gate/up width must be even");
+  GemvArgs a = gemv_args(w, K, rows, x, out, nullptr);
+  a.gain = static_cast<const bf16*>(gain);
+  a.eps = eps;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int sms = current_sm_count();
+  cudaError_t e = swiglu ? launch_gemv<EPI_SWIGLU>(a, sms, st) : launch_gemv<EPI_STORE>(a, sms, st);
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, "norm_projection launch");
+  return QB_OK;
+}
+
+int qb_projection_residual(const void* x, const void* w, const void* residual, void* out, int K, int N,
+                           void* stream) {
+  if (!ptr_ok(x) || !ptr_ok(w) || !ptr_ok(out) || !residual)
+    return set_err(nullptr, QB_ERR_ARG, "x, w, residual, out must be device pointers (16-byte aligned)");
+  if (K <= 0 || K % 256 != 0) return set_err(nullptr, QB_ERR_UNSUPPORTED, "K must be a positive multiple of 256");
+  if (N <= 0) return set_err(nullptr, QB_ERR_ARG, "N must be positive");
+  GemvArgs a = gemv_args(w, K, N, x, out, nullptr);
+  a.residual = static_cast<const bf16*>(residual);
+  cudaError_t e = launch_gemv<EPI_RESIDUAL>(a, current_sm_count(), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, "projection_residual launch");
+  return QB_OK;
+}
+
+int qb_norm_greedy_head(const void* x, const void* gain, const void* w, int K, int V, float eps, void* logits_out,
+                        int64_t* token_out, void* scratch, size_t scratch_bytes, void* stream) {
+  if (!ptr_ok(x) || !ptr_ok(w) || !token_out || (gain && !ptr_ok(gain)) || !ptr_ok(scratch))
+    return set_err(nullptr, QB_ERR_ARG, "x, w, gain, scratch must be 16-byte aligned device pointers");
+  if (scratch_bytes < kOpScratchBytes) return set_err(nullptr, QB_ERR_ARG, "scratch smaller than qb_op_scratch_bytes()");
+  if (K <= 0 || K % 256 != 0) return set_err(nullptr, QB_ERR_UNSUPPORTED, "K must be a positive multiple of 256");
+  if (V <= 0) return set_err(nullptr, QB_ERR_ARG, "V must be positive");
+  uint8_t* s = static_cast<uint8_t*>(scratch);
+  GemvArgs a = gemv_args(w, K, V, x, nullptr, reinterpret_cast<int*>(s + kScrErr));
+  a.gain = static_cast<const bf16*>(gain);
+  a.eps = eps;
+  a.logits = static_cast<bf16*>(logits_out);
+  a.part_val = reinterpret_cast<float*>(s + kScrHeadVal);
+  a.part_idx = reinterpret_cast<int*>(s + kScrHeadIdx);
+  a.counter = reinterpret_cast<unsigned*>(s + kScrCounters) + 128;
+  a.token_out = token_out;
+  cudaError_t e = launch_gemv<EPI_ARGMAX>(a, current_sm_count(), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, "greedy head launch");
+  return QB_OK;
+}
+
+static int op_attention(const void* qkv, const void* q, const void* q_norm, const void* k_norm, const void* cos,
+                        const void* sin, float eps, void* k_cache, void* v_cache, int hq, int hkv, int cap,
+                        int queries, const int64_t* positions, void* out, void* scratch, size_t scratch_bytes,
+                        bool pro, void* stream) {
+  if (!ptr_ok(k_cache) || !ptr_ok(v_cache) || !ptr_ok(out) || !positions || !ptr_ok(scratch))
+    return set_err(nullptr, QB_ERR_ARG, "caches, out, positions, scratch must be aligned device pointers");
+  if (scratch_bytes < kOpScratchBytes) return set_err(nullptr, QB_ERR_ARG, "scratch smaller than qb_op_scratch_bytes()");
+  if (hkv <= 0 || hq <= 0 || hq % hkv != 0) return set_err(nullptr, QB_ERR_ARG, "n_heads must be a multiple of n_kv_heads");
+  if (hkv > 64) return set_err(nullptr, QB_ERR_UNSUPPORTED, "more than 64 KV heads");
+  if (cap <= 0) return set_err(nullptr, QB_ERR_ARG, "capacity must be positive");
+  if (queries < 1 || queries > 8) return set_err(nullptr, QB_ERR_UNSUPPORTED, "queries must be 1..8");
+  const int rows = (hq / hkv) * queries;
+  if (rows > 32 || (pro && rows > 16)) return set_err(nullptr, QB_ERR_UNSUPPORTED, "group x queries above 32 rows");
+  const int sms = current_sm_count();
+  int splits = attn_splits_for(hkv, sms);
+  if (hkv * splits > kMaxAttnCtas) splits = kMaxAttnCtas / hkv > 0 ? kMaxAttnCtas / hkv : 1;
+  if ((size_t)hkv * splits * 32 * 4 > 65536) return set_err(nullptr, QB_ERR_UNSUPPORTED, "too many KV heads for the op scratch");
+  CUtensorMap tk, tv;
+  if (!make_kv_map(&tk, k_cache, hkv, cap) || !make_kv_map(&tv, v_cache, hkv, cap))
+    return set_err(nullptr, QB_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+  uint8_t* s = static_cast<uint8_t*>(scratch);
+  AttnArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.qkv = static_cast<const bf16*>(qkv);
+  a.q = static_cast<const bf16*>(q);
+  a.q_norm = static_cast<const bf16*>(q_norm);
+  a.k_norm = static_cast<const bf16*>(k_norm);
+  a.cos = static_cast<const bf16*>(cos);
+  a.sin = static_cast<const bf16*>(sin);
+  a.eps = eps;
+  a.pos = positions;
+  a.k_cache = static_cast<bf16*>(k_cache);
+  a.v_cache = static_cast<bf16*>(v_cache);
+  a.out = static_cast<bf16*>(out);
+  a.part_lse = reinterpret_cast<float*>(s + kScrAttnLse);
+  a.part_o = reinterpret_cast<float*>(s + kScrAttnO);
+  a.counters = reinterpret_cast<unsigned*>(s + kScrCounters);
+  a.err = reinterpret_cast<int*>(s + kScrErr);
+  a.Hq = hq;
+  a.Hkv = hkv;
+  a.Q = queries;
+  a.cap = cap;
+  a.splits = splits;
+  cudaError_t e = launch_attn(tk, tv, a, pro, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, "attention launch");
+  return QB_OK;
+}
+
+int qb_grouped_attention(const void* q, const void* k_cache, const void* v_cache, int n_heads, int n_kv_heads,
+                         int capacity, int queries, const int64_t* positions, void* out, void* scratch,
+                         size_t scratch_bytes, void* stream) {
+  if (!ptr_ok(q)) return set_err(nullptr, QB_ERR_ARG, "q must be an aligned device pointer");
+  return op_attention(nullptr, q, nullptr, nullptr, nullptr, nullptr, 0.f, const_cast<void*>(k_cache),
+                      const_cast<void*>(v_cache), n_heads, n_kv_heads, capacity, queries, positions, out, scratch,
+                      scratch_bytes, false, stream);
+}
+
+int qb_rope_attention(const void* qkv, const void* q_norm, const void* k_norm, const void* rope_cos,
+                      const void* rope_sin, float eps, void* k_cache, void* v_cache, int n_heads, int n_kv_heads,
+                      int capacity, const int64_t* position, void* out, void* scratch, size_t scratch_bytes,
+                      void* stream) {
+  if (!ptr_ok(qkv) || !ptr_ok(q_norm) || !ptr_ok(k_norm) || !ptr_ok(rope_cos) || !ptr_ok(rope_sin))
+    return set_err(nullptr, QB_ERR_ARG, "qkv, norms and rope tables must be aligned device pointers");
+  return op_attention(qkv, nullptr, q_norm, k_norm, rope_cos, rope_sin, eps, k_cache, v_cache, n_heads, n_kv_heads,
+                      capacity, 1, position, out, scratch, scratch_bytes, true, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,200 @@
+"""Drop-in ``Engine`` for the dryft batch-one Qwen3 decode path, on sm_100a kernels.
+
+Public API (``dryft/QWEN_ENGINE_CONTRACT.md:25-36``, ``dryft/engine/engine.py:175-249``):
+
+    engine = Engine(model_path)                       # HF checkpoint directory
+    for step in engine.generate(input_ids, max_new_tokens):
+        ...                                           # step == [token_id]
+
+``generate`` yields a one-element list exactly ``max_new_tokens`` times and
+never stops at an end-of-sequence token. The internal entry points the north
+star names map as follows: load = ``Engine.__init__``; prefill =
+``DecodeState.prefill``; decode_step = ``DecodeState.step`` (a replay of the
+captured graph); generate = ``Engine.generate``.
+
+PyTorch owns device memory and streams; every kernel is in ``libqb.so``.
+"""
+from __future__ import annotations
+
+from typing import Dict, Iterator, List, Optional
+
+import torch
+
+from . import _lib
+from .config import ModelConfig
+from .weights import PackedWeights, load_checkpoint, random_state_dict, rotary_table
+
+BF16 = torch.bfloat16
+
+
+def stream_decode(state, first_tokens: List[int], output_length: int) -> Iterator[List[int]]:
+    """Overlap the next graph replay with delivery of an already-read token
+    (``dryft/engine/decode.py:8-22``): the final yield has no outstanding replay
+    and ``output_length == 1`` launches none."""
+    tokens = first_tokens
+    for step in range(output_length):
+        has_next = step + 1 < output_length
+        if has_next:
+            state.step()
+        yield tokens
+        if has_next:
+            tokens = state.read_token()
+
+
+class DecodeState:
+    """Fixed-capacity KV cache, RoPE table, device token/position and the
+    captured decode graph (``dryft/engine/decode.py:102-206``).
+
+    Capacity = prompt_length + output_length - 1 + draft slots. The caches are
+    zero-filled (finite), laid out ``[L, Hkv, capacity, D]``.
+    """
+
+    def __init__(self, engine: "Engine", prompt_length: int, output_length: int,
+                 draft_tokens: int = 0, keep_logits: bool = False, capacity: Optional[int] = None):
+        cfg = engine.cfg
+        dev = engine.device
+        self.engine = engine
+        self.shape = (1, prompt_length, output_length)
+        self.capacity = capacity or (prompt_length + max(output_length, 1) - 1 + draft_tokens)
+        shape = (cfg.n_layers, cfg.n_kv_heads, self.capacity, cfg.head_dim)
+        self.keys = torch.zeros(shape, dtype=BF16, device=dev)
+        self.values = torch.zeros(shape, dtype=BF16, device=dev)
+        cos, sin = rotary_table(cfg, self.capacity)
+        self.cos, self.sin = cos.to(dev), sin.to(dev)
+        L = _lib.load()
+        nbytes = _lib.c_size_t()
+        _lib.check(L.qb_workspace_bytes(engine.ctx, _lib.ctypes.byref(nbytes)), engine.ctx)
+        self.workspace = torch.empty(nbytes.value, dtype=torch.uint8, device=dev)
+        self.token = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.position = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.prompt = torch.zeros(max(prompt_length, 1), dtype=torch.int64, device=dev)
+        self.logits = torch.zeros(cfg.vocab, dtype=BF16, device=dev) if keep_logits else None
+        _lib.check(L.qb_bind_state(engine.ctx, self.keys.data_ptr(), self.values.data_ptr(), self.capacity,
+                                   self.cos.data_ptr(), self.sin.data_ptr(), self.workspace.data_ptr(),
+                                   self.workspace.numel()), engine.ctx)
+        engine._bound_state = self
+        self.captured = False
+
+    # -- the four entry points --------------------------------------------------
+    def prefill(self, ids: torch.Tensor) -> torch.Tensor:
+        """Write K/V for the prompt, emit the first token into ``self.token``
+        and set ``position = len(prompt)``."""
+        n = ids.numel()
+        if n > self.capacity:
+            raise ValueError("prompt longer than the KV capacity")
+        if n > self.prompt.numel():
+            self.prompt = torch.zeros(n, dtype=torch.int64, device=self.token.device)
+        self.prompt[:n].copy_(ids.reshape(-1), non_blocking=True)
+        self._ensure_bound()
+        _lib.check(_lib.load().qb_prefill(self.engine.ctx, self.prompt.data_ptr(), n, self.token.data_ptr(),
+                                          self.position.data_ptr(), _lib.ptr(self.logits), _lib.stream_handle()),
+                   self.engine.ctx)
+        return self.token
+
+    def capture(self) -> None:
+        """Capture one decode step as a CUDA graph on a side stream."""
+        self._ensure_bound()
+        side = torch.cuda.Stream(device=self.token.device)
+        side.wait_stream(torch.cuda.current_stream())
+        _lib.check(_lib.load().qb_capture_decode(self.engine.ctx, self.token.data_ptr(), self.position.data_ptr(),
+                                                 _lib.ptr(self.logits), side.cuda_stream), self.engine.ctx)
+        torch.cuda.current_stream().wait_stream(side)
+        self.captured = True
+
+    def step(self) -> None:
+        """One decode step: token <- greedy(next), position += 1."""
+        self._ensure_bound()
+        if not self.captured:
+            self.capture()
+        _lib.check(_lib.load().qb_replay_decode(self.engine.ctx, _lib.stream_handle()), self.engine.ctx)
+
+    def step_eager(self) -> None:
+        self._ensure_bound()
+        _lib.check(_lib.load().qb_decode_step(self.engine.ctx, self.token.data_ptr(), self.position.data_ptr(),
+                                              _lib.ptr(self.logits), _lib.stream_handle()), self.engine.ctx)
+
+    def read_token(self) -> List[int]:
+        return self.token.tolist()
+
+    def check(self) -> None:
+        """Synchronise and raise on a device-side error (bounded wait gave up,
+        token or position out of range)."""
+        _lib.check(_lib.load().qb_check(self.engine.ctx, _lib.stream_handle()), self.engine.ctx)
+
+    def _ensure_bound(self):
+        if self.engine._bound_state is not self:
+            raise RuntimeError("this DecodeState is no longer bound to its engine")
+
+
+class Engine:
+    """``Engine(model_path)``: load an HF Qwen3 checkpoint to ``cuda:0`` in the
+    engine layout; ``generate`` streams greedy tokens."""
+
+    def __init__(self, model_path: Optional[str] = None, device: str = "cuda:0", *,
+                 cfg: Optional[ModelConfig] = None, state: Optional[Dict[str, torch.Tensor]] = None):
+        if not torch.cuda.is_available():
+            raise RuntimeError("Engine needs a CUDA device; there is no CPU fallback")
+        self.device = torch.device(device)
+        torch.cuda.set_device(self.device)
+        if model_path is not None:
+            cfg, state = load_checkpoint(model_path, device="cpu")
+        if cfg is None or state is None:
+            raise ValueError("Engine needs a model_path or (cfg, state)")
+        self.cfg = cfg
+        self.weights = PackedWeights(cfg, state, self.device)
+        L = _lib.load()
+        qc = _lib.QbConfig(cfg.hidden, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn, cfg.n_layers,
+                           cfg.vocab, cfg.rms_eps)
+        ctx = _lib.c_void_p()
+        _lib.check(L.qb_create(_lib.ctypes.byref(qc), self.device.index or 0, 0, 1, _lib.ctypes.byref(ctx)))
+        self.ctx = ctx
+        table = (_lib.QbLayerWeights * cfg.n_layers)()
+        for i, lw in enumerate(self.weights.layers):
+            table[i] = _lib.QbLayerWeights(lw["input_norm"].data_ptr(), lw["qkv"].data_ptr(),
+                                           lw["q_norm"].data_ptr(), lw["k_norm"].data_ptr(), lw["o"].data_ptr(),
+                                           lw["post_norm"].data_ptr(), lw["gu"].data_ptr(), lw["down"].data_ptr())
+        w = self.weights
+        _lib.check(L.qb_bind_weights(ctx, table, cfg.n_layers, w.embed.data_ptr(), w.final_norm.data_ptr(),
+                                     w.lm_head.data_ptr()), ctx)
+        self.state: Optional[DecodeState] = None
+        self._bound_state = None
+
+    @classmethod
+    def from_random(cls, cfg: ModelConfig, seed: int = 0, device: str = "cuda:0", init_device: str = "cpu"):
+        """Seeded random-init weights (see ``weights.random_state_dict``)."""
+        state = random_state_dict(cfg, seed, device=init_device)
+        return cls(None, device, cfg=cfg, state=state)
+
+    def __del__(self):
+        ctx = getattr(self, "ctx", None)
+        if ctx is not None and ctx.value:
+            try:
+                _lib.load().qb_destroy(ctx)
+            except Exception:
+                pass
+            self.ctx = None
+
+    def new_state(self, prompt_length: int, output_length: int, **kw) -> DecodeState:
+        self.state = None
+        self.state = DecodeState(self, prompt_length, output_length, **kw)
+        return self.state
+
+    def generate(self, input_ids: List[List[int]], max_new_tokens: int):
+        """Greedy continuation, one step at a time; yields ``[token]`` exactly
+        ``max_new_tokens`` times (``dryft/engine/engine.py:202-249``)."""
+        if max_new_tokens <= 0:
+            return
+        if len(input_ids) != 1:
+            raise ValueError("this engine implements the batch-one decode path")
+        prompt = list(input_ids[0])
+        if not prompt:
+            raise ValueError("the prompt must hold at least one token")
+        with torch.inference_mode():
+            shape = (1, len(prompt), max_new_tokens)
+            if self.state is None or self.state.shape != shape or self._bound_state is not self.state:
+                self.new_state(len(prompt), max_new_tokens)
+            state = self.state
+            ids = torch.tensor(prompt, dtype=torch.int64).pin_memory()
+            state.prefill(ids.to(self.device, non_blocking=True))
+            first = state.read_token()
+            yield from stream_decode(state, first, max_new_tokens)

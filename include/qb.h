@@ -1,0 +1,179 @@
+/*
+ * qb.h — C ABI of the B200 (sm_100a) Qwen3 batch-one decode engine.
+ *
+ * Plain pointers and sizes only. All tensors are device memory owned by the
+ * caller (PyTorch in this repository), bf16 unless stated, row-major and
+ * contiguous. Every function returns a status code (QB_OK == 0); the message
+ * of the last failure is available from qb_last_error(). Nothing throws across
+ * this boundary. Kernels are launched on the caller's stream and never
+ * synchronise it, except qb_check().
+ *
+ * Each entry point names the reference interface it replaces
+ * (rickytang666/hackthenorth, paths relative to the project root).
+ */
+#ifndef QB_H_
+#define QB_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes -------------------------------------------------------- */
+#define QB_OK 0
+#define QB_ERR_ARG 1         /* shape/pointer/layout contract violated (reference: ValueError) */
+#define QB_ERR_CAPACITY 2    /* position + rows beyond the KV capacity */
+#define QB_ERR_CUDA 3        /* a CUDA runtime or driver call failed */
+#define QB_ERR_TIMEOUT 4     /* a bounded device wait gave up; the kernel returned early */
+#define QB_ERR_STATE 5       /* weights/state not bound, or graph not captured */
+#define QB_ERR_UNSUPPORTED 6 /* shape outside what the kernels implement */
+
+/* ---- model description --------------------------------------------------- */
+typedef struct qb_config {
+  int hidden;      /* H */
+  int n_heads;     /* Hq (query heads) */
+  int n_kv_heads;  /* Hkv */
+  int head_dim;    /* D; the kernels implement D == 128 */
+  int ffn;         /* F */
+  int n_layers;    /* L */
+  int vocab;       /* V */
+  float rms_eps;   /* RMSNorm epsilon (hidden, q and k norms) */
+} qb_config;
+
+/* Per-layer device weights in the engine layout (bf16):
+ *   input_norm [H]; qkv [Hq*D + 2*Hkv*D, H] (q rows, k rows, v rows);
+ *   q_norm, k_norm [D]; o [H, Hq*D]; post_norm [H];
+ *   gate_up [2F, H] with gate row j at 2j and up row j at 2j+1; down [H, F]. */
+typedef struct qb_layer_weights {
+  const void* input_norm;
+  const void* qkv;
+  const void* q_norm;
+  const void* k_norm;
+  const void* o;
+  const void* post_norm;
+  const void* gate_up;
+  const void* down;
+} qb_layer_weights;
+
+typedef struct qb_ctx qb_ctx;
+
+const char* qb_version(void);
+
+/* Message of the last failure on `ctx`, or of the last context-free call on
+ * this thread when ctx is NULL. Never returns NULL. */
+const char* qb_last_error(const qb_ctx* ctx);
+
+/* ---- engine lifecycle ---------------------------------------------------- */
+
+/* Replaces Engine.__init__'s model preparation (dryft/engine/engine.py:176-200).
+ * tp_rank/tp_size: tensor-parallel slot; 0/1 for a single GPU. */
+int qb_create(const qb_config* cfg, int device, int tp_rank, int tp_size, qb_ctx** out);
+int qb_destroy(qb_ctx* ctx);
+
+/* Borrow device weights (no copy). lm_head may equal embed (tied).
+ * Replaces the module surgery of dryft/engine/engine.py:190-199. */
+int qb_bind_weights(qb_ctx* ctx, const qb_layer_weights* layers, int n_layers,
+                    const void* embed, const void* final_norm, const void* lm_head);
+
+/* Bytes of workspace qb_bind_state needs (activations, split-KV partials,
+ * counters, error word). */
+int qb_workspace_bytes(const qb_ctx* ctx, size_t* bytes);
+
+/* Borrow the decode state: K and V caches [L, Hkv, capacity, D] (bf16,
+ * zero-filled by the caller, as KVCache does: dryft/engine/decode.py:25-46),
+ * the RoPE tables [capacity, D] (bf16 cos and sin rows for positions
+ * 0..capacity-1: dryft/engine/decode.py:49-67), and the workspace. The
+ * workspace is zeroed here (synchronously). */
+int qb_bind_state(qb_ctx* ctx, void* k_cache, void* v_cache, int capacity,
+                  const void* rope_cos, const void* rope_sin,
+                  void* workspace, size_t workspace_bytes);
+
+/* One batch-one decode step: DecodeState.step (dryft/engine/decode.py:126-138).
+ * Reads *token (int64, device) at *position (int64, device), appends its K/V,
+ * writes the greedy next token to *token and increments *position.
+ * logits_out (device bf16 [V]) may be NULL. Graph-capturable: no host sync,
+ * no allocation. Fails with QB_ERR_CAPACITY only when detectable on the host. */
+int qb_decode_step(qb_ctx* ctx, int64_t* token, int64_t* position, void* logits_out,
+                   void* stream);
+
+/* Prefill: DecodeState.prefill / prefill.prefill (dryft/engine/decode.py:157-166,
+ * dryft/engine/prefill.py:6-26). ids: device int64 [n]. Writes K/V for
+ * positions 0..n-1, the first generated token to *token and sets
+ * *position = n. Each prompt row runs through the decode kernels. */
+int qb_prefill(qb_ctx* ctx, const int64_t* ids, int n, int64_t* token, int64_t* position,
+               void* logits_out, void* stream);
+
+/* Capture qb_decode_step(token, position, logits_out) into a CUDA graph owned
+ * by ctx (dryft/engine/decode.py:140-155), and replay it. */
+int qb_capture_decode(qb_ctx* ctx, int64_t* token, int64_t* position, void* logits_out,
+                      void* stream);
+int qb_replay_decode(qb_ctx* ctx, void* stream);
+
+/* Synchronise `stream` and report device-side errors (bounded waits that gave
+ * up, out-of-range token ids). Clears the device error word. */
+int qb_check(qb_ctx* ctx, void* stream);
+
+/* ---- op-level entry points (the reference's kernel wrappers) ------------- */
+
+/* RMSNorm(x; gain, eps) fused with y = W . x, fp32 accumulation, one bf16
+ * rounding. gain == NULL skips the norm. swiglu != 0: W is [2N, K] with gate
+ * and up rows interleaved and y[j] = bf16(bf16(silu(gate_j)) * up_j).
+ * Replaces norm_projection (dryft/engine/kernels/projection.py:36-53).
+ * x [K], W [rows, K], out [N]; K a multiple of 256. */
+int qb_norm_projection(const void* x, const void* gain, const void* w, void* out,
+                       int K, int rows, float eps, int swiglu, void* stream);
+
+/* out = bf16(bf16(W . x) + residual). Replaces output_projection_residual
+ * (dryft/engine/kernels/projection.py:70-83) and down_residual
+ * (dryft/engine/kernels/down.py:288-296). x [K], W [N, K], residual/out [N]. */
+int qb_projection_residual(const void* x, const void* w, const void* residual, void* out,
+                           int K, int N, void* stream);
+
+/* Scratch bytes the op-level head and attention calls need (a multiple of
+ * 256). The scratch must be zero-filled before its first use; the kernels
+ * leave their counters at zero again. */
+size_t qb_op_scratch_bytes(void);
+
+/* Final RMSNorm + LM-head GEMV + greedy argmax with the lowest index on exact
+ * ties, logits rounded to bf16 before the comparison. Replaces the final norm
+ * (dryft/engine/decode.py:95) and greedy_token (dryft/engine/kernels/greedy.py:45-60).
+ * x [K], gain [K] or NULL, W [V, K]; logits_out bf16 [V] or NULL;
+ * token_out device int64. */
+int qb_norm_greedy_head(const void* x, const void* gain, const void* w, int K, int V,
+                        float eps, void* logits_out, int64_t* token_out,
+                        void* scratch, size_t scratch_bytes, void* stream);
+
+/* Split-KV grouped-query attention over a fixed-capacity cache for `queries`
+ * rows at absolute device positions (int64 [queries], ascending, consecutive
+ * for queries > 1); query row j sees cache slot c iff c <= positions[j]; slots
+ * past the last position are never read. q [queries, Hq, D] (already
+ * normalised and rotated), k_cache/v_cache [Hkv, capacity, D],
+ * out [queries, Hq, D]. Replaces grouped_attention
+ * (dryft/engine/kernels/attention.py:213-237). queries in 1..8. */
+int qb_grouped_attention(const void* q, const void* k_cache, const void* v_cache,
+                         int n_heads, int n_kv_heads, int capacity, int queries,
+                         const int64_t* positions, void* out,
+                         void* scratch, size_t scratch_bytes, void* stream);
+
+/* Decode attention with its prologue fused: per-head q/k RMSNorm + RoPE from
+ * the packed QKV row, K/V appended at *position, then attention of the one
+ * query row over slots 0..*position. Replaces norm_rope_cache +
+ * grouped_attention on the batch-one path (dryft/engine/fused_layer.py:123-130,
+ * dryft/engine/kernels/fused.py:153-165) and prologue_attention
+ * (dryft/engine/kernels/attention.py:162-196). qkv [Hq*D + 2*Hkv*D];
+ * q_norm/k_norm [D]; rope_cos/rope_sin [capacity, D]; out [Hq, D]. */
+int qb_rope_attention(const void* qkv, const void* q_norm, const void* k_norm,
+                      const void* rope_cos, const void* rope_sin, float eps,
+                      void* k_cache, void* v_cache, int n_heads, int n_kv_heads,
+                      int capacity, const int64_t* position, void* out,
+                      void* scratch, size_t scratch_bytes, void* stream);
+
+/* Read the device error word of an op-level scratch (synchronises stream). */
+int qb_op_check(void* scratch, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QB_H_ */

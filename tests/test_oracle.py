@@ -1,0 +1,236 @@
+"""CPU oracle vs the reference's eager path (golden vectors) and known answers.
+
+The oracle is test infrastructure: these tests pin it before it is trusted to
+check the CUDA kernels. Tolerances:
+* tokens: identical;
+* logits: max abs diff <= LOGIT_ATOL, cosine >= 0.999. LOGIT_ATOL = 0.0625
+  (four bf16 ulps at |logit| in [2, 4)) is set from the measured noise floor of
+  the reference itself on this config: native cached decode vs native
+  full-prefix logits differ by up to 0.039 (recorded in the golden file), and
+  reordering fp32 accumulation alone moves them by ~0.04.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+
+LOGIT_ATOL = 0.0625
+ATTN_RTOL = 1e-2
+
+
+def _golden_json():
+    with open(os.path.join(GOLDEN, "qwen3_0p6b_greedy.json")) as f:
+        return json.load(f)
+
+
+def _bits_to_bf16(a):
+    return torch.from_numpy(a.astype(np.int16)).view(torch.bfloat16)
+
+
+def test_golden_noise_floor_is_below_tolerance():
+    g = _golden_json()
+    assert max(g["self_noise_cached_vs_full_prefix"]) < LOGIT_ATOL
+
+
+def test_rotary_table_matches_native_bit_exact(cpu_threads):
+    # dryft/tests/test_decode.py:55-68
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3RotaryEmbedding
+    from transformers import Qwen3Config
+    from hackthenorth_b200.config import QWEN3_0P6B, QWEN3_4B
+    from hackthenorth_b200.weights import rotary_table
+
+    for cfg in (QWEN3_0P6B, QWEN3_4B):
+        hf = cfg.to_hf()
+        for k in ("architectures", "model_type", "torch_dtype"):
+            hf.pop(k)
+        rot = Qwen3RotaryEmbedding(Qwen3Config(**hf))
+        cos, sin = rotary_table(cfg, 4500)
+        x = torch.zeros(1, 1, 8, dtype=torch.bfloat16)
+        for positions in (torch.arange(7), torch.tensor([7]), torch.tensor([4095, 4096, 4097]),
+                          torch.tensor([4499]), torch.tensor([2, 3])):
+            ec, es = rot(x, positions[None])
+            assert torch.equal(cos[positions], ec[0])
+            assert torch.equal(sin[positions], es[0])
+
+
+def test_norm_rope_matches_native_apply_rotary(cpu_threads):
+    # dryft/tests/test_fused_kernels.py:407-436 (exact here: same bf16 ops)
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3RMSNorm, apply_rotary_pos_emb
+    from oracle.qwen3_oracle import norm_rope
+
+    torch.manual_seed(0)
+    qn, kn = Qwen3RMSNorm(128).bfloat16(), Qwen3RMSNorm(128).bfloat16()
+    with torch.no_grad():
+        qn.weight.normal_()
+        kn.weight.normal_()
+        q = torch.randn(2, 4, 32, 128).bfloat16()
+        k = torch.randn(2, 4, 8, 128).bfloat16()
+        ang = torch.randn(1, 4, 128)
+        cos, sin = ang.cos().bfloat16(), ang.sin().bfloat16()
+        eq, ek = apply_rotary_pos_emb(qn(q).transpose(1, 2), kn(k).transpose(1, 2), cos, sin)
+        aq = norm_rope(q, qn.weight, 1e-6, cos[:, :, None], sin[:, :, None])
+        ak = norm_rope(k, kn.weight, 1e-6, cos[:, :, None], sin[:, :, None])
+    assert torch.equal(aq.transpose(1, 2), eq)
+    assert torch.equal(ak.transpose(1, 2), ek)
+
+
+def test_attention_matches_golden_sdpa_and_ignores_nan_tail(cpu_threads):
+    # dryft/tests/test_fused_kernels.py:385-405
+    from tests.golden.make_golden import attention_inputs
+    from oracle.qwen3_oracle import grouped_attention
+
+    gold = np.load(os.path.join(GOLDEN, "attention_sdpa.npz"))
+    for queries in (1, 5):
+        q, k, v, pos = attention_inputs(512, queries)
+        ref = torch.from_numpy(gold[f"q{queries}"])
+        out = grouped_attention(q, k, v, pos).float()
+        rel = (out - ref).abs().max() / ref.abs().max()
+        assert rel <= ATTN_RTOL, rel
+        # capacity past the last position must never be read
+        k2 = torch.cat((k, torch.full((8, 64, 128), float("nan"), dtype=torch.bfloat16)), 1)
+        v2 = torch.cat((v, torch.full((8, 64, 128), float("nan"), dtype=torch.bfloat16)), 1)
+        out2 = grouped_attention(q, k2, v2, pos, split_size=None)
+        assert torch.isfinite(out2.float()).all()
+        assert (out2.float() - ref).abs().max() / ref.abs().max() <= ATTN_RTOL
+
+
+def test_halfway_projection_rounds_before_residual():
+    # dryft/tests/test_fused_kernels.py:179-187: exactly 0, not 1/256
+    from oracle.qwen3_oracle import linear
+
+    x = torch.ones(1, 33, dtype=torch.bfloat16)
+    w = torch.zeros(3, 33, dtype=torch.bfloat16)
+    w[:, 0] = 1
+    w[:, 1] = 1 / 256
+    res = -torch.ones(1, 3, dtype=torch.bfloat16)
+    assert bool((linear(x, w) + res == 0).all())
+
+
+def test_greedy_lowest_index_on_ties():
+    # dryft/tests/test_fused_kernels.py:169-173
+    from oracle.qwen3_oracle import greedy_token
+
+    w = torch.zeros(1000, 64, dtype=torch.bfloat16)
+    w[3] = 1
+    w[-1] = 1
+    _, tok = greedy_token(torch.ones(1, 64, dtype=torch.bfloat16), w)
+    assert int(tok[0]) == 3
+
+
+def test_small_oracle_matches_golden_full_logits(cpu_threads):
+    from hackthenorth_b200.config import QWEN3_SMALL
+    from hackthenorth_b200.weights import random_state_dict
+    from oracle.qwen3_oracle import OracleQwen3
+
+    g = np.load(os.path.join(GOLDEN, "qwen3_small_greedy.npz"))
+    state = random_state_dict(QWEN3_SMALL, 0)
+    o = OracleQwen3(QWEN3_SMALL, state, 64)
+    logits = []
+    toks = o.greedy(g["prompt"].tolist(), len(g["tokens"]), logits)
+    assert toks == g["tokens"].tolist()
+    ref = _bits_to_bf16(g["logits_bf16"]).float()
+    got = torch.stack(logits).float()
+    assert (got - ref).abs().max() <= LOGIT_ATOL
+    assert torch.nn.functional.cosine_similarity(got, ref, dim=1).min() >= 0.999
+
+
+@pytest.mark.slow
+def test_0p6b_oracle_reproduces_native_greedy_128(cpu_threads):
+    from hackthenorth_b200.config import QWEN3_0P6B
+    from hackthenorth_b200.weights import random_state_dict
+    from oracle.qwen3_oracle import OracleQwen3
+
+    g = _golden_json()
+    state = random_state_dict(QWEN3_0P6B, 0)
+    o = OracleQwen3(QWEN3_0P6B, state, 32 + 128)
+    logits = []
+    toks = o.greedy(g["prompt"], 128, logits)
+    assert toks == g["tokens"]
+    worst = 0.0
+    for row, s in zip(logits, g["steps"]):
+        ids = torch.tensor(s["top_ids"])
+        worst = max(worst, float((row.float()[ids] - torch.tensor(s["top_vals"])).abs().max()))
+    assert worst <= LOGIT_ATOL
+
+
+def _tiny_model():
+    # dryft/tests/test_decode.py:40-53 fixture, with head_dim 128 so the same
+    # shapes also run on the GPU kernels.
+    from hackthenorth_b200.config import ModelConfig
+
+    return ModelConfig("tiny", hidden=256, n_heads=4, n_kv_heads=2, head_dim=128, ffn=512, n_layers=2,
+                       vocab=97, rope_theta=1e6)
+
+
+def test_fixed_cache_matches_full_prefix_and_excludes_stale_slots(cpu_threads):
+    # dryft/tests/test_decode.py:92-115
+    from hackthenorth_b200.weights import random_state_dict
+    from oracle import hf_eager
+    from oracle.qwen3_oracle import OracleQwen3
+
+    cfg = _tiny_model()
+    state = random_state_dict(cfg, 7)
+    model = hf_eager.build_hf_model(cfg, state)
+    gen = torch.Generator().manual_seed(7)
+    for prompt_length, steps in ((1, 5), (7, 6), (4, 1)):
+        cap = prompt_length + steps - 1
+        o = OracleQwen3(cfg, state, cap)
+        for repeat in range(2):
+            o.keys.fill_(1000 if repeat else -1000)
+            o.values.fill_(1000 if repeat else -1000)
+            prefix = torch.randint(0, cfg.vocab, (prompt_length,), generator=gen).tolist()
+            _, cur = o.prefill(prefix)
+            for step in range(steps):
+                with torch.inference_mode():
+                    exp = int(model(torch.tensor([prefix]), use_cache=False).logits[0, -1].float().argmax())
+                assert cur == exp
+                prefix.append(cur)
+                if step + 1 < steps:
+                    _, cur = o.step(cur, prompt_length + step)
+
+
+def test_multi_token_verification_and_rollback_match_native(cpu_threads):
+    # dryft/tests/test_decode.py:117-167
+    from hackthenorth_b200.speculate import verified_tokens
+    from hackthenorth_b200.weights import random_state_dict
+    from oracle import hf_eager
+    from oracle.qwen3_oracle import OracleQwen3
+
+    cfg = _tiny_model()
+    state = random_state_dict(cfg, 7)
+    model = hf_eager.build_hf_model(cfg, state)
+    o = OracleQwen3(cfg, state, 20)
+    gen = torch.Generator().manual_seed(11)
+
+    def native_next(prefix):
+        with torch.inference_mode():
+            return model(torch.tensor([prefix]), use_cache=False).logits[0, -1]
+
+    for accept_count in range(4):
+        prompt = torch.randint(0, cfg.vocab, (7,), generator=gen).tolist()
+        _, cur = o.prefill(prompt)
+        prefix = prompt + [cur]
+        proposal, dp = [], list(prefix)
+        for _ in range(3):
+            d = int(native_next(dp).float().argmax())
+            proposal.append(d)
+            dp.append(d)
+        if accept_count < 3:
+            proposal[accept_count] = (proposal[accept_count] + 1) % cfg.vocab
+        logits, preds = o.forward_rows([cur] + proposal, 7)
+        with torch.inference_mode():
+            teacher = model(torch.tensor([prompt + [cur] + proposal]), use_cache=False).logits[0, 7:]
+        assert (logits.float() - teacher.float()).abs().max() <= LOGIT_ATOL
+        emitted = verified_tokens(proposal, preds.tolist())
+        assert len(emitted) == accept_count + 1
+        for tok in emitted:
+            assert tok == int(native_next(prefix).float().argmax())
+            prefix.append(tok)
+        lg, nxt = o.step(emitted[-1], 7 + len(emitted))
+        ref = native_next(prefix)
+        assert (lg.float() - ref.float()).abs().max() <= LOGIT_ATOL
+        assert nxt == int(ref.float().argmax())
