@@ -99,21 +99,42 @@ def test_bad_token_is_reported_not_faulted(small_engine):
 
 
 @pytest.mark.slow
-def test_0p6b_engine_matches_native_greedy_128(built_lib):
+def test_0p6b_engine_matches_native_greedy_128(built_lib, cpu_threads):
+    """0.6B shape, 32-token prompt, 128 greedy steps.
+
+    1. Teacher-forced on the native tokens: the top-64 logits of every step
+       within LOGIT_ATOL and the native token within LOGIT_ATOL of our max.
+    2. Free-running: identical tokens up to the first step where the native
+       logits themselves hold an exact top-1/top-2 tie (seed-1 prompt: step 14,
+       2.828125 for ids 5664 and 64516); past a genuine tie any other summation
+       order may pick the other id.
+    3. All 128 free-running tokens pass the reference judge's rule
+       (dryft/QWEN_ENGINE_CONTRACT.md:105-121) with a margin of LOGIT_ATOL
+       instead of 2.0: replayed teacher-forced through native Transformers on
+       our own prefix, each token is the argmax or within LOGIT_ATOL of it.
+    """
     from hackthenorth_b200.config import QWEN3_0P6B
     from hackthenorth_b200.engine import Engine
+    from hackthenorth_b200.weights import random_state_dict
+    from oracle import hf_eager
 
     with open(os.path.join(GOLDEN, "qwen3_0p6b_greedy.json")) as f:
         g = json.load(f)
-    engine = Engine.from_random(QWEN3_0P6B, seed=0)
+    state = random_state_dict(QWEN3_0P6B, 0)
+    engine = Engine(None, "cuda:0", cfg=QWEN3_0P6B, state=state)
     got = _teacher_forced(engine, g["prompt"], g["tokens"])
-    worst, cos_min = 0.0, 1.0
-    for row, s in zip(got, g["steps"]):
+    worst = 0.0
+    for i, (row, s) in enumerate(zip(got, g["steps"])):
         ids = torch.tensor(s["top_ids"])
         worst = max(worst, float((row[ids] - torch.tensor(s["top_vals"])).abs().max()))
-        # the emitted (golden) token must be this step's argmax, or within the
-        # reference's own quality margin when the reference itself had a tie
-        assert row.max() - row[s["top_ids"][0]] <= max(LOGIT_ATOL, 0.0)
+        assert row.max() - row[g["tokens"][i]] <= LOGIT_ATOL
     assert worst <= LOGIT_ATOL
+
     free = [s[0] for s in engine.generate([g["prompt"]], 128)]
-    assert free == g["tokens"], f"first divergence at step {next(i for i, (a, b) in enumerate(zip(free, g['tokens'])) if a != b)}"
+    first_tie = next((i for i, s in enumerate(g["steps"]) if s["margin"] == 0.0), 128)
+    assert free[:first_tie] == g["tokens"][:first_tie]
+
+    model = hf_eager.build_hf_model(QWEN3_0P6B, state)
+    native = hf_eager.teacher_forced_logits(model, g["prompt"] + free[:-1], len(g["prompt"]) - 1).float()
+    deficits = native.max(-1).values - native[torch.arange(128), torch.tensor(free)]
+    assert float(deficits.max()) <= LOGIT_ATOL, f"worst deficit {float(deficits.max())} at {int(deficits.argmax())}"
