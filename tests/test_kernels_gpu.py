@@ -19,12 +19,16 @@ BF16 = torch.bfloat16
 DEV = "cuda:0"
 
 
-def _close_bf16(out, ref, max_frac=0.05, rel=2 ** -7):
+def _close_bf16(out, ref, max_frac=0.05, rel=2 ** -7, scale=None):
+    """``scale``: magnitude of an intermediate that was rounded before a final
+    add (the projection before its residual); a one-ulp difference there is
+    bounded by rel*|scale| even when the output itself is near zero."""
     out = out.detach().float().cpu().reshape(-1)
     ref = ref.detach().float().cpu().reshape(-1)
     assert torch.isfinite(out).all()
     diff = (out - ref).abs()
-    bound = rel * ref.abs() + 1e-6
+    mag = ref.abs() if scale is None else torch.maximum(ref.abs(), scale.detach().float().cpu().reshape(-1).abs())
+    bound = rel * mag + 1e-6
     assert bool((diff <= bound).all()), f"max diff {diff.max().item()} (rel bound {rel})"
     frac = (out != ref).float().mean().item()
     assert frac <= max_frac, f"{frac:.3%} of outputs differ"
@@ -89,7 +93,8 @@ def test_projection_residual_matches_oracle(K, N):
         w = (torch.randn(N, K) * 0.02).to(BF16)
         res = torch.randn(N).to(BF16)
         out = ops.output_projection_residual(x.to(DEV), w.to(DEV), res.to(DEV))
-        _close_bf16(out, linear(x[None], w)[0] + res, max_frac=0.08, rel=2 ** -6)
+        proj = linear(x[None], w)[0]
+        _close_bf16(out, proj + res, max_frac=0.08, rel=2 ** -6, scale=proj)
 
 
 def test_greedy_head_matches_oracle_and_breaks_ties_low():
