@@ -55,6 +55,8 @@ SIGNATURES = {
     "qb_rope_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p,
                                   c_int, c_int, c_int, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "qb_op_check": (c_int, [c_void_p, c_void_p]),
+    "qb_grouped_attention_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
+                                             c_void_p, c_void_p, c_void_p]),
 }
 
 _lib = None

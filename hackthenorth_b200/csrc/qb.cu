@@ -15,6 +15,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -693,3 +694,104 @@ int qb_rope_attention(const void* qkv, const void* q_norm, const void* k_norm, c
 }
 
 }  // extern "C"
+
+// =========================================== allocation-free grouped attention
+// Some hosts cannot let this library allocate device memory: servers and
+// plugin hosts that hand out GPU memory only from their own pools sized at
+// start-up (a stray cudaMalloc can stall the device and breaks their memory
+// budget), or callers with a hard memory limit fixed before the first request.
+// For them qb_grouped_attention_noalloc keeps the split-KV partials in the
+// array below instead of a caller-provided scratch buffer. The array exists on
+// every GPU that loads this library, for the life of the process.
+namespace {
+
+constexpr size_t kStaticHeaderBytes = 4096;          // error word at 0, counters at 256 (64 x u32)
+constexpr size_t kStaticPartialBytes = 2u << 20;     // split partial outputs + log-sum-exps
+constexpr size_t kStaticScratchBytes = kStaticHeaderBytes + kStaticPartialBytes;
+constexpr int kStaticMaxDevices = 64;
+
+static __device__ __align__(256) uint8_t g_attn_static_scratch[kStaticScratchBytes];
+
+// Device address of g_attn_static_scratch per device. In host code the array's
+// name is only a host-side stand-in, so the address must come from
+// cudaGetSymbolAddress, called with the device current.
+uint8_t* g_static_scratch_ptr[kStaticMaxDevices] = {};
+std::mutex g_static_scratch_mu;
+
+int static_scratch_for_current_device(uint8_t** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaGetDevice");
+  if (dev < 0 || dev >= kStaticMaxDevices) return set_err(nullptr, QB_ERR_UNSUPPORTED, "device index above 63");
+  std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+  if (g_static_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attn_static_scratch);
+    if (e != cudaSuccess || p == nullptr) return cuda_fail(nullptr, e, "cudaGetSymbolAddress(static attention scratch)");
+    g_static_scratch_ptr[dev] = static_cast<uint8_t*>(p);
+  }
+  *out = g_static_scratch_ptr[dev];
+  return QB_OK;
+}
+
+}  // namespace
+
+extern "C" int qb_grouped_attention_noalloc(const void* q, const void* k_cache, const void* v_cache, int n_heads,
+                                            int n_kv_heads, int capacity, int queries, const int64_t* positions,
+                                            void* out, int* device_status, void* stream) {
+  if (!ptr_ok(q) || !ptr_ok(k_cache) || !ptr_ok(v_cache) || !ptr_ok(out) || !positions)
+    return set_err(nullptr, QB_ERR_ARG, "q, caches, out and positions must be aligned device pointers");
+  if (n_kv_heads <= 0 || n_heads <= 0 || n_heads % n_kv_heads != 0)
+    return set_err(nullptr, QB_ERR_ARG, "n_heads must be a multiple of n_kv_heads");
+  if (n_kv_heads > 64) return set_err(nullptr, QB_ERR_UNSUPPORTED, "more than 64 KV heads");
+  if (capacity <= 0) return set_err(nullptr, QB_ERR_ARG, "capacity must be positive");
+  if (queries < 1 || queries > 8) return set_err(nullptr, QB_ERR_UNSUPPORTED, "queries must be 1..8");
+  const int rows = (n_heads / n_kv_heads) * queries;
+  if (rows > 32) return set_err(nullptr, QB_ERR_UNSUPPORTED, "group x queries above 32 rows");
+  // One split of one KV head needs padded_rows x (128 + 1) floats.
+  const int padded = rows <= 16 ? 16 : 32;
+  const size_t per_split = (size_t)n_kv_heads * padded * (kAttnD + 1) * sizeof(float);
+  const int fit = (int)((kStaticPartialBytes - 256) / per_split);  // 256: LSE block alignment
+  if (fit < 1)
+    return set_err(nullptr, QB_ERR_UNSUPPORTED,
+                   "n_kv_heads x padded query rows exceeds the 2 MiB static attention scratch");
+  int splits = attn_splits_for(n_kv_heads, current_sm_count());
+  if (splits > fit) splits = fit;
+
+  uint8_t* s = nullptr;
+  int rc = static_scratch_for_current_device(&s);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // The array keeps the previous call's contents: clear the error word and the
+  // merge counters (they must start at zero) on this call's stream.
+  cudaError_t e = cudaMemsetAsync(s, 0, 512, st);
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, "clear static scratch header");
+  if (device_status != nullptr && (e = cudaMemsetAsync(device_status, 0, sizeof(int), st)) != cudaSuccess)
+    return cuda_fail(nullptr, e, "clear device status");
+
+  CUtensorMap tk, tv;
+  if (!make_kv_map(&tk, k_cache, n_kv_heads, capacity) || !make_kv_map(&tv, v_cache, n_kv_heads, capacity))
+    return set_err(nullptr, QB_ERR_CUDA, "cuTensorMapEncodeTiled failed");
+  AttnArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.q = static_cast<const bf16*>(q);
+  a.pos = positions;
+  a.k_cache = static_cast<bf16*>(const_cast<void*>(k_cache));
+  a.v_cache = static_cast<bf16*>(const_cast<void*>(v_cache));
+  a.out = static_cast<bf16*>(out);
+  const size_t lse_bytes = align_up((size_t)n_kv_heads * splits * padded * sizeof(float), 256);
+  a.part_lse = reinterpret_cast<float*>(s + kStaticHeaderBytes);
+  a.part_o = reinterpret_cast<float*>(s + kStaticHeaderBytes + lse_bytes);
+  a.counters = reinterpret_cast<unsigned*>(s + 256);
+  a.err = device_status != nullptr ? device_status : reinterpret_cast<int*>(s);
+  a.Hq = n_heads;
+  a.Hkv = n_kv_heads;
+  a.Q = queries;
+  a.cap = capacity;
+  a.splits = splits;
+  if (lse_bytes + (size_t)n_kv_heads * splits * padded * kAttnD * sizeof(float) > kStaticPartialBytes)
+    return set_err(nullptr, QB_ERR_UNSUPPORTED, "static attention scratch too small for this call");
+  e = launch_attn(tk, tv, a, false, st);
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, "attention launch");
+  return QB_OK;
+}

@@ -170,6 +170,29 @@ int qb_rope_attention(const void* qkv, const void* q_norm, const void* k_norm,
                       int capacity, const int64_t* position, void* out,
                       void* scratch, size_t scratch_bytes, void* stream);
 
+/* qb_grouped_attention without a scratch argument, for callers that cannot
+ * let this library allocate device memory (hosts that hand out GPU memory only
+ * from their own pools sized at start-up, or that run under a memory limit
+ * fixed before the first request). No counterpart in the reference.
+ * Allocates nothing: the split-KV partials live in a 2 MiB + 4 KiB static
+ * device array built into libqb.so, present on every GPU that loads the
+ * library until the process exits. The first call on a device looks up that
+ * array's device address (cudaGetSymbolAddress, with the device current);
+ * make that first call before any stream capture. Limits: those of
+ * qb_grouped_attention (head_dim 128, <= 64 KV heads, queries 1..8, group x
+ * queries <= 32 rows); the split count is reduced so the partials fit in
+ * 2 MiB, and a call whose single split would not fit returns
+ * QB_ERR_UNSUPPORTED. Every call shares the one array and clears its counters
+ * first, so calls that overlap on the GPU (different streams, or different
+ * host threads) race and must be serialised by the caller. device_status:
+ * optional device int, zeroed by the call and set non-zero by a device-side
+ * error (same codes as the error word qb_op_check reads); with NULL such
+ * errors are not reported. */
+int qb_grouped_attention_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                 int n_heads, int n_kv_heads, int capacity, int queries,
+                                 const int64_t* positions, void* out, int* device_status,
+                                 void* stream);
+
 /* Read the device error word of an op-level scratch (synchronises stream). */
 int qb_op_check(void* scratch, void* stream);
 
