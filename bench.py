@@ -239,6 +239,12 @@ def run_ours(args):
     world, rank, local = dist_setup(args.gpus)
     qbuild.build()
     cfg = get_config(args.config)
+    if args.layers:
+        # Profiling only: fewer layers of the same shapes (keeps each kernel's
+        # launch identical, and the device footprint small enough for ncu).
+        import dataclasses
+
+        cfg = dataclasses.replace(cfg, n_layers=args.layers)
     dev = torch.device(f"cuda:{local}")
     peak_gbs, peak_kind = load_peaks()
     engine = Engine.from_random(cfg, seed=0, device=str(dev), init_device=str(dev))
@@ -336,6 +342,7 @@ def run_ours(args):
                 "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
                 "d2h_bytes_per_step": host_out.numel() * host_out.element_size()},
         "gpu_launches": launches_per_step * args.steps,
+        "profile_only": bool(args.layers),
         "clocks": clk,
     }
     if world == 1 and not args.no_cpu_baseline:
@@ -393,6 +400,8 @@ def main(argv=None):
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="profiling only: override the layer count (the line is marked profile_only)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")

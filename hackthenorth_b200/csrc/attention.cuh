@@ -455,17 +455,40 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   named_barrier(kAttnBarrierId, kAttnWarps * 32);
   if (flags[1] == 0) return;
   __threadfence();
-  for (int r = 0; r < nrows; ++r) {
-    const size_t base = (size_t)kvh * S * ROWS + r;
+  // Merge weights exp2(lse_s - max) / sum, as dryft/engine/kernels/attention.py:204-206.
+  // All LSEs are loaded at once (independent loads), each row's weights are
+  // computed once, then every (row, dim) output sums its S partials in split order.
+  float* wts = reinterpret_cast<float*>(ring);  // [nrows][S]; the ring is free now
+  for (int i = ctid; i < nrows * S; i += kAttnWarps * 32) {
+    const int r = i / S, sp = i - r * S;
+    wts[i] = __ldcg(a.part_lse + ((size_t)kvh * S + sp) * ROWS + r);
+  }
+  named_barrier(kAttnBarrierId, kAttnWarps * 32);
+  if (ctid < nrows) {
+    float* wr = wts + ctid * S;
     float mx = -INFINITY;
-    for (int sp = 0; sp < S; ++sp) mx = fmaxf(mx, __ldcg(a.part_lse + base + (size_t)sp * ROWS));
+    for (int sp = 0; sp < S; ++sp) mx = fmaxf(mx, wr[sp]);
     float wsum = 0.f;
-    for (int sp = 0; sp < S; ++sp) wsum += exp2f(__ldcg(a.part_lse + base + (size_t)sp * ROWS) - mx);
+    for (int sp = 0; sp < S; ++sp) wsum += exp2f(wr[sp] - mx);
+    for (int sp = 0; sp < S; ++sp) wr[sp] = exp2f(wr[sp] - mx) / wsum;
+  }
+  named_barrier(kAttnBarrierId, kAttnWarps * 32);
+  for (int r = 0; r < nrows; ++r) {
+    const float* wr = wts + r * S;
+    const float* po = a.part_o + ((size_t)kvh * S * ROWS + r) * kAttnD + d;
     float acc = 0.f;
-    for (int sp = 0; sp < S; ++sp) {
-      const float w = exp2f(__ldcg(a.part_lse + base + (size_t)sp * ROWS) - mx) / wsum;
-      acc += __ldcg(a.part_o + (base + (size_t)sp * ROWS) * kAttnD + d) * w;
+    int sp = 0;
+    for (; sp + 4 <= S; sp += 4) {
+      const float p0 = __ldcg(po + (size_t)(sp + 0) * ROWS * kAttnD);
+      const float p1 = __ldcg(po + (size_t)(sp + 1) * ROWS * kAttnD);
+      const float p2 = __ldcg(po + (size_t)(sp + 2) * ROWS * kAttnD);
+      const float p3 = __ldcg(po + (size_t)(sp + 3) * ROWS * kAttnD);
+      acc += p0 * wr[sp];
+      acc += p1 * wr[sp + 1];
+      acc += p2 * wr[sp + 2];
+      acc += p3 * wr[sp + 3];
     }
+    for (; sp < S; ++sp) acc += __ldcg(po + (size_t)sp * ROWS * kAttnD) * wr[sp];
     const int g = r / a.Q, qi = r % a.Q;
     a.out[((size_t)qi * a.Hq + kvh * G + g) * kAttnD + d] = __float2bfloat16_rn(acc);
   }

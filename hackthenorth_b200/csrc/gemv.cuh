@@ -4,19 +4,21 @@
 //
 // Design (HBM-bound: every weight byte is read exactly once per decode step):
 //  * grid = one CTA per SM; CTA b owns the contiguous row range
-//    [b*U/G, (b+1)*U/G) of the row-major weight (U = output units), so its
-//    bytes are one contiguous stream.
-//  * one producer lane streams that range through a ring of 16 KB stages with
-//    1D bulk copies (cp.async.bulk + mbarrier complete_tx), evict-first in L2;
-//  * 8 consumer warps: warp w takes the 512-byte "warp chunks" w, w+8, ... of
-//    the stream; lane l multiplies 8 weights by x[col .. col+8) held in shared
-//    memory and accumulates in fp32. Because K is a multiple of 256, a warp
-//    chunk never straddles rows; when a warp moves to a new row it reduces its
-//    partial (shuffles) into red[row][warp]. The epilogue sums the 8 warp
-//    partials in a fixed order, so results are deterministic.
+//    [b*U/G, (b+1)*U/G) of the row-major weight (U = output units), which
+//    balances the work to within one row.
+//  * rows are taken 8 at a time (one per consumer warp) and K in pieces of
+//    1024 columns: a 16 KB stage holds the same 1024-column piece of 8 rows,
+//    brought in by 8 one-dimensional bulk copies (cp.async.bulk + mbarrier
+//    complete_tx, 2 KB each, evict-first in L2) issued by one producer lane
+//    into a ring of 3-8 stages;
+//  * consumer warp w owns row w of every 8-row block for the whole K, so it
+//    accumulates in registers (fp32) across stages and reduces across its
+//    lanes (5 shuffles) once per row; x sits in shared memory as fp32 after
+//    the prologue. Each row's sum has one fixed order, so results are
+//    deterministic;
 //  * PDL: the producer fills the ring before griddepcontrol.wait (weights are
-//    immutable), so a GEMV's first ~100 KB per SM load while the previous
-//    kernel is still finishing.
+//    immutable), so a GEMV streams its first stages while the previous kernel
+//    finishes.
 #pragma once
 #include "common.cuh"
 
@@ -24,10 +26,10 @@ namespace qb {
 
 constexpr int kGemvConsumerWarps = 8;
 constexpr int kGemvThreads = (kGemvConsumerWarps + 1) * 32;
-constexpr int kGemvStageBytes = 16384;
-constexpr int kGemvWarpChunk = 512;  // bytes: 32 lanes x 16 B
-constexpr int kGemvChunksPerStage = kGemvStageBytes / kGemvWarpChunk;  // 32
-constexpr int kGemvBarrierId = 1;    // named barrier of the 256 consumer threads
+constexpr int kGemvKChunk = 1024;                                   // columns per row piece
+constexpr int kGemvPieceBytes = kGemvKChunk * 2;                    // 2 KB
+constexpr int kGemvStageBytes = kGemvConsumerWarps * kGemvPieceBytes;  // 16 KB
+constexpr int kGemvBarrierId = 1;  // named barrier of the 256 consumer threads
 
 enum GemvEpilogue : int { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
 
@@ -52,14 +54,28 @@ struct GemvArgs {
   int64_t* pos_inc;     // optional: *pos_inc += 1 once the result is written
   int* err;             // device error word
   int stages;           // ring stages
-  int max_rows;         // max rows any CTA owns (size of red)
+  int max_rows;         // max rows any CTA owns (size of rowsum)
 };
 
 __host__ __device__ inline int gemv_rows_per_unit(int epi) { return epi == EPI_SWIGLU ? 2 : 1; }
 
 __host__ inline size_t gemv_smem_bytes(int K, int stages, int max_rows) {
-  return (size_t)stages * kGemvStageBytes + (size_t)K * 2 + (size_t)max_rows * kGemvConsumerWarps * 4 +
+  return (size_t)stages * kGemvStageBytes + (size_t)K * 4 + (((size_t)max_rows * 4 + 15) & ~size_t(15)) +
          (size_t)2 * stages * 8 + 64 * 4;
+}
+
+__device__ __forceinline__ float dot8_f32x(const uint4 w, const float* x, float acc) {
+  const float4 x0 = *reinterpret_cast<const float4*>(x);
+  const float4 x1 = *reinterpret_cast<const float4*>(x + 4);
+  acc = fmaf(bf_lo(w.x), x0.x, acc);
+  acc = fmaf(bf_hi(w.x), x0.y, acc);
+  acc = fmaf(bf_lo(w.y), x0.z, acc);
+  acc = fmaf(bf_hi(w.y), x0.w, acc);
+  acc = fmaf(bf_lo(w.z), x1.x, acc);
+  acc = fmaf(bf_hi(w.z), x1.y, acc);
+  acc = fmaf(bf_lo(w.w), x1.z, acc);
+  acc = fmaf(bf_hi(w.w), x1.w, acc);
+  return acc;
 }
 
 template <int EPI>
@@ -79,13 +95,14 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
   const int u1 = (int)(((long long)units * (b + 1)) / G);
   const int r0 = u0 * rpu;
   const int nrows = (u1 - u0) * rpu;
-  const long long bytes_total = (long long)nrows * K * 2;
-  const int nchunks = (int)((bytes_total + kGemvStageBytes - 1) / kGemvStageBytes);
+  const int nkc = (K + kGemvKChunk - 1) / kGemvKChunk;
+  const int nblk = (nrows + kGemvConsumerWarps - 1) / kGemvConsumerWarps;
+  const int nstage = nblk * nkc;
 
   uint8_t* ring = smem;
-  bf16* xs = reinterpret_cast<bf16*>(smem + (size_t)stages * kGemvStageBytes);
-  float* red = reinterpret_cast<float*>(xs + K);
-  uint64_t* full = reinterpret_cast<uint64_t*>(red + (size_t)a.max_rows * kGemvConsumerWarps);
+  float* xs = reinterpret_cast<float*>(smem + (size_t)stages * kGemvStageBytes);
+  float* rowsum = xs + K;
+  uint64_t* full = reinterpret_cast<uint64_t*>(rowsum + ((a.max_rows + 3) & ~3));
   uint64_t* empty = full + stages;
   float* misc = reinterpret_cast<float*>(empty + stages);
 
@@ -102,12 +119,11 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
   if (warp == kGemvConsumerWarps) {
     // ---------------- producer warp ----------------
     if (lane == 0) {
-      const uint8_t* src = reinterpret_cast<const uint8_t*>(a.w + (size_t)r0 * K);
       const uint64_t policy = policy_evict_first();
       int issued = 0;
       bool ok = true;
       bool waited = false;
-      for (int c = 0; c < nchunks; ++c) {
+      for (int c = 0; c < nstage; ++c) {
         const int s = c % stages;
         if (c >= stages) {
           if (!waited) {
@@ -120,10 +136,15 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
             break;
           }
         }
-        const long long left = bytes_total - (long long)c * kGemvStageBytes;
-        const uint32_t bytes = (uint32_t)(left < kGemvStageBytes ? left : kGemvStageBytes);
-        mbar_arrive_expect_tx(&full[s], bytes);
-        bulk_g2s(ring + (size_t)s * kGemvStageBytes, src + (size_t)c * kGemvStageBytes, bytes, &full[s], policy);
+        const int blk = c / nkc, kc = c - blk * nkc;
+        const int nr = min(kGemvConsumerWarps, nrows - blk * kGemvConsumerWarps);
+        const int c0 = kc * kGemvKChunk;
+        const uint32_t piece = (uint32_t)min(kGemvKChunk, K - c0) * 2;
+        mbar_arrive_expect_tx(&full[s], piece * nr);
+        const bf16* src = a.w + (size_t)(r0 + blk * kGemvConsumerWarps) * K + c0;
+        uint8_t* dst = ring + (size_t)s * kGemvStageBytes;
+        for (int r = 0; r < nr; ++r)
+          bulk_g2s(dst + r * kGemvPieceBytes, src + (size_t)r * K, piece, &full[s], policy);
         issued = c + 1;
       }
       if (!waited) {
@@ -147,7 +168,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
   pdl_wait();
   pdl_trigger();
 
-  // 1. Input row (optionally the embedding gather) and its RMSNorm.
+  // 1. Input row (optionally the embedding gather) and its RMSNorm, to fp32 smem.
   const bf16* xsrc = a.x;
   if (a.embed != nullptr) {
     long long t = *a.token;
@@ -160,18 +181,15 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
   float ss = 0.f;
   for (int i = ctid * 8; i < K; i += 256 * 8) {
     const uint4 v = ldg128_nc(xsrc + i);
-    *reinterpret_cast<uint4*>(xs + i) = v;
     if (a.x_copy != nullptr && b == 0) *reinterpret_cast<uint4*>(a.x_copy + i) = v;
-    ss = fmaf(bf_lo(v.x), bf_lo(v.x), ss);
-    ss = fmaf(bf_hi(v.x), bf_hi(v.x), ss);
-    ss = fmaf(bf_lo(v.y), bf_lo(v.y), ss);
-    ss = fmaf(bf_hi(v.y), bf_hi(v.y), ss);
-    ss = fmaf(bf_lo(v.z), bf_lo(v.z), ss);
-    ss = fmaf(bf_hi(v.z), bf_hi(v.z), ss);
-    ss = fmaf(bf_lo(v.w), bf_lo(v.w), ss);
-    ss = fmaf(bf_hi(v.w), bf_hi(v.w), ss);
+    const float f[8] = {bf_lo(v.x), bf_hi(v.x), bf_lo(v.y), bf_hi(v.y),
+                        bf_lo(v.z), bf_hi(v.z), bf_lo(v.w), bf_hi(v.w)};
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      xs[i + j] = f[j];
+      ss = fmaf(f[j], f[j], ss);
+    }
   }
-  for (int i = ctid; i < a.max_rows * kGemvConsumerWarps; i += 256) red[i] = 0.f;
   if (a.gain != nullptr) {
     ss = warp_sum(ss);
     if (lane == 0) misc[warp] = ss;
@@ -182,97 +200,74 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
     // rsqrt(mean(x^2) + eps) as 1/sqrt: correctly rounded sqrt and division.
     const float inv = 1.0f / sqrtf(tot / (float)K + a.eps);
     for (int i = ctid * 8; i < K; i += 256 * 8) {
-      uint4 v = *reinterpret_cast<const uint4*>(xs + i);
       const uint4 g = ldg128_nc(a.gain + i);
-      uint32_t* pv = reinterpret_cast<uint32_t*>(&v);
-      const uint32_t* pg = reinterpret_cast<const uint32_t*>(&g);
+      const float gf[8] = {bf_lo(g.x), bf_hi(g.x), bf_lo(g.y), bf_hi(g.y),
+                           bf_lo(g.z), bf_hi(g.z), bf_lo(g.w), bf_hi(g.w)};
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float n0 = round_bf16(bf_lo(pv[j]) * inv) * bf_lo(pg[j]);
-        const float n1 = round_bf16(bf_hi(pv[j]) * inv) * bf_hi(pg[j]);
-        pv[j] = pack_bf16(n0, n1);
-      }
-      *reinterpret_cast<uint4*>(xs + i) = v;
+      for (int j = 0; j < 8; ++j) xs[i + j] = round_bf16(round_bf16(xs[i + j] * inv) * gf[j]);
     }
   }
   named_barrier(kGemvBarrierId, 256);
 
-  // 2. Stream the weights.
-  const int wc_total = (int)(bytes_total / kGemvWarpChunk);
-  int row = 0;
-  int col = warp * 256;
-  while (col >= K) { col -= K; ++row; }
-  int cur_row = row;
-  float acc = 0.f;
-  bool touched = false;
+  // 2. Stream the weights: warp w owns row w of every 8-row block.
+  float rowacc = 0.f;
   bool ok = true;
-  for (int c = 0; c < nchunks && ok; ++c) {
+  for (int c = 0; c < nstage; ++c) {
     const int s = c % stages;
     if (!mbar_wait(&full[s], (c / stages) & 1, a.err, DEV_TIMEOUT_GEMV_FULL)) {
       ok = false;
       break;
     }
-    const uint8_t* st = ring + (size_t)s * kGemvStageBytes;
-    const int base_wc = c * kGemvChunksPerStage;
-    const int nwc = min(kGemvChunksPerStage, wc_total - base_wc);
-    float d[kGemvChunksPerStage / kGemvConsumerWarps];
-    int rws[kGemvChunksPerStage / kGemvConsumerWarps];
-#pragma unroll
-    for (int j = 0; j < kGemvChunksPerStage / kGemvConsumerWarps; ++j) {
-      const int wc = warp + kGemvConsumerWarps * j;
-      d[j] = 0.f;
-      rws[j] = row;
-      if (wc < nwc) {
-        const uint4 wv = lds128(st + wc * kGemvWarpChunk + lane * 16);
-        const uint4 xv = lds128(xs + col + lane * 8);
-        d[j] = dot8(wv, xv, 0.f);
-        col += kGemvConsumerWarps * 256;
-        while (col >= K) { col -= K; ++row; }
-      }
-    }
-#pragma unroll
-    for (int j = 0; j < kGemvChunksPerStage / kGemvConsumerWarps; ++j) {
-      const int wc = warp + kGemvConsumerWarps * j;
-      if (wc < nwc) {
-        if (rws[j] != cur_row) {
-          const float t = warp_sum(acc);
-          if (lane == 0) red[cur_row * kGemvConsumerWarps + warp] = t;
-          acc = 0.f;
-          cur_row = rws[j];
+    const int blk = c / nkc, kc = c - blk * nkc;
+    const int row = blk * kGemvConsumerWarps + warp;
+    if (row < nrows) {
+      const int c0 = kc * kGemvKChunk;
+      const int nwc = min(kGemvKChunk, K - c0) >> 8;  // 256-column warp chunks: 1..4
+      const uint8_t* piece = ring + (size_t)s * kGemvStageBytes + warp * kGemvPieceBytes + lane * 16;
+      const float* xp = xs + c0 + lane * 8;
+      float a0 = 0.f, a1 = 0.f;
+      if (nwc == 4) {
+        const uint4 w0 = lds128(piece);
+        const uint4 w1 = lds128(piece + 512);
+        const uint4 w2 = lds128(piece + 1024);
+        const uint4 w3 = lds128(piece + 1536);
+        a0 = dot8_f32x(w0, xp, a0);
+        a1 = dot8_f32x(w1, xp + 256, a1);
+        a0 = dot8_f32x(w2, xp + 512, a0);
+        a1 = dot8_f32x(w3, xp + 768, a1);
+      } else {
+        for (int j = 0; j < nwc; ++j) {
+          const uint4 wv = lds128(piece + j * 512);
+          if (j & 1) a1 = dot8_f32x(wv, xp + j * 256, a1);
+          else a0 = dot8_f32x(wv, xp + j * 256, a0);
         }
-        acc += d[j];
-        touched = true;
+      }
+      rowacc += a0 + a1;
+      if (kc == nkc - 1) {
+        const float t = warp_sum(rowacc);
+        if (lane == 0) rowsum[row] = t;
+        rowacc = 0.f;
       }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-  }
-  if (touched) {
-    const float t = warp_sum(acc);
-    if (lane == 0) red[cur_row * kGemvConsumerWarps + warp] = t;
   }
   if (!ok && lane == 0) reinterpret_cast<volatile int*>(misc)[60] = 1;
   named_barrier(kGemvBarrierId, 256);
   if (reinterpret_cast<volatile int*>(misc)[60] != 0) return;  // uniform across the CTA
 
   // 3. Epilogue.
-  auto row_sum = [&](int r) {
-    float s = 0.f;
-#pragma unroll
-    for (int w = 0; w < kGemvConsumerWarps; ++w) s += red[r * kGemvConsumerWarps + w];
-    return s;
-  };
   if constexpr (EPI == EPI_STORE) {
-    for (int r = ctid; r < nrows; r += 256) a.out[r0 + r] = __float2bfloat16_rn(row_sum(r));
+    for (int r = ctid; r < nrows; r += 256) a.out[r0 + r] = __float2bfloat16_rn(rowsum[r]);
   } else if constexpr (EPI == EPI_RESIDUAL) {
     for (int r = ctid; r < nrows; r += 256) {
-      const float p = round_bf16(row_sum(r));
+      const float p = round_bf16(rowsum[r]);
       a.out[r0 + r] = __float2bfloat16_rn(p + __bfloat162float(a.residual[r0 + r]));
     }
   } else if constexpr (EPI == EPI_SWIGLU) {
     for (int j = ctid; j < nrows / 2; j += 256) {
-      const float g = round_bf16(row_sum(2 * j));
-      const float u = round_bf16(row_sum(2 * j + 1));
+      const float g = round_bf16(rowsum[2 * j]);
+      const float u = round_bf16(rowsum[2 * j + 1]);
       const float act = round_bf16(silu_f32(g));
       a.out[r0 / 2 + j] = __float2bfloat16_rn(act * u);
     }
@@ -280,7 +275,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
     float best = -INFINITY;
     int best_i = 0x7fffffff;
     for (int r = ctid; r < nrows; r += 256) {
-      const bf16 lb = __float2bfloat16_rn(row_sum(r));
+      const bf16 lb = __float2bfloat16_rn(rowsum[r]);
       if (a.logits != nullptr) a.logits[r0 + r] = lb;
       const float v = __bfloat162float(lb);
       if (v > best) { best = v; best_i = r0 + r; }  // rows ascend: first max kept

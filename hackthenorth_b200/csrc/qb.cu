@@ -31,8 +31,10 @@ thread_local std::string g_last_error = "";
 
 // Per-CTA shared-memory budget of the GEMV: two CTAs of consecutive kernels
 // fit on one SM (228 KB), which is what lets PDL overlap them.
-constexpr size_t kGemvSmemBudget = 113 * 1024;
-constexpr int kMaxGemvStages = 8;
+// QB_GEMV_SMEM_KB overrides the budget (tuning: a deeper ring keeps more bytes
+// in flight per SM but stops the next kernel's CTAs from co-residing).
+constexpr size_t kGemvSmemBudgetDefault = 113 * 1024;
+constexpr int kMaxGemvStages = 12;
 constexpr size_t kOpScratchBytes = 16u << 20;
 
 // Op-level scratch layout (bytes).
@@ -99,7 +101,18 @@ struct GemvPlan {
   size_t smem;
 };
 
+size_t gemv_smem_budget() {
+  static size_t v = 0;
+  if (v == 0) {
+    const char* e = std::getenv("QB_GEMV_SMEM_KB");
+    long kb = e ? std::strtol(e, nullptr, 10) : 0;
+    v = (kb >= 48 && kb <= 227) ? (size_t)kb * 1024 : kGemvSmemBudgetDefault;
+  }
+  return v;
+}
+
 bool plan_gemv(int epi, int K, int rows, int sm_count, GemvPlan* p) {
+  const size_t kGemvSmemBudget = gemv_smem_budget();
   const int rpu = gemv_rows_per_unit(epi);
   const int units = rows / rpu;
   if (units <= 0) return false;
