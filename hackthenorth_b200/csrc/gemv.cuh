@@ -24,12 +24,14 @@
 
 namespace qb {
 
-constexpr int kGemvConsumerWarps = 8;
-constexpr int kGemvThreads = (kGemvConsumerWarps + 1) * 32;
-constexpr int kGemvKChunk = 1024;                                   // columns per row piece
-constexpr int kGemvPieceBytes = kGemvKChunk * 2;                    // 2 KB
-constexpr int kGemvStageBytes = kGemvConsumerWarps * kGemvPieceBytes;  // 16 KB
-constexpr int kGemvBarrierId = 1;  // named barrier of the 256 consumer threads
+constexpr int kGemvConsumerWarps = 16;
+constexpr int kGemvConsumers = kGemvConsumerWarps * 32;
+constexpr int kGemvThreads = kGemvConsumers + 32;
+// A stage holds the same kc-column piece (kc = 1024 or 2048) of 16 rows:
+// 16 one-dimensional bulk copies of 2 or 4 KB, one per row, issued by 16
+// producer lanes in parallel.
+__host__ __device__ inline int gemv_stage_bytes(int kc) { return kGemvConsumerWarps * kc * 2; }
+constexpr int kGemvBarrierId = 1;  // named barrier of the consumer threads
 
 enum GemvEpilogue : int { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
 
@@ -55,31 +57,39 @@ struct GemvArgs {
   int* err;             // device error word
   int stages;           // ring stages
   int max_rows;         // max rows any CTA owns (size of rowsum)
+  int kc;               // columns per row piece: 1024 or 2048
 };
 
 __host__ __device__ inline int gemv_rows_per_unit(int epi) { return epi == EPI_SWIGLU ? 2 : 1; }
 
-__host__ inline size_t gemv_smem_bytes(int K, int stages, int max_rows) {
-  return (size_t)stages * kGemvStageBytes + (size_t)K * 4 + (((size_t)max_rows * 4 + 15) & ~size_t(15)) +
-         (size_t)2 * stages * 8 + 64 * 4;
+__host__ inline size_t gemv_smem_bytes(int K, int stages, int max_rows, int kc) {
+  return (size_t)stages * gemv_stage_bytes(kc) + (size_t)K * 2 + (((size_t)max_rows * 4 + 15) & ~size_t(15)) +
+         (size_t)2 * stages * 8 + 128 * 4;
 }
 
-__device__ __forceinline__ float dot8_f32x(const uint4 w, const float* x, float acc) {
-  const float4 x0 = *reinterpret_cast<const float4*>(x);
-  const float4 x1 = *reinterpret_cast<const float4*>(x + 4);
-  acc = fmaf(bf_lo(w.x), x0.x, acc);
-  acc = fmaf(bf_hi(w.x), x0.y, acc);
-  acc = fmaf(bf_lo(w.y), x0.z, acc);
-  acc = fmaf(bf_hi(w.y), x0.w, acc);
-  acc = fmaf(bf_lo(w.z), x1.x, acc);
-  acc = fmaf(bf_hi(w.z), x1.y, acc);
-  acc = fmaf(bf_lo(w.w), x1.z, acc);
-  acc = fmaf(bf_hi(w.w), x1.w, acc);
+// acc += w.x for two packed bf16 pairs with sm_100's mixed-precision FMA
+// (bf16 operands, fp32 addend and result, one rounding): the same value as
+// converting both operands to fp32 and calling fmaf.
+__device__ __forceinline__ float fma2_bf16(uint32_t w, uint32_t x, float acc) {
+  asm("{\n\t.reg .b16 wl, wh, xl, xh;\n\t"
+      "mov.b32 {wl, wh}, %1;\n\t"
+      "mov.b32 {xl, xh}, %2;\n\t"
+      "fma.rn.f32.bf16 %0, wl, xl, %0;\n\t"
+      "fma.rn.f32.bf16 %0, wh, xh, %0;\n\t}"
+      : "+f"(acc)
+      : "r"(w), "r"(x));
+  return acc;
+}
+__device__ __forceinline__ float dot8_bf16(const uint4 w, const uint4 x, float acc) {
+  acc = fma2_bf16(w.x, x.x, acc);
+  acc = fma2_bf16(w.y, x.y, acc);
+  acc = fma2_bf16(w.z, x.z, acc);
+  acc = fma2_bf16(w.w, x.w, acc);
   return acc;
 }
 
 template <int EPI>
-__global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -95,13 +105,15 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
   const int u1 = (int)(((long long)units * (b + 1)) / G);
   const int r0 = u0 * rpu;
   const int nrows = (u1 - u0) * rpu;
-  const int nkc = (K + kGemvKChunk - 1) / kGemvKChunk;
+  const int KC = a.kc;
+  const int stage_bytes = gemv_stage_bytes(KC);
+  const int nkc = (K + KC - 1) / KC;
   const int nblk = (nrows + kGemvConsumerWarps - 1) / kGemvConsumerWarps;
   const int nstage = nblk * nkc;
 
   uint8_t* ring = smem;
-  float* xs = reinterpret_cast<float*>(smem + (size_t)stages * kGemvStageBytes);
-  float* rowsum = xs + K;
+  bf16* xs = reinterpret_cast<bf16*>(smem + (size_t)stages * stage_bytes);
+  float* rowsum = reinterpret_cast<float*>(xs + K);
   uint64_t* full = reinterpret_cast<uint64_t*>(rowsum + ((a.max_rows + 3) & ~3));
   uint64_t* empty = full + stages;
   float* misc = reinterpret_cast<float*>(empty + stages);
@@ -112,59 +124,58 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
       mbar_init(&empty[s], kGemvConsumerWarps);
     }
     fence_mbar_init();
-    reinterpret_cast<int*>(misc)[60] = 0;  // CTA-wide abort flag
+    reinterpret_cast<int*>(misc)[100] = 0;  // CTA-wide abort flag
   }
   __syncthreads();
 
   if (warp == kGemvConsumerWarps) {
     // ---------------- producer warp ----------------
-    if (lane == 0) {
-      const uint64_t policy = policy_evict_first();
-      int issued = 0;
-      bool ok = true;
-      bool waited = false;
-      for (int c = 0; c < nstage; ++c) {
-        const int s = c % stages;
-        if (c >= stages) {
-          if (!waited) {
-            pdl_wait();
-            pdl_trigger();
-            waited = true;
-          }
-          if (!mbar_wait(&empty[s], ((c / stages) - 1) & 1, a.err, DEV_TIMEOUT_GEMV_EMPTY)) {
-            ok = false;
-            break;
-          }
+    // Lane r copies row r of each 16-row block; lane 0 also drives the ring.
+    const uint64_t policy = policy_evict_first();
+    int issued = 0;
+    bool ok = true;
+    bool waited = false;
+    for (int c = 0; c < nstage; ++c) {
+      const int s = c % stages;
+      if (c >= stages) {
+        if (!waited) {
+          pdl_wait();
+          pdl_trigger();
+          waited = true;
         }
-        const int blk = c / nkc, kc = c - blk * nkc;
-        const int nr = min(kGemvConsumerWarps, nrows - blk * kGemvConsumerWarps);
-        const int c0 = kc * kGemvKChunk;
-        const uint32_t piece = (uint32_t)min(kGemvKChunk, K - c0) * 2;
-        mbar_arrive_expect_tx(&full[s], piece * nr);
-        const bf16* src = a.w + (size_t)(r0 + blk * kGemvConsumerWarps) * K + c0;
-        uint8_t* dst = ring + (size_t)s * kGemvStageBytes;
-        for (int r = 0; r < nr; ++r)
-          bulk_g2s(dst + r * kGemvPieceBytes, src + (size_t)r * K, piece, &full[s], policy);
-        issued = c + 1;
+        int good = 1;
+        if (lane == 0) good = mbar_wait(&empty[s], ((c / stages) - 1) & 1, a.err, DEV_TIMEOUT_GEMV_EMPTY) ? 1 : 0;
+        good = __shfl_sync(0xffffffffu, good, 0);
+        if (!good) {
+          ok = false;
+          break;
+        }
       }
-      if (!waited) {
-        pdl_wait();
-        pdl_trigger();
-      }
-      if (!ok) {
-        // Keep shared memory alive until the copies already in flight land.
-        for (int c = (issued > stages ? issued - stages : 0); c < issued; ++c)
-          mbar_wait(&full[c % stages], (c / stages) & 1, nullptr, 0);
-      }
-    } else {
+      const int blk = c / nkc, kc = c - blk * nkc;
+      const int nr = min(kGemvConsumerWarps, nrows - blk * kGemvConsumerWarps);
+      const int c0 = kc * KC;
+      const uint32_t piece = (uint32_t)min(KC, K - c0) * 2;
+      if (lane == 0) mbar_arrive_expect_tx(&full[s], piece * nr);
+      __syncwarp();
+      if (lane < nr)
+        bulk_g2s(ring + (size_t)s * stage_bytes + lane * (KC * 2),
+                 a.w + (size_t)(r0 + blk * kGemvConsumerWarps + lane) * K + c0, piece, &full[s], policy);
+      issued = c + 1;
+    }
+    if (!waited) {
       pdl_wait();
       pdl_trigger();
+    }
+    if (!ok && lane == 0) {
+      // Keep shared memory alive until the copies already in flight land.
+      for (int c = (issued > stages ? issued - stages : 0); c < issued; ++c)
+        mbar_wait(&full[c % stages], (c / stages) & 1, nullptr, 0);
     }
     return;
   }
 
-  // ---------------- consumer warps (256 threads) ----------------
-  const int ctid = tid;  // 0..255
+  // ---------------- consumer warps ----------------
+  const int ctid = tid;  // 0..kGemvConsumers-1
   pdl_wait();
   pdl_trigger();
 
@@ -179,93 +190,104 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
     xsrc = a.embed + (size_t)t * K;
   }
   float ss = 0.f;
-  for (int i = ctid * 8; i < K; i += 256 * 8) {
+  for (int i = ctid * 8; i < K; i += kGemvConsumers * 8) {
     const uint4 v = ldg128_nc(xsrc + i);
     if (a.x_copy != nullptr && b == 0) *reinterpret_cast<uint4*>(a.x_copy + i) = v;
-    const float f[8] = {bf_lo(v.x), bf_hi(v.x), bf_lo(v.y), bf_hi(v.y),
-                        bf_lo(v.z), bf_hi(v.z), bf_lo(v.w), bf_hi(v.w)};
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      xs[i + j] = f[j];
-      ss = fmaf(f[j], f[j], ss);
-    }
+    *reinterpret_cast<uint4*>(xs + i) = v;
+    ss = fmaf(bf_lo(v.x), bf_lo(v.x), ss);
+    ss = fmaf(bf_hi(v.x), bf_hi(v.x), ss);
+    ss = fmaf(bf_lo(v.y), bf_lo(v.y), ss);
+    ss = fmaf(bf_hi(v.y), bf_hi(v.y), ss);
+    ss = fmaf(bf_lo(v.z), bf_lo(v.z), ss);
+    ss = fmaf(bf_hi(v.z), bf_hi(v.z), ss);
+    ss = fmaf(bf_lo(v.w), bf_lo(v.w), ss);
+    ss = fmaf(bf_hi(v.w), bf_hi(v.w), ss);
   }
   if (a.gain != nullptr) {
     ss = warp_sum(ss);
     if (lane == 0) misc[warp] = ss;
-    named_barrier(kGemvBarrierId, 256);
+    named_barrier(kGemvBarrierId, kGemvConsumers);
     float tot = 0.f;
 #pragma unroll
     for (int w = 0; w < kGemvConsumerWarps; ++w) tot += misc[w];
     // rsqrt(mean(x^2) + eps) as 1/sqrt: correctly rounded sqrt and division.
     const float inv = 1.0f / sqrtf(tot / (float)K + a.eps);
-    for (int i = ctid * 8; i < K; i += 256 * 8) {
+    for (int i = ctid * 8; i < K; i += kGemvConsumers * 8) {
+      uint4 v = *reinterpret_cast<const uint4*>(xs + i);
       const uint4 g = ldg128_nc(a.gain + i);
-      const float gf[8] = {bf_lo(g.x), bf_hi(g.x), bf_lo(g.y), bf_hi(g.y),
-                           bf_lo(g.z), bf_hi(g.z), bf_lo(g.w), bf_hi(g.w)};
+      uint32_t* pv = reinterpret_cast<uint32_t*>(&v);
+      const uint32_t* pg = reinterpret_cast<const uint32_t*>(&g);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) xs[i + j] = round_bf16(round_bf16(xs[i + j] * inv) * gf[j]);
+      for (int j = 0; j < 4; ++j) {
+        const float n0 = round_bf16(bf_lo(pv[j]) * inv) * bf_lo(pg[j]);
+        const float n1 = round_bf16(bf_hi(pv[j]) * inv) * bf_hi(pg[j]);
+        pv[j] = pack_bf16(n0, n1);
+      }
+      *reinterpret_cast<uint4*>(xs + i) = v;
     }
   }
-  named_barrier(kGemvBarrierId, 256);
+  named_barrier(kGemvBarrierId, kGemvConsumers);
 
-  // 2. Stream the weights: warp w owns row w of every 8-row block.
+  // 2. Stream the weights: warp w owns row w of every 16-row block.
   float rowacc = 0.f;
   bool ok = true;
-  for (int c = 0; c < nstage; ++c) {
-    const int s = c % stages;
-    if (!mbar_wait(&full[s], (c / stages) & 1, a.err, DEV_TIMEOUT_GEMV_FULL)) {
-      ok = false;
-      break;
-    }
-    const int blk = c / nkc, kc = c - blk * nkc;
+  int c = 0;
+  for (int blk = 0; blk < nblk && ok; ++blk) {
     const int row = blk * kGemvConsumerWarps + warp;
-    if (row < nrows) {
-      const int c0 = kc * kGemvKChunk;
-      const int nwc = min(kGemvKChunk, K - c0) >> 8;  // 256-column warp chunks: 1..4
-      const uint8_t* piece = ring + (size_t)s * kGemvStageBytes + warp * kGemvPieceBytes + lane * 16;
-      const float* xp = xs + c0 + lane * 8;
-      float a0 = 0.f, a1 = 0.f;
-      if (nwc == 4) {
-        const uint4 w0 = lds128(piece);
-        const uint4 w1 = lds128(piece + 512);
-        const uint4 w2 = lds128(piece + 1024);
-        const uint4 w3 = lds128(piece + 1536);
-        a0 = dot8_f32x(w0, xp, a0);
-        a1 = dot8_f32x(w1, xp + 256, a1);
-        a0 = dot8_f32x(w2, xp + 512, a0);
-        a1 = dot8_f32x(w3, xp + 768, a1);
-      } else {
-        for (int j = 0; j < nwc; ++j) {
-          const uint4 wv = lds128(piece + j * 512);
-          if (j & 1) a1 = dot8_f32x(wv, xp + j * 256, a1);
-          else a0 = dot8_f32x(wv, xp + j * 256, a0);
+    const bool active = row < nrows;
+    for (int kc = 0; kc < nkc; ++kc, ++c) {
+      const int s = c % stages;
+      if (!mbar_wait(&full[s], (c / stages) & 1, a.err, DEV_TIMEOUT_GEMV_FULL)) {
+        ok = false;
+        break;
+      }
+      if (active) {
+        const int c0 = kc * KC;
+        const uint8_t* piece = ring + (size_t)s * stage_bytes + warp * (KC * 2) + lane * 16;
+        const bf16* xp = xs + c0 + lane * 8;
+        const int ncols = min(KC, K - c0);
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+        int j = 0;
+        for (; j + 1024 <= ncols; j += 1024) {
+          const uint4 w0 = lds128(piece + j * 2);
+          const uint4 w1 = lds128(piece + j * 2 + 512);
+          const uint4 w2 = lds128(piece + j * 2 + 1024);
+          const uint4 w3 = lds128(piece + j * 2 + 1536);
+          const uint4 x0 = lds128(xp + j);
+          const uint4 x1 = lds128(xp + j + 256);
+          const uint4 x2 = lds128(xp + j + 512);
+          const uint4 x3 = lds128(xp + j + 768);
+          a0 = dot8_bf16(w0, x0, a0);
+          a1 = dot8_bf16(w1, x1, a1);
+          a2 = dot8_bf16(w2, x2, a2);
+          a3 = dot8_bf16(w3, x3, a3);
+        }
+        for (; j < ncols; j += 256) a0 = dot8_bf16(lds128(piece + j * 2), lds128(xp + j), a0);
+        rowacc += (a0 + a1) + (a2 + a3);
+        if (kc == nkc - 1) {
+          const float t = warp_sum(rowacc);
+          if (lane == 0) rowsum[row] = t;
+          rowacc = 0.f;
         }
       }
-      rowacc += a0 + a1;
-      if (kc == nkc - 1) {
-        const float t = warp_sum(rowacc);
-        if (lane == 0) rowsum[row] = t;
-        rowacc = 0.f;
-      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
   }
-  if (!ok && lane == 0) reinterpret_cast<volatile int*>(misc)[60] = 1;
-  named_barrier(kGemvBarrierId, 256);
-  if (reinterpret_cast<volatile int*>(misc)[60] != 0) return;  // uniform across the CTA
+  if (!ok && lane == 0) reinterpret_cast<volatile int*>(misc)[100] = 1;
+  named_barrier(kGemvBarrierId, kGemvConsumers);
+  if (reinterpret_cast<volatile int*>(misc)[100] != 0) return;  // uniform across the CTA
 
   // 3. Epilogue.
   if constexpr (EPI == EPI_STORE) {
-    for (int r = ctid; r < nrows; r += 256) a.out[r0 + r] = __float2bfloat16_rn(rowsum[r]);
+    for (int r = ctid; r < nrows; r += kGemvConsumers) a.out[r0 + r] = __float2bfloat16_rn(rowsum[r]);
   } else if constexpr (EPI == EPI_RESIDUAL) {
-    for (int r = ctid; r < nrows; r += 256) {
+    for (int r = ctid; r < nrows; r += kGemvConsumers) {
       const float p = round_bf16(rowsum[r]);
       a.out[r0 + r] = __float2bfloat16_rn(p + __bfloat162float(a.residual[r0 + r]));
     }
   } else if constexpr (EPI == EPI_SWIGLU) {
-    for (int j = ctid; j < nrows / 2; j += 256) {
+    for (int j = ctid; j < nrows / 2; j += kGemvConsumers) {
       const float g = round_bf16(rowsum[2 * j]);
       const float u = round_bf16(rowsum[2 * j + 1]);
       const float act = round_bf16(silu_f32(g));
@@ -274,7 +296,7 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
   } else {  // EPI_ARGMAX
     float best = -INFINITY;
     int best_i = 0x7fffffff;
-    for (int r = ctid; r < nrows; r += 256) {
+    for (int r = ctid; r < nrows; r += kGemvConsumers) {
       const bf16 lb = __float2bfloat16_rn(rowsum[r]);
       if (a.logits != nullptr) a.logits[r0 + r] = lb;
       const float v = __bfloat162float(lb);
@@ -287,26 +309,26 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
       if (ov > best || (ov == best && oi < best_i)) { best = ov; best_i = oi; }
     }
     int* misci = reinterpret_cast<int*>(misc);
-    if (lane == 0) { misc[8 + warp] = best; misci[16 + warp] = best_i; }
-    named_barrier(kGemvBarrierId, 256);
+    if (lane == 0) { misc[16 + warp] = best; misci[32 + warp] = best_i; }
+    named_barrier(kGemvBarrierId, kGemvConsumers);
     if (ctid == 0) {
       for (int w = 0; w < kGemvConsumerWarps; ++w) {
-        const float ov = misc[8 + w];
-        const int oi = misci[16 + w];
+        const float ov = misc[16 + w];
+        const int oi = misci[32 + w];
         if (ov > best || (ov == best && oi < best_i)) { best = ov; best_i = oi; }
       }
       a.part_val[b] = best;
       a.part_idx[b] = best_i;
       __threadfence();
       const unsigned ticket = atomicAdd(a.counter, 1u);
-      misci[32] = (ticket == (unsigned)(G - 1)) ? 1 : 0;
+      misci[48] = (ticket == (unsigned)(G - 1)) ? 1 : 0;
     }
-    named_barrier(kGemvBarrierId, 256);
-    if (misci[32]) {
+    named_barrier(kGemvBarrierId, kGemvConsumers);
+    if (misci[48]) {
       __threadfence();
       best = -INFINITY;
       best_i = 0x7fffffff;
-      for (int i = ctid; i < G; i += 256) {
+      for (int i = ctid; i < G; i += kGemvConsumers) {
         const float ov = __ldcg(a.part_val + i);
         const int oi = __ldcg(a.part_idx + i);
         if (ov > best || (ov == best && oi < best_i)) { best = ov; best_i = oi; }
@@ -317,12 +339,12 @@ __global__ void __launch_bounds__(kGemvThreads, 2) gemv_kernel(const GemvArgs a)
         const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
         if (ov > best || (ov == best && oi < best_i)) { best = ov; best_i = oi; }
       }
-      if (lane == 0) { misc[40 + warp] = best; misci[48 + warp] = best_i; }
-      named_barrier(kGemvBarrierId, 256);
+      if (lane == 0) { misc[64 + warp] = best; misci[80 + warp] = best_i; }
+      named_barrier(kGemvBarrierId, kGemvConsumers);
       if (ctid == 0) {
         for (int w = 0; w < kGemvConsumerWarps; ++w) {
-          const float ov = misc[40 + w];
-          const int oi = misci[48 + w];
+          const float ov = misc[64 + w];
+          const int oi = misci[80 + w];
           if (ov > best || (ov == best && oi < best_i)) { best = ov; best_i = oi; }
         }
         *a.token_out = (best_i == 0x7fffffff) ? 0 : (int64_t)best_i;

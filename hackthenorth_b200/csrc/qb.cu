@@ -33,7 +33,7 @@ thread_local std::string g_last_error = "";
 // fit on one SM (228 KB), which is what lets PDL overlap them.
 // QB_GEMV_SMEM_KB overrides the budget (tuning: a deeper ring keeps more bytes
 // in flight per SM but stops the next kernel's CTAs from co-residing).
-constexpr size_t kGemvSmemBudgetDefault = 113 * 1024;
+constexpr size_t kGemvSmemBudgetDefault = 220 * 1024;
 constexpr int kMaxGemvStages = 12;
 constexpr size_t kOpScratchBytes = 16u << 20;
 
@@ -97,9 +97,18 @@ cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sm
 
 // ---------------------------------------------------------------- GEMV launch
 struct GemvPlan {
-  int grid, stages, max_rows;
+  int grid, stages, max_rows, kc;
   size_t smem;
 };
+
+int gemv_kc_pref() {
+  static int v = 0;
+  if (v == 0) {
+    const char* e = std::getenv("QB_GEMV_KC");
+    v = (e && std::strtol(e, nullptr, 10) == 1024) ? 1024 : 2048;
+  }
+  return v;
+}
 
 size_t gemv_smem_budget() {
   static size_t v = 0;
@@ -118,13 +127,17 @@ bool plan_gemv(int epi, int K, int rows, int sm_count, GemvPlan* p) {
   if (units <= 0) return false;
   p->grid = units < sm_count ? units : sm_count;
   p->max_rows = ((units + p->grid - 1) / p->grid) * rpu;
-  const size_t fixed = gemv_smem_bytes(K, 0, p->max_rows);
+  const size_t fixed = gemv_smem_bytes(K, 0, p->max_rows, 1024);
+  // Wider pieces when K allows and the ring still holds >= 3 of them.
+  int kc = (K >= 2048 && gemv_kc_pref() == 2048) ? 2048 : 1024;
+  if (kc == 2048 && (fixed + 3 * (size_t)(gemv_stage_bytes(2048) + 16) > kGemvSmemBudget)) kc = 1024;
   int stages = 0;
-  if (fixed < kGemvSmemBudget) stages = (int)((kGemvSmemBudget - fixed) / (kGemvStageBytes + 16));
+  if (fixed < kGemvSmemBudget) stages = (int)((kGemvSmemBudget - fixed) / (gemv_stage_bytes(kc) + 16));
   if (stages > kMaxGemvStages) stages = kMaxGemvStages;
   if (stages < 2) stages = 2;
+  p->kc = kc;
   p->stages = stages;
-  p->smem = gemv_smem_bytes(K, stages, p->max_rows);
+  p->smem = gemv_smem_bytes(K, stages, p->max_rows, kc);
   return p->smem <= 227 * 1024;
 }
 
@@ -140,6 +153,7 @@ cudaError_t launch_gemv(GemvArgs a, int sm_count, cudaStream_t st) {
   if (!plan_gemv(EPI, a.K, a.rows, sm_count, &p)) return cudaErrorInvalidValue;
   a.stages = p.stages;
   a.max_rows = p.max_rows;
+  a.kc = p.kc;
   return launch_ex(gemv_kernel<EPI>, dim3(p.grid), dim3(kGemvThreads), p.smem, st, a);
 }
 
