@@ -204,6 +204,19 @@ def sum_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
+def profiled_traffic(name):
+    """dram__bytes_read.sum + dram__bytes_write.sum per launch from the
+    committed ncu summary ``profiles/<name>.md`` (None if absent)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", name + ".md")) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return int(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
 def time_dominant_kernel(engine, reps_per_layer=2):
     """Gate/up + SwiGLU GEMV (about half of a step's bytes) launched alone over
     every layer's weights in turn, timed with CUDA events on the launching
@@ -333,7 +346,8 @@ def run_ours(args):
                      "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
                      "frac": round(achieved / peak_gbs, 4), "peak_source": peak_kind,
                      "bytes_per_launch": kern_bytes, "us_per_launch": round(kern_s * 1e6, 2),
-                     "traffic": None},
+                     "traffic": profiled_traffic("gemv_swiglu_qwen3-8b") if cfg.name == "qwen3-8b" else None,
+                     "traffic_source": "ncu capture, profiles/gemv_swiglu_qwen3-8b.md"},
         "step_roofline": {"bytes_per_step": step_bytes, "achieved": round(step_bytes / (t_dev / args.steps) / 1e9, 1),
                           "peak": peak_gbs, "unit": "GB/s",
                           "frac": round(step_bytes / (t_dev / args.steps) / 1e9 / peak_gbs, 4),
