@@ -371,6 +371,50 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_attention_sweep(args):
+    """Op sweep of SURVEY config 2 (GQA 32/8, D 128, bf16 N(0,1), batch 1):
+    KV lengths 512..131072, 1 query row and the 5-row causal verify variant.
+    Each timed launch reads a different KV buffer (>= 256 MB cycled), so the
+    K/V bytes come from HBM. One JSON line with a per-case list."""
+    from hackthenorth_b200 import build as qbuild
+    from hackthenorth_b200 import ops
+
+    qbuild.build()
+    torch.cuda.set_device(0)
+    peak_gbs, peak_kind = load_peaks()
+    gen = torch.Generator(device="cuda").manual_seed(2)
+    cases = []
+    for L in (512, 4096, 32768, 131072):
+        for queries in (1, 5):
+            per_call = 2 * 8 * L * 128 * 2
+            nbuf = max(2, min(64, -(-(256 << 20) // per_call)))
+            kv = [(torch.randn(8, L, 128, generator=gen, device="cuda").to(torch.bfloat16),
+                   torch.randn(8, L, 128, generator=gen, device="cuda").to(torch.bfloat16)) for _ in range(nbuf)]
+            q = torch.randn(queries, 32, 128, generator=gen, device="cuda").to(torch.bfloat16)
+            pos = torch.arange(L - queries, L, device="cuda")
+            for k, v in kv[:2]:
+                ops.grouped_attention(q, k, v, pos)
+            torch.cuda.synchronize()
+            reps = max(args.warmup + 3, 40 if L <= 4096 else 10)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(reps):
+                k, v = kv[i % nbuf]
+                ops.grouped_attention(q, k, v, pos)
+            e1.record()
+            torch.cuda.synchronize()
+            ops.check_device_errors()
+            sec = e0.elapsed_time(e1) / 1000.0 / reps
+            nbytes = per_call + 2 * q.numel() * 2 + queries * 8
+            cases.append({"kv_len": L, "queries": queries, "us": round(sec * 1e6, 2),
+                          "GBps": round(nbytes / sec / 1e9, 1), "frac": round(nbytes / sec / 1e9 / peak_gbs, 4)})
+            del kv
+            torch.cuda.empty_cache()
+    print(json.dumps({"op": "grouped_attention", "metric": "decode attention us and GB/s of K/V reads",
+                      "peak_gbs": peak_gbs, "peak_source": peak_kind, "dtype": "bf16",
+                      "config": {"q_heads": 32, "kv_heads": 8, "head_dim": 128}, "cases": cases}), flush=True)
+
+
 def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -414,6 +458,8 @@ def main(argv=None):
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--op", choices=("decode", "attention"), default="decode",
+                    help="attention: the decode-attention op sweep (not the headline line)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: override the layer count (the line is marked profile_only)")
     args = ap.parse_args(argv)
@@ -421,6 +467,8 @@ def main(argv=None):
         ap.error("--warmup must be at least 3")
     if args.impl == "reference":
         run_reference(args)
+    elif args.op == "attention":
+        run_attention_sweep(args)
     else:
         run_ours(args)
 

@@ -5,16 +5,20 @@
 // computed on the device from the live position, so one captured launch stays
 // balanced as the context grows.
 //
-// Per CTA: one producer lane streams 16-key stages of K and V with 2D TMA tensor
-// loads ([16 keys][64 dims] boxes, 128-byte swizzle, no multicast) into an
-// 8-stage ring; 4 consumer warps take stages round-robin and run
+// Per CTA: one producer lane streams 64-key stages of K and V with 2D TMA tensor
+// loads ([64 keys][64 dims] boxes of 8 KB, 128-byte swizzle, no multicast) into
+// a 4-stage ring; 4 consumer warps take stages round-robin and, 16 keys at a
+// time, run
 // S = Q.K^T and O += P.V on mma.sync m16n8k16 (bf16 in, fp32 accumulate) with a
 // base-2 online softmax; P is rounded to bf16 before the P.V product and the
 // softmax denominator sums the unrounded fp32 P, as the reference kernel does
 // (dryft/engine/kernels/attention.py:49-57). Rows are (head-in-group, query)
 // pairs of one KV head, head-major, padded to 16 or 32. The 4 warps' states are
-// combined in a fixed order; splits are merged by log-sum-exp in the CTA that
-// arrives last for its KV head (dryft/engine/kernels/attention.py:200-210).
+// combined in a fixed order; splits are merged by log-sum-exp
+// (dryft/engine/kernels/attention.py:200-210). Decode launches one thread-block
+// cluster per KV head and merges through the leader CTA's shared memory
+// (attn_decode_cluster_kernel); other uses merge through global memory in the
+// CTA that arrives last for its KV head (attn_kernel).
 //
 // PRO (decode prologue) variant: the CTA computes its query rows from the
 // packed QKV row (per-head RMSNorm, bf16 x gain, rotate-half RoPE with the
@@ -31,11 +35,17 @@ namespace qb {
 constexpr int kAttnD = 128;
 constexpr int kAttnWarps = 4;
 constexpr int kAttnThreads = (kAttnWarps + 1) * 32;
-constexpr int kAttnKeys = 16;
-constexpr int kAttnSubTile = kAttnKeys * 128;        // [16 keys][64 dims] bf16 = 2 KB
-constexpr int kAttnStageBytes = 4 * kAttnSubTile;    // K lo, K hi, V lo, V hi
-constexpr int kAttnStages = 8;
+constexpr int kAttnKeys = 64;                        // keys per stage (one TMA box row count)
+constexpr int kAttnSub = 16;                         // keys per mma sub-block
+constexpr int kAttnSubTile = kAttnKeys * 128;        // [64 keys][64 dims] bf16 = 8 KB
+constexpr int kAttnStageBytes = 4 * kAttnSubTile;    // K lo, K hi, V lo, V hi = 32 KB
+constexpr int kAttnStages = 4;
+// Warp w consumes stages w, w+4, ...; a ring slot must always be consumed by
+// the same warp, so that warp observes every phase of the slot's mbarrier
+// (a parity wait on a phase two steps ahead would pass immediately).
+static_assert(kAttnStages % kAttnWarps == 0, "each ring slot must map to one consumer warp");
 constexpr int kAttnBarrierId = 2;
+constexpr int kAttnMinSplitKeys = 256;
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct AttnArgs {
@@ -119,105 +129,112 @@ __device__ __forceinline__ void norm_rope_head(const bf16* src, const bf16* gain
   if (dst_global != nullptr) *reinterpret_cast<uint2*>(dst_global + 4 * lane) = ov;
 }
 
-template <int MT, bool PRO>
-__global__ void __launch_bounds__(kAttnThreads, 1)
-    attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, const AttnArgs a) {
+// Cluster helpers (thread-block clusters, distributed shared memory).
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Full-cluster barrier; every thread of every CTA in the cluster must execute it.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t map_shared_rank(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+
+struct AttnSmem {
+  uint8_t* ring;
+  bf16* qs;
+  bf16* kvnew;
+  uint64_t* full;
+  uint64_t* empty;
+  float* ml;
+  volatile int* flags;
+};
+
+template <int MT>
+__device__ __forceinline__ AttnSmem attn_carve(uint8_t* smem_raw) {
   constexpr int ROWS = 16 * MT;
-  extern __shared__ uint8_t smem_raw[];
+  AttnSmem m;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* ring = smem;
-  bf16* qs = reinterpret_cast<bf16*>(ring + kAttnStages * kAttnStageBytes);  // [ROWS][128]
-  bf16* kvnew = qs + ROWS * kAttnD;                                          // k_new[128], v_new[128]
-  uint64_t* full = reinterpret_cast<uint64_t*>(kvnew + 2 * kAttnD);
-  uint64_t* empty = full + kAttnStages;
-  float* ml = reinterpret_cast<float*>(empty + kAttnStages);  // [warps][ROWS][2]
-  volatile int* flags = reinterpret_cast<volatile int*>(ml + kAttnWarps * ROWS * 2);
+  m.ring = smem;
+  m.qs = reinterpret_cast<bf16*>(m.ring + kAttnStages * kAttnStageBytes);  // [ROWS][128]
+  m.kvnew = m.qs + ROWS * kAttnD;                                          // k_new[128], v_new[128]
+  m.full = reinterpret_cast<uint64_t*>(m.kvnew + 2 * kAttnD);
+  m.empty = m.full + kAttnStages;
+  m.ml = reinterpret_cast<float*>(m.empty + kAttnStages);  // [warps][ROWS][2]
+  m.flags = reinterpret_cast<volatile int*>(m.ml + kAttnWarps * ROWS * 2);
+  return m;
+}
 
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5;
-  const int lane = tid & 31;
-  const int S = a.splits;
-  const int kvh = blockIdx.x / S;
-  const int split = blockIdx.x % S;
-  const int G = a.Hq / a.Hkv;
-  const int nrows = G * a.Q;
-
-  if (tid == 0) {
-    for (int s = 0; s < kAttnStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
-    }
-    fence_mbar_init();
-    flags[0] = 0;
-    flags[1] = 0;
-  }
-  __syncthreads();
-
-  // Live key range. PRO reads the position before griddepcontrol.wait: it was
-  // written by the previous step, two or more launches earlier.
-  if (!PRO) {
-    pdl_wait();
-    pdl_trigger();
-  }
-  long long last = PRO ? a.pos[0] : a.pos[a.Q - 1];
-  if (last < 0 || last >= a.cap) {
-    if (tid == 0 && blockIdx.x == 0) report_error(a.err, DEV_BAD_POSITION);
-    last = -1;
-  }
-  const int n = (int)last + 1;
-  int per = (n + S - 1) / S;
-  per = (per + kAttnKeys - 1) & ~(kAttnKeys - 1);
-  const int k0 = min(n, split * per);
-  const int k1 = min(n, k0 + per);
-  const int nst = (k1 - k0 + kAttnKeys - 1) / kAttnKeys;
-
-  if (warp == kAttnWarps) {
-    // ---------------- producer ----------------
-    if (lane == 0) {
-      prefetch_tensormap(&tmk);
-      prefetch_tensormap(&tmv);
-      bool waited = !PRO;
-      bool ok = true;
-      int issued = 0;
-      for (int c = 0; c < nst; ++c) {
-        const int s = c % kAttnStages;
-        if (c >= kAttnStages) {
-          if (!waited) {
-            pdl_wait();
-            pdl_trigger();
-            waited = true;
-          }
-          if (!mbar_wait(&empty[s], ((c / kAttnStages) - 1) & 1, a.err, DEV_TIMEOUT_ATTN_EMPTY)) {
-            ok = false;
-            break;
-          }
-        }
-        uint8_t* st = ring + s * kAttnStageBytes;
-        const int y = kvh * a.cap + k0 + c * kAttnKeys;
-        mbar_arrive_expect_tx(&full[s], kAttnStageBytes);
-        tma_load_2d(st, &tmk, 0, y, &full[s]);
-        tma_load_2d(st + kAttnSubTile, &tmk, 64, y, &full[s]);
-        tma_load_2d(st + 2 * kAttnSubTile, &tmv, 0, y, &full[s]);
-        tma_load_2d(st + 3 * kAttnSubTile, &tmv, 64, y, &full[s]);
-        issued = c + 1;
-      }
+// Producer lane: stream stages [0, nst) of keys [k0, k1) of KV head kvh.
+template <bool PRO>
+__device__ __forceinline__ void attn_produce(const CUtensorMap* tmk, const CUtensorMap* tmv, const AttnArgs& a,
+                                             const AttnSmem& sm, int kvh, int k0, int nst) {
+  prefetch_tensormap(tmk);
+  prefetch_tensormap(tmv);
+  bool waited = !PRO;
+  bool ok = true;
+  int issued = 0;
+  for (int c = 0; c < nst; ++c) {
+    const int s = c % kAttnStages;
+    if (c >= kAttnStages) {
       if (!waited) {
         pdl_wait();
         pdl_trigger();
+        waited = true;
       }
-      if (!ok) {
-        for (int c = (issued > kAttnStages ? issued - kAttnStages : 0); c < issued; ++c)
-          mbar_wait(&full[c % kAttnStages], (c / kAttnStages) & 1, nullptr, 0);
+      if (!mbar_wait(&sm.empty[s], ((c / kAttnStages) - 1) & 1, a.err, DEV_TIMEOUT_ATTN_EMPTY)) {
+        ok = false;
+        break;
       }
-    } else if (PRO) {
-      pdl_wait();
-      pdl_trigger();
     }
-    return;
+    uint8_t* st = sm.ring + s * kAttnStageBytes;
+    const int y = kvh * a.cap + k0 + c * kAttnKeys;
+    mbar_arrive_expect_tx(&sm.full[s], kAttnStageBytes);
+    tma_load_2d(st, tmk, 0, y, &sm.full[s]);
+    tma_load_2d(st + kAttnSubTile, tmk, 64, y, &sm.full[s]);
+    tma_load_2d(st + 2 * kAttnSubTile, tmv, 0, y, &sm.full[s]);
+    tma_load_2d(st + 3 * kAttnSubTile, tmv, 64, y, &sm.full[s]);
+    issued = c + 1;
   }
+  if (!waited) {
+    pdl_wait();
+    pdl_trigger();
+  }
+  if (!ok) {
+    // Keep shared memory alive until the copies already in flight land.
+    for (int c = (issued > kAttnStages ? issued - kAttnStages : 0); c < issued; ++c)
+      mbar_wait(&sm.full[c % kAttnStages], (c / kAttnStages) & 1, nullptr, 0);
+  }
+}
 
-  // ---------------- consumers (128 threads) ----------------
+// Consumers: build the query rows (PRO: norm + RoPE + KV append), stream the
+// stages, and combine the 4 warps. On return thread d (< 128) holds, for every
+// row r < nrows, the split's normalised output val[r] and its log-sum-exp
+// lse[r]. Returns false if a bounded wait gave up (CTA-uniform).
+template <int MT, bool PRO>
+__device__ __forceinline__ bool attn_consume(const AttnArgs& a, const AttnSmem& sm, int kvh, long long last, int n,
+                                             int k0, int k1, int nst, float (&val)[16 * MT],
+                                             float (&lsev)[16 * MT]) {
+  constexpr int ROWS = 16 * MT;
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
   const int ctid = tid;
+  const int G = a.Hq / a.Hkv;
+  const int nrows = G * a.Q;
+  uint8_t* ring = sm.ring;
+  bf16* qs = sm.qs;
+  bf16* kvnew = sm.kvnew;
+  float* ml = sm.ml;
+
   if (PRO) {
     pdl_wait();
     pdl_trigger();
@@ -294,30 +311,32 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   bool ok = true;
   for (int c = warp; c < nst; c += kAttnWarps) {
     const int s = c % kAttnStages;
-    if (!mbar_wait(&full[s], (c / kAttnStages) & 1, a.err, DEV_TIMEOUT_ATTN_FULL)) {
+    if (!mbar_wait(&sm.full[s], (c / kAttnStages) & 1, a.err, DEV_TIMEOUT_ATTN_FULL)) {
       ok = false;
       break;
     }
-    uint8_t* st = ring + s * kAttnStageBytes;
-    const int kb = k0 + c * kAttnKeys;
-    if (owns_new && kb <= last && last < kb + kAttnKeys) {
-      const int kr = (int)last - kb;
+    uint8_t* stage = ring + s * kAttnStageBytes;
+    const int kstage = k0 + c * kAttnKeys;
+    if (owns_new && kstage <= last && last < kstage + kAttnKeys) {
+      const int kr = (int)last - kstage;
       const int which = lane >> 3, ch = lane & 7;
-      *reinterpret_cast<uint4*>(st + which * kAttnSubTile + swz(kr, ch)) =
+      *reinterpret_cast<uint4*>(stage + which * kAttnSubTile + swz(kr, ch)) =
           *reinterpret_cast<const uint4*>(kvnew + (which >> 1) * kAttnD + (which & 1) * 64 + ch * 8);
     }
-    const int valid = k1 - kb;
-    if (valid < kAttnKeys) {
+    const int svalid = k1 - kstage;
+    if (svalid < kAttnKeys) {
       // Slots past the live range may hold anything (even NaN); P is 0 there,
       // but 0 * NaN is NaN, so clear those V rows.
-      for (int i = lane; i < (kAttnKeys - valid) * 16; i += 32) {
-        const int row = valid + (i >> 4);
+      for (int i = lane; i < (kAttnKeys - svalid) * 16; i += 32) {
+        const int row = svalid + (i >> 4);
         const int sub = (i >> 3) & 1, ch = i & 7;
-        *reinterpret_cast<uint4*>(st + (2 + sub) * kAttnSubTile + swz(row, ch)) = make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(stage + (2 + sub) * kAttnSubTile + swz(row, ch)) = make_uint4(0, 0, 0, 0);
       }
     }
     __syncwarp();
-
+    for (int sb = 0; sb < kAttnKeys / kAttnSub && kstage + sb * kAttnSub < k1; ++sb) {
+    uint8_t* st = stage + sb * kAttnSub * 128;  // 16-row block inside each sub-tile
+    const int kb = kstage + sb * kAttnSub;
     float sc[MT][2][4];
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt)
@@ -394,15 +413,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         mma_bf16_16816(o[mt][2 * dp + 1], pa[mt], b[2], b[3]);
       }
     }
+    }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
+    if (lane == 0) mbar_arrive(&sm.empty[s]);
   }
-  if (!ok && lane == 0) flags[0] = 1;
+  if (!ok && lane == 0) sm.flags[0] = 1;
   named_barrier(kAttnBarrierId, kAttnWarps * 32);
-  if (flags[0] != 0) return;
+  if (sm.flags[0] != 0) return false;
 
   // Combine the four warps (fixed order) through the drained ring.
-  float* ob = reinterpret_cast<float*>(ring);  // [warps][ROWS][128]
+  constexpr int kObStride = kAttnD + 4;  // padded row: no bank conflicts on the fragment stores
+  float* ob = reinterpret_cast<float*>(ring);  // [warps][ROWS][kObStride]
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -411,7 +432,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         float2 v = make_float2(o[mt][j][h * 2], o[mt][j][h * 2 + 1]);
-        *reinterpret_cast<float2*>(ob + ((size_t)warp * ROWS + r) * kAttnD + j * 8 + 2 * t4) = v;
+        *reinterpret_cast<float2*>(ob + ((size_t)warp * ROWS + r) * kObStride + j * 8 + 2 * t4) = v;
       }
       if (t4 == 0) {
         ml[(warp * ROWS + r) * 2] = m[mt][h];
@@ -420,79 +441,252 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   named_barrier(kAttnBarrierId, kAttnWarps * 32);
   const int d = ctid;  // one head dim per thread
-  for (int r = 0; r < nrows; ++r) {
-    float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, ml[(w * ROWS + r) * 2]);
-    float L = 0.f, acc = 0.f;
+  for (int r = 0; r < ROWS; ++r) {
+    val[r] = 0.f;
+    lsev[r] = -INFINITY;
+    if (r < nrows) {
+      float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kAttnWarps; ++w) {
-      const float mw = ml[(w * ROWS + r) * 2];
-      const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
-      L += ml[(w * ROWS + r) * 2 + 1] * f;
-      acc += ob[((size_t)w * ROWS + r) * kAttnD + d] * f;
-    }
-    const float val = L > 0.f ? acc / L : 0.f;
-    const float lse = L > 0.f ? M + log2f(L) : -INFINITY;
-    const int g = r / a.Q, qi = r % a.Q;
-    if (S == 1) {
-      a.out[((size_t)qi * a.Hq + kvh * G + g) * kAttnD + d] = __float2bfloat16_rn(val);
-    } else {
-      const size_t idx = ((size_t)kvh * S + split) * ROWS + r;
-      a.part_o[idx * kAttnD + d] = val;
-      if (d == 0) a.part_lse[idx] = lse;
+      for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, ml[(w * ROWS + r) * 2]);
+      float L = 0.f, acc = 0.f;
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; ++w) {
+        const float mw = ml[(w * ROWS + r) * 2];
+        const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+        L += ml[(w * ROWS + r) * 2 + 1] * f;
+        acc += ob[((size_t)w * ROWS + r) * kObStride + d] * f;
+      }
+      val[r] = L > 0.f ? acc / L : 0.f;
+      lsev[r] = L > 0.f ? M + log2f(L) : -INFINITY;
     }
   }
-  if (S == 1) return;
+  return true;
+}
 
-  // The CTA that completes its KV head merges the S slices.
-  __threadfence();
+// Setup shared by both kernels: barriers, the live key range and this CTA's slice.
+struct AttnRange {
+  long long last;
+  int n, Se, k0, k1, nst;
+};
+
+template <int MT>
+__device__ __forceinline__ AttnRange attn_setup(const AttnArgs& a, const AttnSmem& sm, int split, bool pro) {
+  const int tid = threadIdx.x;
+  if (tid == 0) {
+    for (int s = 0; s < kAttnStages; ++s) {
+      mbar_init(&sm.full[s], 1);
+      mbar_init(&sm.empty[s], 1);
+    }
+    fence_mbar_init();
+    sm.flags[0] = 0;
+    sm.flags[1] = 0;
+  }
+  __syncthreads();
+  // Live key range. The decode prologue variant reads the position before
+  // griddepcontrol.wait: it was written by the previous step, two or more
+  // launches earlier.
+  if (!pro) {
+    pdl_wait();
+    pdl_trigger();
+  }
+  AttnRange R;
+  long long last = pro ? a.pos[0] : a.pos[a.Q - 1];
+  if (last < 0 || last >= a.cap) {
+    if (tid == 0 && blockIdx.x == 0) report_error(a.err, DEV_BAD_POSITION);
+    last = -1;
+  }
+  R.last = last;
+  R.n = (int)last + 1;
+  // Splits actually used: about kAttnMinSplitKeys keys each, at most the
+  // grid's split count. Short contexts then need no merge at all.
+  R.Se = max(1, min(a.splits, (R.n + kAttnMinSplitKeys - 1) / kAttnMinSplitKeys));
+  int per = (R.n + R.Se - 1) / R.Se;
+  per = (per + kAttnSub - 1) & ~(kAttnSub - 1);
+  R.k0 = min(R.n, split * per);
+  R.k1 = min(R.n, R.k0 + per);
+  R.nst = (R.k1 - R.k0 + kAttnKeys - 1) / kAttnKeys;
+  return R;
+}
+
+__device__ __forceinline__ void attn_store_out(const AttnArgs& a, int kvh, int r, int d, float v) {
+  const int G = a.Hq / a.Hkv;
+  const int g = r / a.Q, qi = r % a.Q;
+  a.out[((size_t)qi * a.Hq + kvh * G + g) * kAttnD + d] = __float2bfloat16_rn(v);
+}
+
+// Split-KV attention with the splits merged through global memory by the CTA
+// that arrives last for its KV head (any query count, either prologue mode).
+template <int MT, bool PRO>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    attn_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv, const AttnArgs a) {
+  constexpr int ROWS = 16 * MT;
+  extern __shared__ uint8_t smem_raw[];
+  const AttnSmem sm = attn_carve<MT>(smem_raw);
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int S = a.splits;
+  const int kvh = blockIdx.x / S;
+  const int split = blockIdx.x % S;
+  const int nrows = (a.Hq / a.Hkv) * a.Q;
+  const AttnRange R = attn_setup<MT>(a, sm, split, PRO);
+  const int Se = R.Se;
+  if (split >= Se) return;  // surplus CTA: no loads, no partials, not counted
+
+  if (warp == kAttnWarps) {
+    if ((tid & 31) == 0) attn_produce<PRO>(&tmk, &tmv, a, sm, kvh, R.k0, R.nst);
+    else if (PRO) {
+      pdl_wait();
+      pdl_trigger();
+    }
+    return;
+  }
+  float val[ROWS], lsev[ROWS];
+  if (!attn_consume<MT, PRO>(a, sm, kvh, R.last, R.n, R.k0, R.k1, R.nst, val, lsev)) return;
+  const int ctid = tid, d = tid;
+#pragma unroll
+  for (int r = 0; r < ROWS; ++r) {
+    if (r < nrows) {
+      if (Se == 1) {
+        attn_store_out(a, kvh, r, d, val[r]);
+      } else {
+        const size_t idx = ((size_t)kvh * S + split) * ROWS + r;
+        a.part_o[idx * kAttnD + d] = val[r];
+        if (d == 0) a.part_lse[idx] = lsev[r];
+      }
+    }
+  }
+  if (Se == 1) return;
+
+  // The CTA that completes its KV head merges the Se slices.
   named_barrier(kAttnBarrierId, kAttnWarps * 32);
   if (ctid == 0) {
-    const unsigned ticket = atomicAdd(&a.counters[kvh], 1u);
-    flags[1] = (ticket == (unsigned)(S - 1)) ? 1 : 0;
+    const unsigned ticket = atomic_add_acq_rel_gpu(&a.counters[kvh], 1u);
+    sm.flags[1] = (ticket == (unsigned)(Se - 1)) ? 1 : 0;
   }
   named_barrier(kAttnBarrierId, kAttnWarps * 32);
-  if (flags[1] == 0) return;
-  __threadfence();
-  // Merge weights exp2(lse_s - max) / sum, as dryft/engine/kernels/attention.py:204-206.
-  // All LSEs are loaded at once (independent loads), each row's weights are
-  // computed once, then every (row, dim) output sums its S partials in split order.
-  float* wts = reinterpret_cast<float*>(ring);  // [nrows][S]; the ring is free now
-  for (int i = ctid; i < nrows * S; i += kAttnWarps * 32) {
-    const int r = i / S, sp = i - r * S;
-    wts[i] = __ldcg(a.part_lse + ((size_t)kvh * S + sp) * ROWS + r);
-  }
-  named_barrier(kAttnBarrierId, kAttnWarps * 32);
-  if (ctid < nrows) {
-    float* wr = wts + ctid * S;
-    float mx = -INFINITY;
-    for (int sp = 0; sp < S; ++sp) mx = fmaxf(mx, wr[sp]);
-    float wsum = 0.f;
-    for (int sp = 0; sp < S; ++sp) wsum += exp2f(wr[sp] - mx);
-    for (int sp = 0; sp < S; ++sp) wr[sp] = exp2f(wr[sp] - mx) / wsum;
-  }
-  named_barrier(kAttnBarrierId, kAttnWarps * 32);
-  for (int r = 0; r < nrows; ++r) {
-    const float* wr = wts + r * S;
-    const float* po = a.part_o + ((size_t)kvh * S * ROWS + r) * kAttnD + d;
-    float acc = 0.f;
-    int sp = 0;
-    for (; sp + 4 <= S; sp += 4) {
-      const float p0 = __ldcg(po + (size_t)(sp + 0) * ROWS * kAttnD);
-      const float p1 = __ldcg(po + (size_t)(sp + 1) * ROWS * kAttnD);
-      const float p2 = __ldcg(po + (size_t)(sp + 2) * ROWS * kAttnD);
-      const float p3 = __ldcg(po + (size_t)(sp + 3) * ROWS * kAttnD);
-      acc += p0 * wr[sp];
-      acc += p1 * wr[sp + 1];
-      acc += p2 * wr[sp + 2];
-      acc += p3 * wr[sp + 3];
+  if (sm.flags[1] == 0) return;
+  // Merge by log-sum-exp: weight_s = exp2(lse_s - max) / sum_s exp2(lse_s - max)
+  // as dryft/engine/kernels/attention.py:204-206, with the division applied
+  // once after the weighted sum. Each thread owns one head dim; per batch of up
+  // to 8 splits x 4 rows the log-sum-exps and partials are loaded in a single
+  // round (indices clamped into the written range, extra terms dropped), and
+  // batches combine with a running max.
+  for (int r0 = 0; r0 < nrows; r0 += 4) {
+    float acc[4], den[4], mx[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) { acc[j] = 0.f; den[j] = 0.f; mx[j] = -INFINITY; }
+    for (int sp0 = 0; sp0 < Se; sp0 += 8) {
+      float v[8][4], lv[8][4];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const size_t idx = ((size_t)kvh * S + min(sp0 + i, Se - 1)) * ROWS + min(r0 + j, nrows - 1);
+          lv[i][j] = __ldcg(a.part_lse + idx);
+          v[i][j] = __ldcg(a.part_o + idx * kAttnD + d);
+        }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float bm = mx[j];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) bm = (sp0 + i < Se) ? fmaxf(bm, lv[i][j]) : bm;
+        const float corr = (mx[j] == -INFINITY) ? 0.f : exp2f(mx[j] - bm);
+        acc[j] *= corr;
+        den[j] *= corr;
+        mx[j] = bm;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float w = (sp0 + i < Se) ? exp2f(lv[i][j] - bm) : 0.f;
+          den[j] += w;
+          acc[j] = fmaf(v[i][j], w, acc[j]);
+        }
+      }
     }
-    for (; sp < S; ++sp) acc += __ldcg(po + (size_t)sp * ROWS * kAttnD) * wr[sp];
-    const int g = r / a.Q, qi = r % a.Q;
-    a.out[((size_t)qi * a.Hq + kvh * G + g) * kAttnD + d] = __float2bfloat16_rn(acc);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (r0 + j < nrows) attn_store_out(a, kvh, r0 + j, d, acc[j] / den[j]);
   }
   if (ctid == 0) a.counters[kvh] = 0u;
+}
+
+// Decode attention (one query row, prologue fused) with the KV head's splits
+// launched as one thread-block cluster: each CTA writes its split's output and
+// log-sum-exp into the leader CTA's shared memory (distributed shared memory),
+// and the leader merges them after a cluster barrier. No global partials, no
+// atomics. Every thread of every CTA reaches both cluster barriers, including
+// CTAs without work and CTAs whose bounded waits gave up.
+// Cluster size = a.splits; the leader's ring holds [splits][rows][129] floats.
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    attn_decode_cluster_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                               const AttnArgs a) {
+  constexpr int MT = 1;
+  constexpr int ROWS = 16;
+  extern __shared__ uint8_t smem_raw[];
+  const AttnSmem sm = attn_carve<MT>(smem_raw);
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int S = a.splits;
+  const int kvh = blockIdx.x / S;
+  const int split = blockIdx.x % S;  // == cluster rank
+  const int nrows = a.Hq / a.Hkv;
+  const AttnRange R = attn_setup<MT>(a, sm, split, true);
+  const int Se = R.Se;
+  const bool idle = split >= Se;
+  float val[ROWS], lsev[ROWS];
+  bool ok = false;
+  if (warp == kAttnWarps) {
+    if (!idle && (tid & 31) == 0) attn_produce<true>(&tmk, &tmv, a, sm, kvh, R.k0, R.nst);
+    else {
+      pdl_wait();
+      pdl_trigger();
+    }
+    __syncwarp();
+  } else if (!idle) {
+    ok = attn_consume<MT, true>(a, sm, kvh, R.last, R.n, R.k0, R.k1, R.nst, val, lsev);
+  } else {
+    pdl_wait();
+    pdl_trigger();
+  }
+  if (Se == 1) {  // uniform across the cluster: the single split is the answer
+    if (warp < kAttnWarps && split == 0 && ok)
+#pragma unroll
+      for (int r = 0; r < ROWS; ++r)
+        if (r < nrows) attn_store_out(a, kvh, r, tid, val[r]);
+    return;
+  }
+  // Barrier 1: every CTA is done with its own ring, so the leader's ring can
+  // receive the splits. Then each active CTA writes rows [nrows][128] + lse.
+  cluster_sync_all();
+  float* mbuf = reinterpret_cast<float*>(sm.ring);  // leader: [Se][nrows][128], then lse [Se][nrows]
+  float* mlse = mbuf + (size_t)S * nrows * kAttnD;
+  if (warp < kAttnWarps && !idle && ok) {
+    const uint32_t base = map_shared_rank(mbuf, 0);
+    const uint32_t lbase = map_shared_rank(mlse, 0);
+#pragma unroll
+    for (int r = 0; r < ROWS; ++r) {
+      if (r < nrows) {
+        st_cluster_f32(base + (uint32_t)(((split * nrows + r) * kAttnD + tid) * 4), val[r]);
+        if (tid == 0) st_cluster_f32(lbase + (uint32_t)((split * nrows + r) * 4), lsev[r]);
+      }
+    }
+  }
+  cluster_sync_all();
+  if (split != 0 || warp >= kAttnWarps) return;
+  // Leader: weights exp2(lse_s - max) / sum over the Se splits
+  // (dryft/engine/kernels/attention.py:204-206), summed in split order.
+  const int d = tid;
+  for (int r = 0; r < nrows; ++r) {
+    float mx = -INFINITY;
+    for (int sp = 0; sp < Se; ++sp) mx = fmaxf(mx, mlse[sp * nrows + r]);
+    float den = 0.f, acc = 0.f;
+    for (int sp = 0; sp < Se; ++sp) {
+      const float w = exp2f(mlse[sp * nrows + r] - mx);
+      den += w;
+      acc = fmaf(mbuf[(sp * nrows + r) * kAttnD + d], w, acc);
+    }
+    attn_store_out(a, kvh, r, d, acc / den);
+  }
 }
 
 }  // namespace qb

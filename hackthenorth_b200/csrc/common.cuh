@@ -158,6 +158,15 @@ __device__ __forceinline__ uint4 ldg128_nc(const void* p) {
                : "l"(p));
   return v;
 }
+// Ticket counter: one atomic with acquire-release semantics at GPU scope. The
+// caller first synchronises its CTA (bar.sync), so every thread's earlier
+// writes are released, and the CTA that draws the last ticket acquires all
+// other CTAs' writes.
+__device__ __forceinline__ unsigned atomic_add_acq_rel_gpu(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
 // Coherent (L1-bypassing) load for data written by other CTAs of this grid.
 __device__ __forceinline__ float ldcg_f32(const float* p) { return __ldcg(p); }
 

@@ -190,7 +190,7 @@ EncodeTiledFn encode_fn() {
 }
 
 // Tensor map over one layer's cache viewed as [Hkv*cap rows][128 dims] bf16,
-// box [16 rows][64 dims], 128-byte swizzle; out-of-range rows read as zero.
+// box [64 rows][64 dims], 128-byte swizzle; out-of-range rows read as zero.
 bool make_kv_map(CUtensorMap* m, const void* base, int hkv, int cap) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
@@ -222,7 +222,71 @@ cudaError_t launch_attn_t(const CUtensorMap& tk, const CUtensorMap& tv, const At
   return launch_ex(attn_kernel<MT, PRO>, dim3(a.Hkv * a.splits), dim3(kAttnThreads), smem, st, tk, tv, a);
 }
 
+// Decode attention as one thread-block cluster per KV head (splits merged
+// through distributed shared memory). Returns the cluster size to use for
+// `hkv` heads of `rows` query rows, or 0 when clusters do not fit (then the
+// global-merge kernel is used). QB_ATTN_CLUSTER=0 disables clusters.
+int decode_cluster_size(int hkv, int rows) {
+  static int cached_hkv = -1, cached_rows = -1, cached = 0;
+  if (hkv == cached_hkv && rows == cached_rows) return cached;
+  cached_hkv = hkv;
+  cached_rows = rows;
+  cached = 0;
+  const char* e = std::getenv("QB_ATTN_CLUSTER");
+  if (e && e[0] == '0') return 0;
+  const size_t smem = attn_smem_bytes(1);
+  if (cudaFuncSetAttribute(attn_decode_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+      cudaSuccess)
+    return 0;
+  cudaFuncSetAttribute(attn_decode_cluster_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  const int sizes[2] = {16, 8};
+  for (int cs : sizes) {
+    if ((size_t)cs * rows * (kAttnD + 1) * 4 > (size_t)kAttnStages * kAttnStageBytes) continue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(hkv * cs);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, attn_decode_cluster_kernel, &cfg) == cudaSuccess && n >= hkv) {
+      cached = cs;
+      break;
+    }
+    cudaGetLastError();
+  }
+  return cached;
+}
+
+cudaError_t launch_attn_cluster(const CUtensorMap& tk, const CUtensorMap& tv, AttnArgs a, int cs, cudaStream_t st) {
+  a.splits = cs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.Hkv * cs);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.dynamicSmemBytes = attn_smem_bytes(1);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, attn_decode_cluster_kernel, tk, tv, a);
+}
+
 cudaError_t launch_attn(const CUtensorMap& tk, const CUtensorMap& tv, const AttnArgs& a, bool pro, cudaStream_t st) {
+  if (pro && a.Q == 1) {
+    const int cs = decode_cluster_size(a.Hkv, a.Hq / a.Hkv);
+    if (cs > 0) return launch_attn_cluster(tk, tv, a, cs, st);
+  }
   const int rows = (a.Hq / a.Hkv) * a.Q;
   if (pro) return launch_attn_t<1, true>(tk, tv, a, st);
   if (rows <= 16) return launch_attn_t<1, false>(tk, tv, a, st);
