@@ -37,6 +37,8 @@ SIGNATURES = {
     "qb_last_error": (ctypes.c_char_p, [c_void_p]),
     "qb_create": (c_int, [ctypes.POINTER(QbConfig), c_int, c_int, c_int, ctypes.POINTER(c_void_p)]),
     "qb_destroy": (c_int, [c_void_p]),
+    "qb_nccl_unique_id": (c_int, [c_void_p, c_size_t]),
+    "qb_tp_init": (c_int, [c_void_p, c_void_p]),
     "qb_bind_weights": (c_int, [c_void_p, ctypes.POINTER(QbLayerWeights), c_int, c_void_p, c_void_p, c_void_p]),
     "qb_workspace_bytes": (c_int, [c_void_p, ctypes.POINTER(c_size_t)]),
     "qb_bind_state": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_size_t]),

@@ -41,11 +41,21 @@ def up_to_date() -> bool:
     return all(os.path.getmtime(f) <= t for f in _sources())
 
 
+def nccl_dirs():
+    """Headers and library of the NCCL that PyTorch loads (one libnccl.so.2 per process)."""
+    import nvidia.nccl
+
+    root = list(nvidia.nccl.__path__)[0]
+    return os.path.join(root, "include"), os.path.join(root, "lib")
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
     if not force and up_to_date():
         return LIB
+    nccl_inc, nccl_lib = nccl_dirs()
     cmd = [nvcc_path(), "-O3", "-std=c++17", *ARCH, "-lineinfo", "-Xcompiler", "-fPIC", "-shared",
-           "-I", INCLUDE, "-o", LIB + ".tmp", os.path.join(CSRC, "qb.cu")]
+           "-I", INCLUDE, "-I", nccl_inc, "-o", LIB + ".tmp", os.path.join(CSRC, "qb.cu"),
+           "-L", nccl_lib, "-l:libnccl.so.2", "-Xlinker", "-rpath=" + nccl_lib]
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
     res = subprocess.run(cmd, capture_output=True, text=True)

@@ -33,7 +33,7 @@ constexpr int kGemvThreads = kGemvConsumers + 32;
 __host__ __device__ inline int gemv_stage_bytes(int kc) { return kGemvConsumerWarps * kc * 2; }
 constexpr int kGemvBarrierId = 1;  // named barrier of the consumer threads
 
-enum GemvEpilogue : int { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
+enum GemvEpilogue : int { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3, EPI_PARTIAL = 4 };
 
 struct GemvArgs {
   const bf16* w;        // [rows][K]
@@ -44,10 +44,16 @@ struct GemvArgs {
   const int64_t* token; // device token id for the gather
   int vocab;            // rows of embed (bounds check)
   bf16* x_copy;         // gather: CTA 0 stores the gathered row here (residual stream)
+  const float* x32;     // tensor parallel: all-reduced fp32 projection sums; the input row is
+                        // then bf16(bf16(x32) + x_res) and CTA 0 stores it to x_copy
+  const bf16* x_res;    // residual added to x32
   const bf16* gain;     // [K] RMSNorm gain, or NULL (no norm)
   float eps;
   const bf16* residual; // EPI_RESIDUAL
   bf16* out;            // EPI_STORE/RESIDUAL: [rows]; SWIGLU: [rows/2]
+  float* out32;         // EPI_PARTIAL: [rows] fp32 sums (not rounded; reduced across ranks next)
+  int row_base;         // EPI_ARGMAX: global index of weight row 0 (vocabulary shard offset)
+  float* pair_out;      // EPI_ARGMAX under tensor parallelism: {max, index bits} instead of a token
   bf16* logits;         // EPI_ARGMAX: optional [rows]
   float* part_val;      // EPI_ARGMAX: [gridDim] partial maxima
   int* part_idx;        // EPI_ARGMAX: [gridDim] partial argmax
@@ -191,7 +197,20 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
   }
   float ss = 0.f;
   for (int i = ctid * 8; i < K; i += kGemvConsumers * 8) {
-    const uint4 v = ldg128_nc(xsrc + i);
+    uint4 v;
+    if (a.x32 != nullptr) {
+      // Residual add after the cross-rank reduction: the projection is
+      // rounded to bf16 once, then added to the residual and rounded again.
+      const float4 p0 = __ldcg(reinterpret_cast<const float4*>(a.x32 + i));
+      const float4 p1 = __ldcg(reinterpret_cast<const float4*>(a.x32 + i + 4));
+      const uint4 rv = *reinterpret_cast<const uint4*>(a.x_res + i);
+      v.x = pack_bf16(round_bf16(p0.x) + bf_lo(rv.x), round_bf16(p0.y) + bf_hi(rv.x));
+      v.y = pack_bf16(round_bf16(p0.z) + bf_lo(rv.y), round_bf16(p0.w) + bf_hi(rv.y));
+      v.z = pack_bf16(round_bf16(p1.x) + bf_lo(rv.z), round_bf16(p1.y) + bf_hi(rv.z));
+      v.w = pack_bf16(round_bf16(p1.z) + bf_lo(rv.w), round_bf16(p1.w) + bf_hi(rv.w));
+    } else {
+      v = ldg128_nc(xsrc + i);
+    }
     if (a.x_copy != nullptr && b == 0) *reinterpret_cast<uint4*>(a.x_copy + i) = v;
     *reinterpret_cast<uint4*>(xs + i) = v;
     ss = fmaf(bf_lo(v.x), bf_lo(v.x), ss);
@@ -281,6 +300,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
   // 3. Epilogue.
   if constexpr (EPI == EPI_STORE) {
     for (int r = ctid; r < nrows; r += kGemvConsumers) a.out[r0 + r] = __float2bfloat16_rn(rowsum[r]);
+  } else if constexpr (EPI == EPI_PARTIAL) {
+    for (int r = ctid; r < nrows; r += kGemvConsumers) a.out32[r0 + r] = rowsum[r];
   } else if constexpr (EPI == EPI_RESIDUAL) {
     for (int r = ctid; r < nrows; r += kGemvConsumers) {
       const float p = round_bf16(rowsum[r]);
@@ -300,7 +321,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
       const bf16 lb = __float2bfloat16_rn(rowsum[r]);
       if (a.logits != nullptr) a.logits[r0 + r] = lb;
       const float v = __bfloat162float(lb);
-      if (v > best) { best = v; best_i = r0 + r; }  // rows ascend: first max kept
+      if (v > best) { best = v; best_i = a.row_base + r0 + r; }  // rows ascend: first max kept
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -347,8 +368,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
           const int oi = misci[80 + w];
           if (ov > best || (ov == best && oi < best_i)) { best = ov; best_i = oi; }
         }
-        *a.token_out = (best_i == 0x7fffffff) ? 0 : (int64_t)best_i;
-        if (a.pos_inc != nullptr) *a.pos_inc += 1;
+        if (a.pair_out != nullptr) {
+          a.pair_out[0] = best;
+          a.pair_out[1] = __int_as_float(best_i);
+        } else {
+          *a.token_out = (best_i == 0x7fffffff) ? 0 : (int64_t)best_i;
+          if (a.pos_inc != nullptr) *a.pos_inc += 1;
+        }
         *a.counter = 0u;
       }
     }
@@ -361,4 +387,23 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
   }
 }
 
+}  // namespace qb
+
+namespace qb {
+// Tensor-parallel greedy pick: pairs[n] = {max logit, global index bits} from
+// every rank's vocabulary shard; the largest value wins, the lowest index on
+// ties (the single-device rule). Writes the token and advances the position.
+__global__ void tp_pick_kernel(const float* pairs, int n, int64_t* token_out, int64_t* pos_inc) {
+  pdl_wait();
+  if (threadIdx.x != 0) return;
+  float best = -INFINITY;
+  int best_i = 0x7fffffff;
+  for (int r = 0; r < n; ++r) {
+    const float v = pairs[2 * r];
+    const int i = __float_as_int(pairs[2 * r + 1]);
+    if (v > best || (v == best && i < best_i)) { best = v; best_i = i; }
+  }
+  if (token_out != nullptr) *token_out = (best_i == 0x7fffffff) ? 0 : (int64_t)best_i;
+  if (pos_inc != nullptr) *pos_inc += 1;
+}
 }  // namespace qb

@@ -12,6 +12,8 @@
 // its predecessor drains.
 #include "../../include/qb.h"
 
+#include <nccl.h>
+
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -299,9 +301,13 @@ bool ptr_ok(const void* p) { return p != nullptr && (reinterpret_cast<uintptr_t>
 
 // =================================================================== context
 struct qb_ctx {
-  qb_config cfg;
+  qb_config cfg;  // the whole model
+  qb_config lc;   // this rank's shard: Hq/n, Hkv/n, F/n, V/n (equal to cfg without tensor parallelism)
   int device = 0;
   int tp_rank = 0, tp_size = 1;
+  ncclComm_t comm = nullptr;
+  float* y32 = nullptr;    // [H] fp32 partial sums, all-reduced across ranks
+  float* pairs = nullptr;  // [2] this rank's {max, index}; then [2 * tp_size] gathered
   int sm_count = 148;
   std::vector<qb_layer_weights> layers;
   const bf16* embed = nullptr;
@@ -333,11 +339,11 @@ struct qb_ctx {
 namespace {
 
 struct WsLayout {
-  size_t err, counters, head_val, head_idx, xa, xb, qkv, attn, act, part_lse, part_o, total;
+  size_t err, counters, head_val, head_idx, xa, xb, qkv, attn, act, part_lse, part_o, y32, pairs, total;
 };
 
 WsLayout ws_layout(const qb_ctx* c) {
-  const qb_config& g = c->cfg;
+  const qb_config& g = c->lc;
   WsLayout L;
   size_t o = 0;
   L.err = o; o += 256;
@@ -352,6 +358,8 @@ WsLayout ws_layout(const qb_ctx* c) {
   const size_t parts = (size_t)g.n_kv_heads * c->splits * 32;
   L.part_lse = o; o = align_up(o + parts * 4, 256);
   L.part_o = o; o = align_up(o + parts * kAttnD * 4, 256);
+  L.y32 = o; o = align_up(o + (size_t)g.hidden * 4, 256);
+  L.pairs = o; o = align_up(o + (size_t)(2 + 2 * c->tp_size) * 4, 256);
   L.total = o;
   return L;
 }
@@ -374,22 +382,35 @@ int validate_config(const qb_config* g, std::string* msg) {
 // One decode row through every layer. tok_in: device id; pos: device position
 // (read, then incremented by the last kernel). head=false skips the LM head
 // and lets the last down-projection increment the position (prefill rows).
+// Under tensor parallelism (tp_size > 1) the o-proj and down GEMVs write fp32
+// partial sums, one NCCL all-reduce per sublayer combines them, and the next
+// GEMV's prologue rounds the sum, adds the residual and stores the new
+// residual stream; the LM head picks the greedy token across vocabulary
+// shards with an 8-byte all-gather.
 int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t* pos, void* logits, bool head,
                     cudaStream_t st) {
-  const qb_config& g = c->cfg;
+  const qb_config& g = c->lc;
   const int H = g.hidden, D = g.head_dim;
   const int nqkv = (g.n_heads + 2 * g.n_kv_heads) * D;
+  const bool tp = c->tp_size > 1;
   cudaError_t e;
+  ncclResult_t nr;
   for (int l = 0; l < g.n_layers; ++l) {
     const qb_layer_weights& w = c->layers[l];
-    // 1. RMSNorm + QKV (layer 0 gathers the embedding row into xa)
+    // 1. RMSNorm + QKV (layer 0 gathers the embedding row into xa; under TP
+    //    later layers finish the previous down's reduction: xa = xb + sum)
     GemvArgs a = gemv_args(w.qkv, H, nqkv, l == 0 ? nullptr : c->xa, c->qkv, c->err);
     a.gain = static_cast<const bf16*>(w.input_norm);
     a.eps = g.rms_eps;
     if (l == 0) {
       a.embed = c->embed;
       a.token = tok_in;
-      a.vocab = g.vocab;
+      a.vocab = c->cfg.vocab;
+      a.x_copy = c->xa;
+    } else if (tp) {
+      a.x = nullptr;
+      a.x32 = c->y32;
+      a.x_res = c->xb;
       a.x_copy = c->xa;
     }
     if ((e = launch_gemv<EPI_STORE>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "qkv launch");
@@ -418,22 +439,70 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
     at.splits = c->splits;
     if ((e = launch_attn(c->tmk[l], c->tmv[l], at, true, st)) != cudaSuccess)
       return cuda_fail(&c->msg, e, "attention launch");
-    // 3. o-proj + residual: xb = xa + O . attn
-    a = gemv_args(w.o, g.n_heads * D, H, c->attn, c->xb, c->err);
-    a.residual = c->xa;
-    if ((e = launch_gemv<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "o launch");
+    // 3. o-proj (+ residual): xb = xa + O . attn
+    if (tp) {
+      a = gemv_args(w.o, g.n_heads * D, H, c->attn, nullptr, c->err);
+      a.out32 = c->y32;
+      if ((e = launch_gemv<EPI_PARTIAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "o launch");
+      if ((nr = ncclAllReduce(c->y32, c->y32, H, ncclFloat32, ncclSum, c->comm, st)) != ncclSuccess)
+        return set_err(&c->msg, QB_ERR_CUDA, std::string("ncclAllReduce: ") + ncclGetErrorString(nr));
+    } else {
+      a = gemv_args(w.o, g.n_heads * D, H, c->attn, c->xb, c->err);
+      a.residual = c->xa;
+      if ((e = launch_gemv<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "o launch");
+    }
     // 4. RMSNorm + gate/up + SwiGLU
     a = gemv_args(w.gate_up, H, 2 * g.ffn, c->xb, c->act, c->err);
     a.gain = static_cast<const bf16*>(w.post_norm);
     a.eps = g.rms_eps;
+    if (tp) {
+      a.x = nullptr;
+      a.x32 = c->y32;
+      a.x_res = c->xa;
+      a.x_copy = c->xb;
+    }
     if ((e = launch_gemv<EPI_SWIGLU>(a, c->sm_count, st)) != cudaSuccess)
       return cuda_fail(&c->msg, e, "gate/up launch");
-    // 5. down + residual: xa = xb + Down . act
-    a = gemv_args(w.down, g.ffn, H, c->act, c->xa, c->err);
-    a.residual = c->xb;
-    if (!head && l == g.n_layers - 1) a.pos_inc = pos;
-    if ((e = launch_gemv<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess)
-      return cuda_fail(&c->msg, e, "down launch");
+    // 5. down (+ residual): xa = xb + Down . act
+    if (tp) {
+      a = gemv_args(w.down, g.ffn, H, c->act, nullptr, c->err);
+      a.out32 = c->y32;
+      if ((e = launch_gemv<EPI_PARTIAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "down launch");
+      if ((nr = ncclAllReduce(c->y32, c->y32, H, ncclFloat32, ncclSum, c->comm, st)) != ncclSuccess)
+        return set_err(&c->msg, QB_ERR_CUDA, std::string("ncclAllReduce: ") + ncclGetErrorString(nr));
+    } else {
+      a = gemv_args(w.down, g.ffn, H, c->act, c->xa, c->err);
+      a.residual = c->xb;
+      if (!head && l == g.n_layers - 1) a.pos_inc = pos;
+      if ((e = launch_gemv<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess)
+        return cuda_fail(&c->msg, e, "down launch");
+    }
+  }
+  if (tp) {
+    if (head) {
+      GemvArgs a = gemv_args(c->lm_head, H, g.vocab, nullptr, nullptr, c->err);
+      a.x32 = c->y32;
+      a.x_res = c->xb;
+      a.x_copy = c->xa;
+      a.gain = c->final_norm;
+      a.eps = g.rms_eps;
+      a.logits = static_cast<bf16*>(logits);
+      a.part_val = c->head_val;
+      a.part_idx = c->head_idx;
+      a.counter = c->counters + 64;
+      a.row_base = c->tp_rank * g.vocab;
+      a.pair_out = c->pairs;
+      if ((e = launch_gemv<EPI_ARGMAX>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "head launch");
+      if ((nr = ncclAllGather(c->pairs, c->pairs + 2, 2, ncclFloat32, c->comm, st)) != ncclSuccess)
+        return set_err(&c->msg, QB_ERR_CUDA, std::string("ncclAllGather: ") + ncclGetErrorString(nr));
+      tp_pick_kernel<<<1, 32, 0, st>>>(c->pairs + 2, c->tp_size, tok_out, pos);
+    } else {
+      tp_pick_kernel<<<1, 32, 0, st>>>(nullptr, 0, nullptr, pos);  // prefill row: only advance the position
+    }
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(&c->msg, e, "pick launch");
+    // The next step's layer 0 reads xa from the embedding; the final residual
+    // is only needed by the head, which stored it.
+    return QB_OK;
   }
   if (head) {
     GemvArgs a = gemv_args(c->lm_head, H, g.vocab, c->xa, nullptr, c->err);
@@ -454,6 +523,7 @@ int require_ready(qb_ctx* c) {
   if (!c) return set_err(nullptr, QB_ERR_ARG, "ctx is NULL");
   if (!c->weights_bound) return set_err(&c->msg, QB_ERR_STATE, "weights not bound");
   if (!c->state_bound) return set_err(&c->msg, QB_ERR_STATE, "state not bound");
+  if (c->tp_size > 1 && !c->comm) return set_err(&c->msg, QB_ERR_STATE, "tensor-parallel context without qb_tp_init");
   return QB_OK;
 }
 
@@ -475,17 +545,28 @@ int qb_create(const qb_config* cfg, int device, int tp_rank, int tp_size, qb_ctx
   std::string msg;
   int rc = validate_config(cfg, &msg);
   if (rc) return rc;
-  if (tp_size != 1 || tp_rank != 0)
-    return set_err(nullptr, QB_ERR_UNSUPPORTED, "tensor-parallel contexts are created by qb_create_tp");
+  if (tp_size < 1 || tp_rank < 0 || tp_rank >= tp_size)
+    return set_err(nullptr, QB_ERR_ARG, "tp_rank must lie in [0, tp_size)");
+  // Shard: KV heads (with their query heads), FFN columns and vocabulary rows.
+  qb_config lc = *cfg;
+  if (cfg->n_kv_heads % tp_size || cfg->ffn % tp_size || cfg->vocab % tp_size)
+    return set_err(nullptr, QB_ERR_UNSUPPORTED, "n_kv_heads, ffn and vocab must divide by tp_size");
+  lc.n_heads = cfg->n_heads / tp_size;
+  lc.n_kv_heads = cfg->n_kv_heads / tp_size;
+  lc.ffn = cfg->ffn / tp_size;
+  lc.vocab = cfg->vocab / tp_size;
+  if ((lc.n_heads * lc.head_dim) % 256 || lc.ffn % 256)
+    return set_err(nullptr, QB_ERR_UNSUPPORTED, "per-rank Hq*D and ffn must be multiples of 256");
   cudaError_t e = cudaSetDevice(device);
   if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaSetDevice");
   qb_ctx* c = new qb_ctx();
   c->cfg = *cfg;
+  c->lc = lc;
   c->device = device;
   c->tp_rank = tp_rank;
   c->tp_size = tp_size;
   c->sm_count = sm_count_of(device);
-  c->splits = attn_splits_for(cfg->n_kv_heads, c->sm_count);
+  c->splits = attn_splits_for(lc.n_kv_heads, c->sm_count);
   *out = c;
   return QB_OK;
 }
@@ -494,6 +575,7 @@ int qb_destroy(qb_ctx* c) {
   if (!c) return QB_OK;
   if (c->exec) cudaGraphExecDestroy(c->exec);
   if (c->graph) cudaGraphDestroy(c->graph);
+  if (c->comm) ncclCommDestroy(c->comm);
   delete c;
   return QB_OK;
 }
@@ -552,8 +634,10 @@ int qb_bind_state(qb_ctx* c, void* k_cache, void* v_cache, int capacity, const v
   c->act = reinterpret_cast<bf16*>(c->ws + L.act);
   c->part_lse = reinterpret_cast<float*>(c->ws + L.part_lse);
   c->part_o = reinterpret_cast<float*>(c->ws + L.part_o);
+  c->y32 = reinterpret_cast<float*>(c->ws + L.y32);
+  c->pairs = reinterpret_cast<float*>(c->ws + L.pairs);
   if ((e = cudaMemset(workspace, 0, L.total)) != cudaSuccess) return cuda_fail(&c->msg, e, "workspace memset");
-  const qb_config& g = c->cfg;
+  const qb_config& g = c->lc;
   c->tmk.assign(g.n_layers, CUtensorMap());
   c->tmv.assign(g.n_layers, CUtensorMap());
   for (int l = 0; l < g.n_layers; ++l) {
@@ -571,6 +655,31 @@ int qb_bind_state(qb_ctx* c, void* k_cache, void* v_cache, int capacity, const v
     c->graph = nullptr;
   }
   c->state_bound = true;
+  return QB_OK;
+}
+
+int qb_nccl_unique_id(void* out, size_t bytes) {
+  if (!out || bytes < sizeof(ncclUniqueId)) return set_err(nullptr, QB_ERR_ARG, "unique id buffer smaller than 128 bytes");
+  ncclUniqueId id;
+  ncclResult_t r = ncclGetUniqueId(&id);
+  if (r != ncclSuccess) return set_err(nullptr, QB_ERR_CUDA, std::string("ncclGetUniqueId: ") + ncclGetErrorString(r));
+  std::memcpy(out, &id, sizeof(id));
+  return QB_OK;
+}
+
+int qb_tp_init(qb_ctx* c, const void* unique_id) {
+  if (!c || !unique_id) return set_err(nullptr, QB_ERR_ARG, "NULL argument");
+  if (c->tp_size == 1) return QB_OK;
+  if (c->comm) return set_err(&c->msg, QB_ERR_STATE, "communicator already initialised");
+  cudaError_t e = cudaSetDevice(c->device);
+  if (e != cudaSuccess) return cuda_fail(&c->msg, e, "cudaSetDevice");
+  ncclUniqueId id;
+  std::memcpy(&id, unique_id, sizeof(id));
+  ncclResult_t r = ncclCommInitRank(&c->comm, c->tp_size, id, c->tp_rank);
+  if (r != ncclSuccess) {
+    c->comm = nullptr;
+    return set_err(&c->msg, QB_ERR_CUDA, std::string("ncclCommInitRank: ") + ncclGetErrorString(r));
+  }
   return QB_OK;
 }
 

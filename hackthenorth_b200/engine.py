@@ -56,7 +56,7 @@ class DecodeState:
         self.engine = engine
         self.shape = (1, prompt_length, output_length)
         self.capacity = capacity or (prompt_length + max(output_length, 1) - 1 + draft_tokens)
-        shape = (cfg.n_layers, cfg.n_kv_heads, self.capacity, cfg.head_dim)
+        shape = (cfg.n_layers, cfg.n_kv_heads // engine.tp_size, self.capacity, cfg.head_dim)
         self.keys = torch.zeros(shape, dtype=BF16, device=dev)
         self.values = torch.zeros(shape, dtype=BF16, device=dev)
         cos, sin = rotary_table(cfg, self.capacity)
@@ -131,7 +131,11 @@ class Engine:
     engine layout; ``generate`` streams greedy tokens."""
 
     def __init__(self, model_path: Optional[str] = None, device: str = "cuda:0", *,
-                 cfg: Optional[ModelConfig] = None, state: Optional[Dict[str, torch.Tensor]] = None):
+                 cfg: Optional[ModelConfig] = None, state: Optional[Dict[str, torch.Tensor]] = None,
+                 tp_rank: int = 0, tp_size: int = 1, unique_id: Optional[bytes] = None):
+        """``tp_rank``/``tp_size``: tensor-parallel slot (one process per GPU);
+        every rank of the group passes the same ``unique_id`` (from
+        ``hackthenorth_b200.tp.unique_id`` on rank 0, shared by the caller)."""
         if not torch.cuda.is_available():
             raise RuntimeError("Engine needs a CUDA device; there is no CPU fallback")
         self.device = torch.device(device)
@@ -141,13 +145,20 @@ class Engine:
         if cfg is None or state is None:
             raise ValueError("Engine needs a model_path or (cfg, state)")
         self.cfg = cfg
-        self.weights = PackedWeights(cfg, state, self.device)
+        self.tp_rank, self.tp_size = tp_rank, tp_size
+        self.weights = PackedWeights(cfg, state, self.device, tp_rank, tp_size)
         L = _lib.load()
         qc = _lib.QbConfig(cfg.hidden, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn, cfg.n_layers,
                            cfg.vocab, cfg.rms_eps)
         ctx = _lib.c_void_p()
-        _lib.check(L.qb_create(_lib.ctypes.byref(qc), self.device.index or 0, 0, 1, _lib.ctypes.byref(ctx)))
+        _lib.check(L.qb_create(_lib.ctypes.byref(qc), self.device.index or 0, tp_rank, tp_size,
+                               _lib.ctypes.byref(ctx)))
         self.ctx = ctx
+        if tp_size > 1:
+            if unique_id is None:
+                raise ValueError("tensor parallelism needs the group's NCCL unique id")
+            buf = _lib.ctypes.create_string_buffer(bytes(unique_id), len(unique_id))
+            _lib.check(L.qb_tp_init(ctx, buf), ctx)
         table = (_lib.QbLayerWeights * cfg.n_layers)()
         for i, lw in enumerate(self.weights.layers):
             table[i] = _lib.QbLayerWeights(lw["input_norm"].data_ptr(), lw["qkv"].data_ptr(),
@@ -160,10 +171,12 @@ class Engine:
         self._bound_state = None
 
     @classmethod
-    def from_random(cls, cfg: ModelConfig, seed: int = 0, device: str = "cuda:0", init_device: str = "cpu"):
-        """Seeded random-init weights (see ``weights.random_state_dict``)."""
+    def from_random(cls, cfg: ModelConfig, seed: int = 0, device: str = "cuda:0", init_device: str = "cpu",
+                    tp_rank: int = 0, tp_size: int = 1, unique_id: Optional[bytes] = None):
+        """Seeded random-init weights (see ``weights.random_state_dict``); every
+        tensor-parallel rank draws the same full set and keeps its shard."""
         state = random_state_dict(cfg, seed, device=init_device)
-        return cls(None, device, cfg=cfg, state=state)
+        return cls(None, device, cfg=cfg, state=state, tp_rank=tp_rank, tp_size=tp_size, unique_id=unique_id)
 
     def __del__(self):
         ctx = getattr(self, "ctx", None)

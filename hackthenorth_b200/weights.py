@@ -100,33 +100,56 @@ def load_checkpoint(path: str, device="cpu") -> Tuple[ModelConfig, Dict[str, tor
 
 
 class PackedWeights:
-    """Device-resident weights in the engine's layout (see module docstring)."""
+    """Device-resident weights in the engine's layout (see module docstring).
 
-    def __init__(self, cfg: ModelConfig, state: Dict[str, torch.Tensor], device="cuda:0"):
+    With ``tp_size > 1`` only rank ``tp_rank``'s shard is kept (Megatron-style):
+    KV heads [r*Hkv/n, (r+1)*Hkv/n) with their query heads (q/k/v rows of qkv,
+    the matching input columns of o), FFN columns [r*F/n, (r+1)*F/n) (gate/up
+    rows, down input columns) and vocabulary rows [r*V/n, (r+1)*V/n) of the
+    head; the embedding and the norm gains stay whole.
+    """
+
+    def __init__(self, cfg: ModelConfig, state: Dict[str, torch.Tensor], device="cuda:0",
+                 tp_rank: int = 0, tp_size: int = 1):
         self.cfg = cfg
+        self.tp_rank, self.tp_size = tp_rank, tp_size
         dev = torch.device(device)
+        n, r = tp_size, tp_rank
+        D = cfg.head_dim
+        if cfg.n_kv_heads % n or cfg.ffn % n or cfg.vocab % n:
+            raise ValueError("n_kv_heads, ffn and vocab must divide by tp_size")
+        hq, hkv, f, v = cfg.n_heads // n, cfg.n_kv_heads // n, cfg.ffn // n, cfg.vocab // n
+        qs, ks, fs = slice(r * hq * D, (r + 1) * hq * D), slice(r * hkv * D, (r + 1) * hkv * D), slice(r * f, (r + 1) * f)
 
         def get(name):
             return state[name].to(device=dev, dtype=torch.bfloat16).contiguous()
 
+        def dev_bf16(t):
+            return t.to(device=dev, dtype=torch.bfloat16).contiguous()
+
         self.embed = get("model.embed_tokens.weight")
         self.final_norm = get("model.norm.weight")
         head = state.get("lm_head.weight")
-        self.lm_head = self.embed if (cfg.tied or head is None) else get("lm_head.weight")
+        full_head = state["model.embed_tokens.weight"] if (cfg.tied or head is None) else head
+        if n == 1:
+            self.lm_head = self.embed if (cfg.tied or head is None) else get("lm_head.weight")
+        else:
+            self.lm_head = dev_bf16(full_head[r * v:(r + 1) * v])
         self.layers = []
         for i in range(cfg.n_layers):
             p = f"model.layers.{i}."
-            q, k, v = (state[p + f"self_attn.{n}_proj.weight"] for n in "qkv")
+            q, k, vv = (state[p + f"self_attn.{nm}_proj.weight"] for nm in "qkv")
             gate, up = state[p + "mlp.gate_proj.weight"], state[p + "mlp.up_proj.weight"]
+            o, down = state[p + "self_attn.o_proj.weight"], state[p + "mlp.down_proj.weight"]
             self.layers.append({
                 "input_norm": get(p + "input_layernorm.weight"),
-                "qkv": torch.cat((q, k, v)).to(dev, torch.bfloat16).contiguous(),
+                "qkv": dev_bf16(torch.cat((q[qs], k[ks], vv[ks]))),
                 "q_norm": get(p + "self_attn.q_norm.weight"),
                 "k_norm": get(p + "self_attn.k_norm.weight"),
-                "o": get(p + "self_attn.o_proj.weight"),
+                "o": dev_bf16(o[:, qs]) if n > 1 else get(p + "self_attn.o_proj.weight"),
                 "post_norm": get(p + "post_attention_layernorm.weight"),
-                "gu": interleave_gate_up(gate, up).to(dev, torch.bfloat16).contiguous(),
-                "down": get(p + "mlp.down_proj.weight"),
+                "gu": dev_bf16(interleave_gate_up(gate[fs], up[fs])),
+                "down": dev_bf16(down[:, fs]) if n > 1 else get(p + "mlp.down_proj.weight"),
             })
 
     def nbytes(self) -> int:

@@ -68,12 +68,30 @@ const char* qb_last_error(const qb_ctx* ctx);
 /* ---- engine lifecycle ---------------------------------------------------- */
 
 /* Replaces Engine.__init__'s model preparation (dryft/engine/engine.py:176-200).
- * tp_rank/tp_size: tensor-parallel slot; 0/1 for a single GPU. */
+ * cfg describes the whole model. tp_rank/tp_size: tensor-parallel slot (0/1
+ * for one GPU). With tp_size > 1 this rank owns KV heads
+ * [r*Hkv/n, (r+1)*Hkv/n) with their query heads, FFN columns [r*F/n, (r+1)*F/n)
+ * and vocabulary rows [r*V/n, (r+1)*V/n); the weights bound later are that
+ * shard (see qb_bind_weights) and qb_tp_init must be called before a step.
+ * The reference has no multi-GPU path; this follows its single-GPU arithmetic
+ * with fp32 partial sums reduced across ranks before the one bf16 rounding. */
 int qb_create(const qb_config* cfg, int device, int tp_rank, int tp_size, qb_ctx** out);
+
+/* NCCL unique id for a tensor-parallel group (rank 0 creates it and shares the
+ * bytes with the other ranks); `bytes` >= 128. */
+int qb_nccl_unique_id(void* out, size_t bytes);
+
+/* Join the tensor-parallel group: one NCCL communicator per context, used for
+ * an fp32 all-reduce of [H] after every o-proj and down projection and an
+ * 8-byte all-gather of each rank's greedy candidate. No-op when tp_size == 1. */
+int qb_tp_init(qb_ctx* ctx, const void* unique_id);
 int qb_destroy(qb_ctx* ctx);
 
 /* Borrow device weights (no copy). lm_head may equal embed (tied).
- * Replaces the module surgery of dryft/engine/engine.py:190-199. */
+ * Replaces the module surgery of dryft/engine/engine.py:190-199.
+ * Under tensor parallelism each table holds this rank's shard: qkv rows of its
+ * q heads, k heads and v heads; o [H, Hq*D/n] (its input columns); gate_up
+ * [2F/n, H]; down [H, F/n]; lm_head [V/n, H]; embed and norms whole. */
 int qb_bind_weights(qb_ctx* ctx, const qb_layer_weights* layers, int n_layers,
                     const void* embed, const void* final_norm, const void* lm_head);
 
@@ -81,7 +99,7 @@ int qb_bind_weights(qb_ctx* ctx, const qb_layer_weights* layers, int n_layers,
  * counters, error word). */
 int qb_workspace_bytes(const qb_ctx* ctx, size_t* bytes);
 
-/* Borrow the decode state: K and V caches [L, Hkv, capacity, D] (bf16,
+/* Borrow the decode state: K and V caches [L, Hkv/n, capacity, D] (bf16,
  * zero-filled by the caller, as KVCache does: dryft/engine/decode.py:25-46),
  * the RoPE tables [capacity, D] (bf16 cos and sin rows for positions
  * 0..capacity-1: dryft/engine/decode.py:49-67), and the workspace. The
