@@ -19,6 +19,7 @@ enum DeviceError : int {
   DEV_TIMEOUT_GEMV_EMPTY = 0x102,
   DEV_TIMEOUT_ATTN_FULL = 0x201,
   DEV_TIMEOUT_ATTN_EMPTY = 0x202,
+  DEV_TIMEOUT_PEER_FLAG = 0x401,
   DEV_BAD_TOKEN = 0x301,
   DEV_BAD_POSITION = 0x302,
 };
@@ -166,6 +167,55 @@ __device__ __forceinline__ unsigned atomic_add_acq_rel_gpu(unsigned* p, unsigned
   unsigned old;
   asm volatile("atom.add.acq_rel.gpu.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
   return old;
+}
+// System-scope flag handshake for peer-to-peer reductions over NVLink.
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// Bounded wait for a 64-bit word whose high half equals `token`; returns its
+// low half (fp32 bits). One aligned 64-bit store carries both halves, so a
+// matching token means the value beside it is the one that was sent.
+__device__ __forceinline__ float wait_tagged(const unsigned long long* p, uint32_t token, int* err, int code) {
+  unsigned long long w = ld_relaxed_sys_u64(p);
+  if ((uint32_t)(w >> 32) == token) return __uint_as_float((uint32_t)w);
+  const unsigned long long t0 = global_timer_ns();
+  while (true) {
+    for (int i = 0; i < 32; ++i) {
+      w = ld_relaxed_sys_u64(p);
+      if ((uint32_t)(w >> 32) == token) return __uint_as_float((uint32_t)w);
+    }
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      report_error(err, code);
+      return 0.f;
+    }
+  }
+}
+// Bounded wait until *p >= v (another GPU's release store); false on timeout.
+__device__ __forceinline__ bool wait_flag_geq(const unsigned long long* p, unsigned long long v, int* err, int code) {
+  if (ld_acquire_sys_u64(p) >= v) return true;
+  const unsigned long long t0 = global_timer_ns();
+  while (true) {
+    for (int i = 0; i < 32; ++i)
+      if (ld_acquire_sys_u64(p) >= v) return true;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      report_error(err, code);
+      return false;
+    }
+  }
 }
 // Coherent (L1-bypassing) load for data written by other CTAs of this grid.
 __device__ __forceinline__ float ldcg_f32(const float* p) { return __ldcg(p); }

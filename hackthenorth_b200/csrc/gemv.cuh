@@ -35,6 +35,28 @@ constexpr int kGemvBarrierId = 1;  // named barrier of the consumer threads
 
 enum GemvEpilogue : int { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3, EPI_PARTIAL = 4 };
 
+constexpr int kMaxTp = 8;
+constexpr int kPeerFlagSlots = 256;  // producer CTAs per (parity, sender)
+
+// Tensor-parallel reduction over NVLink peer memory, fused into the o-proj and
+// down GEMVs (EPI_RESIDUAL with tp.size > 1): each CTA stores its fp32 partial
+// rows into recv[parity][my_rank][row] of every rank as 64-bit words
+// {token, value}, reads back the n words of its own rows (waiting, bounded,
+// until their tokens match: one aligned store carries both halves, so no
+// fences or flags are needed) and sums them in rank order, so every rank gets
+// the same bf16 result. Tokens grow with a per-context epoch (one per decode
+// row), so nothing is ever reset; the two parity halves keep a fast rank's
+// next sublayer from overwriting words a slow rank has not read yet.
+struct TpPeers {
+  unsigned long long* recv[kMaxTp];     // each rank's receive words [2][n][H]
+  const unsigned long long* epoch;      // this rank's decode-row counter
+  int rank, size;
+};
+
+__device__ __forceinline__ uint32_t tp_token(const TpPeers& t, int sub_id) {
+  return (uint32_t)((*t.epoch + 1ull) * 256ull + (unsigned long long)(sub_id + 1));
+}
+
 struct GemvArgs {
   const bf16* w;        // [rows][K]
   int K;                // multiple of 256
@@ -54,6 +76,10 @@ struct GemvArgs {
   float* out32;         // EPI_PARTIAL: [rows] fp32 sums (not rounded; reduced across ranks next)
   int row_base;         // EPI_ARGMAX: global index of weight row 0 (vocabulary shard offset)
   float* pair_out;      // EPI_ARGMAX under tensor parallelism: {max, index bits} instead of a token
+  TpPeers tp;           // EPI_RESIDUAL across ranks (tp.size > 1): peer-memory reduction
+  int tp_sub;           // sublayer id of the reduction (0..255)
+  int tp_parity;        // receive buffer half (0: o-proj, 1: down)
+  int hidden;           // H (length of the reduced vector)
   bf16* logits;         // EPI_ARGMAX: optional [rows]
   float* part_val;      // EPI_ARGMAX: [gridDim] partial maxima
   int* part_idx;        // EPI_ARGMAX: [gridDim] partial argmax
@@ -195,14 +221,15 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
     }
     xsrc = a.embed + (size_t)t * K;
   }
+  const float* x32 = a.x32;
   float ss = 0.f;
   for (int i = ctid * 8; i < K; i += kGemvConsumers * 8) {
     uint4 v;
-    if (a.x32 != nullptr) {
+    if (x32 != nullptr) {
       // Residual add after the cross-rank reduction: the projection is
       // rounded to bf16 once, then added to the residual and rounded again.
-      const float4 p0 = __ldcg(reinterpret_cast<const float4*>(a.x32 + i));
-      const float4 p1 = __ldcg(reinterpret_cast<const float4*>(a.x32 + i + 4));
+      const float4 p0 = __ldcg(reinterpret_cast<const float4*>(x32 + i));
+      const float4 p1 = __ldcg(reinterpret_cast<const float4*>(x32 + i + 4));
       const uint4 rv = *reinterpret_cast<const uint4*>(a.x_res + i);
       v.x = pack_bf16(round_bf16(p0.x) + bf_lo(rv.x), round_bf16(p0.y) + bf_hi(rv.x));
       v.y = pack_bf16(round_bf16(p0.z) + bf_lo(rv.y), round_bf16(p0.w) + bf_hi(rv.y));
@@ -303,9 +330,38 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
   } else if constexpr (EPI == EPI_PARTIAL) {
     for (int r = ctid; r < nrows; r += kGemvConsumers) a.out32[r0 + r] = rowsum[r];
   } else if constexpr (EPI == EPI_RESIDUAL) {
-    for (int r = ctid; r < nrows; r += kGemvConsumers) {
-      const float p = round_bf16(rowsum[r]);
-      a.out[r0 + r] = __float2bfloat16_rn(p + __bfloat162float(a.residual[r0 + r]));
+    if (a.tp.size > 1) {
+      // Tensor parallel: every rank partitions the rows across CTAs the same
+      // way, so CTA b exchanges only its own rows with CTA b of the other ranks.
+      // Send {token, partial} words to every rank, then gather the n partials of
+      // each row (one NVLink round trip), add them in rank order and finish the
+      // row as on one GPU: bf16(bf16(sum) + residual).
+      const size_t slot = (size_t)a.tp_parity * a.tp.size * a.hidden + r0;
+      const uint32_t tok = tp_token(a.tp, a.tp_sub);
+      const unsigned long long tag = (unsigned long long)tok << 32;
+      for (int p = 0; p < a.tp.size; ++p)
+        for (int r = ctid; r < nrows; r += kGemvConsumers)
+          st_relaxed_sys_u64(a.tp.recv[p] + slot + (size_t)a.tp.rank * a.hidden + r, tag | __float_as_uint(rowsum[r]));
+      const unsigned long long* mine = a.tp.recv[a.tp.rank] + slot;
+      for (int r = ctid; r < nrows; r += kGemvConsumers) {
+        unsigned long long w[kMaxTp];
+#pragma unroll
+        for (int p = 0; p < kMaxTp; ++p)
+          if (p < a.tp.size) w[p] = ld_relaxed_sys_u64(mine + (size_t)p * a.hidden + r);
+        float sum = 0.f;
+#pragma unroll
+        for (int p = 0; p < kMaxTp; ++p)
+          if (p < a.tp.size)
+            sum += ((uint32_t)(w[p] >> 32) == tok)
+                       ? __uint_as_float((uint32_t)w[p])
+                       : wait_tagged(mine + (size_t)p * a.hidden + r, tok, a.err, DEV_TIMEOUT_PEER_FLAG);
+        a.out[r0 + r] = __float2bfloat16_rn(round_bf16(sum) + __bfloat162float(a.residual[r0 + r]));
+      }
+    } else {
+      for (int r = ctid; r < nrows; r += kGemvConsumers) {
+        const float p = round_bf16(rowsum[r]);
+        a.out[r0 + r] = __float2bfloat16_rn(p + __bfloat162float(a.residual[r0 + r]));
+      }
     }
   } else if constexpr (EPI == EPI_SWIGLU) {
     for (int j = ctid; j < nrows / 2; j += kGemvConsumers) {
@@ -393,9 +449,20 @@ namespace qb {
 // Tensor-parallel greedy pick: pairs[n] = {max logit, global index bits} from
 // every rank's vocabulary shard; the largest value wins, the lowest index on
 // ties (the single-device rule). Writes the token and advances the position.
-__global__ void tp_pick_kernel(const float* pairs, int n, int64_t* token_out, int64_t* pos_inc) {
+// With wait_words set (prefill rows without the head), first waits until every
+// rank's last down-projection words have arrived, so no rank starts the next
+// row (and overwrites a peer's receive words) before all ranks have read them.
+__global__ void tp_pick_kernel(const float* pairs, int n, int64_t* token_out, int64_t* pos_inc,
+                               unsigned long long* epoch, const unsigned long long* wait_words,
+                               unsigned long long wait_token_base, int wait_count, int* err) {
   pdl_wait();
+  if (wait_words != nullptr) {
+    const uint32_t tok = (uint32_t)((*epoch + 1ull) * 256ull + wait_token_base);
+    for (int i = threadIdx.x; i < wait_count; i += blockDim.x) wait_tagged(wait_words + i, tok, err, DEV_TIMEOUT_PEER_FLAG);
+    __syncthreads();
+  }
   if (threadIdx.x != 0) return;
+  if (epoch != nullptr) *epoch += 1;  // one decode row done on this rank
   float best = -INFINITY;
   int best_i = 0x7fffffff;
   for (int r = 0; r < n; ++r) {

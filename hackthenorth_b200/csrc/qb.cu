@@ -306,6 +306,10 @@ struct qb_ctx {
   int device = 0;
   int tp_rank = 0, tp_size = 1;
   ncclComm_t comm = nullptr;
+  bool p2p = false;                 // peer-memory reduction (else NCCL all-reduce)
+  void* tp_base = nullptr;          // this rank's [tagged receive words | epoch] allocation
+  TpPeers peers = {};               // every rank's receive words (peers IPC-mapped)
+  unsigned long long* tp_epoch() { return const_cast<unsigned long long*>(peers.epoch); }
   float* y32 = nullptr;    // [H] fp32 partial sums, all-reduced across ranks
   float* pairs = nullptr;  // [2] this rank's {max, index}; then [2 * tp_size] gathered
   int sm_count = 148;
@@ -393,8 +397,22 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
   const int H = g.hidden, D = g.head_dim;
   const int nqkv = (g.n_heads + 2 * g.n_kv_heads) * D;
   const bool tp = c->tp_size > 1;
+  const bool p2p = tp && c->p2p;
   cudaError_t e;
   ncclResult_t nr;
+  // NCCL fallback: the next GEMV finishes the all-reduced sum (round + residual).
+  auto peer_reduce = [&](GemvArgs& a, int sub, int parity) {
+    a.tp = c->peers;
+    a.tp_sub = sub;
+    a.tp_parity = parity;
+    a.hidden = H;
+  };
+  auto consume = [&](GemvArgs& a, const bf16* res, bf16* copy) {
+    a.x = nullptr;
+    a.x_res = res;
+    a.x_copy = copy;
+    a.x32 = c->y32;
+  };
   for (int l = 0; l < g.n_layers; ++l) {
     const qb_layer_weights& w = c->layers[l];
     // 1. RMSNorm + QKV (layer 0 gathers the embedding row into xa; under TP
@@ -407,11 +425,8 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
       a.token = tok_in;
       a.vocab = c->cfg.vocab;
       a.x_copy = c->xa;
-    } else if (tp) {
-      a.x = nullptr;
-      a.x32 = c->y32;
-      a.x_res = c->xb;
-      a.x_copy = c->xa;
+    } else if (tp && !p2p) {
+      consume(a, c->xb, c->xa);
     }
     if ((e = launch_gemv<EPI_STORE>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "qkv launch");
     // 2. attention with the norm/rope/append prologue
@@ -440,7 +455,7 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
     if ((e = launch_attn(c->tmk[l], c->tmv[l], at, true, st)) != cudaSuccess)
       return cuda_fail(&c->msg, e, "attention launch");
     // 3. o-proj (+ residual): xb = xa + O . attn
-    if (tp) {
+    if (tp && !p2p) {
       a = gemv_args(w.o, g.n_heads * D, H, c->attn, nullptr, c->err);
       a.out32 = c->y32;
       if ((e = launch_gemv<EPI_PARTIAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "o launch");
@@ -449,22 +464,18 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
     } else {
       a = gemv_args(w.o, g.n_heads * D, H, c->attn, c->xb, c->err);
       a.residual = c->xa;
+      if (p2p) peer_reduce(a, 2 * l, 0);
       if ((e = launch_gemv<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "o launch");
     }
     // 4. RMSNorm + gate/up + SwiGLU
     a = gemv_args(w.gate_up, H, 2 * g.ffn, c->xb, c->act, c->err);
     a.gain = static_cast<const bf16*>(w.post_norm);
     a.eps = g.rms_eps;
-    if (tp) {
-      a.x = nullptr;
-      a.x32 = c->y32;
-      a.x_res = c->xa;
-      a.x_copy = c->xb;
-    }
+    if (tp && !p2p) consume(a, c->xa, c->xb);
     if ((e = launch_gemv<EPI_SWIGLU>(a, c->sm_count, st)) != cudaSuccess)
       return cuda_fail(&c->msg, e, "gate/up launch");
     // 5. down (+ residual): xa = xb + Down . act
-    if (tp) {
+    if (tp && !p2p) {
       a = gemv_args(w.down, g.ffn, H, c->act, nullptr, c->err);
       a.out32 = c->y32;
       if ((e = launch_gemv<EPI_PARTIAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "down launch");
@@ -473,17 +484,16 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
     } else {
       a = gemv_args(w.down, g.ffn, H, c->act, c->xa, c->err);
       a.residual = c->xb;
-      if (!head && l == g.n_layers - 1) a.pos_inc = pos;
+      if (p2p) peer_reduce(a, 2 * l + 1, 1);
+      else if (!head && l == g.n_layers - 1) a.pos_inc = pos;
       if ((e = launch_gemv<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess)
         return cuda_fail(&c->msg, e, "down launch");
     }
   }
   if (tp) {
     if (head) {
-      GemvArgs a = gemv_args(c->lm_head, H, g.vocab, nullptr, nullptr, c->err);
-      a.x32 = c->y32;
-      a.x_res = c->xb;
-      a.x_copy = c->xa;
+      GemvArgs a = gemv_args(c->lm_head, H, g.vocab, c->xa, nullptr, c->err);
+      if (!p2p) consume(a, c->xb, c->xa);
       a.gain = c->final_norm;
       a.eps = g.rms_eps;
       a.logits = static_cast<bf16*>(logits);
@@ -495,9 +505,12 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
       if ((e = launch_gemv<EPI_ARGMAX>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "head launch");
       if ((nr = ncclAllGather(c->pairs, c->pairs + 2, 2, ncclFloat32, c->comm, st)) != ncclSuccess)
         return set_err(&c->msg, QB_ERR_CUDA, std::string("ncclAllGather: ") + ncclGetErrorString(nr));
-      tp_pick_kernel<<<1, 32, 0, st>>>(c->pairs + 2, c->tp_size, tok_out, pos);
+      tp_pick_kernel<<<1, 32, 0, st>>>(c->pairs + 2, c->tp_size, tok_out, pos, p2p ? c->tp_epoch() : nullptr,
+                                       nullptr, 0, 0, c->err);
     } else {
-      tp_pick_kernel<<<1, 32, 0, st>>>(nullptr, 0, nullptr, pos);  // prefill row: only advance the position
+      // prefill row: advance the position (and the peer-reduction epoch)
+      tp_pick_kernel<<<1, 32, 0, st>>>(nullptr, 0, nullptr, pos, p2p ? c->tp_epoch() : nullptr, nullptr, 0, 0,
+                                       c->err);
     }
     if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(&c->msg, e, "pick launch");
     // The next step's layer 0 reads xa from the embedding; the final residual
@@ -575,6 +588,12 @@ int qb_destroy(qb_ctx* c) {
   if (!c) return QB_OK;
   if (c->exec) cudaGraphExecDestroy(c->exec);
   if (c->graph) cudaGraphDestroy(c->graph);
+  if (c->p2p) {
+    cudaSetDevice(c->device);
+    for (int r = 0; r < c->tp_size; ++r)
+      if (r != c->tp_rank && c->peers.recv[r]) cudaIpcCloseMemHandle(c->peers.recv[r]);
+  }
+  if (c->tp_base) cudaFree(c->tp_base);
   if (c->comm) ncclCommDestroy(c->comm);
   delete c;
   return QB_OK;
@@ -680,6 +699,46 @@ int qb_tp_init(qb_ctx* c, const void* unique_id) {
     c->comm = nullptr;
     return set_err(&c->msg, QB_ERR_CUDA, std::string("ncclCommInitRank: ") + ncclGetErrorString(r));
   }
+  if (c->tp_size > kMaxTp) return QB_OK;  // NCCL path only
+  const char* env = std::getenv("QB_TP_NCCL");
+  if (env && env[0] == '1') return QB_OK;
+  // Peer-memory reduction buffers: tagged words [2][n][H] u64 | epoch.
+  const size_t recv_bytes = align_up((size_t)2 * c->tp_size * c->cfg.hidden * 8, 256);
+  const size_t flag_bytes = 0;
+  const size_t total = recv_bytes + flag_bytes + 256;
+  if ((e = cudaMalloc(&c->tp_base, total)) != cudaSuccess) return cuda_fail(&c->msg, e, "peer buffer cudaMalloc");
+  if ((e = cudaMemset(c->tp_base, 0, total)) != cudaSuccess) return cuda_fail(&c->msg, e, "peer buffer memset");
+  cudaIpcMemHandle_t mine;
+  if ((e = cudaIpcGetMemHandle(&mine, c->tp_base)) != cudaSuccess) return cuda_fail(&c->msg, e, "cudaIpcGetMemHandle");
+  void* dev_handles = nullptr;
+  if ((e = cudaMalloc(&dev_handles, sizeof(mine) * (c->tp_size + 1))) != cudaSuccess)
+    return cuda_fail(&c->msg, e, "handle buffer");
+  cudaMemcpy(dev_handles, &mine, sizeof(mine), cudaMemcpyHostToDevice);
+  r = ncclAllGather(dev_handles, static_cast<char*>(dev_handles) + sizeof(mine), sizeof(mine), ncclChar, c->comm,
+                    nullptr);
+  std::vector<cudaIpcMemHandle_t> all(c->tp_size);
+  cudaStreamSynchronize(nullptr);
+  cudaMemcpy(all.data(), static_cast<char*>(dev_handles) + sizeof(mine), sizeof(mine) * c->tp_size,
+             cudaMemcpyDeviceToHost);
+  cudaFree(dev_handles);
+  if (r != ncclSuccess) return set_err(&c->msg, QB_ERR_CUDA, std::string("ncclAllGather: ") + ncclGetErrorString(r));
+  for (int k = 0; k < c->tp_size; ++k) {
+    void* base = c->tp_base;
+    if (k != c->tp_rank) {
+      if ((e = cudaIpcOpenMemHandle(&base, all[k], cudaIpcMemLazyEnablePeerAccess)) != cudaSuccess) {
+        cudaGetLastError();
+        for (int j = 0; j < k; ++j)
+          if (j != c->tp_rank && c->peers.recv[j]) cudaIpcCloseMemHandle(c->peers.recv[j]);
+        std::memset(&c->peers, 0, sizeof(c->peers));
+        return QB_OK;  // no peer mapping: stay on the NCCL all-reduce path
+      }
+    }
+    c->peers.recv[k] = static_cast<unsigned long long*>(base);
+  }
+  c->peers.epoch = reinterpret_cast<unsigned long long*>(static_cast<char*>(c->tp_base) + recv_bytes + flag_bytes);
+  c->peers.rank = c->tp_rank;
+  c->peers.size = c->tp_size;
+  c->p2p = true;
   return QB_OK;
 }
 

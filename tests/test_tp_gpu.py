@@ -23,11 +23,11 @@ def _port():
     return p
 
 
-def _run(world, config, tmp_path):
+def _run(world, config, tmp_path, nccl_only=False):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
-    out = str(tmp_path / f"tp{world}_{config}.json")
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    out = str(tmp_path / f"tp{world}_{config}_{int(nccl_only)}.json")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", QB_TP_NCCL="1" if nccl_only else "0")
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={world}", "--master-addr", "127.0.0.1", "--master-port", str(_port()),
            os.path.join(ROOT, "tests", "tp_gpu_worker.py"), out, config]
@@ -38,8 +38,9 @@ def _run(world, config, tmp_path):
 
 
 @pytest.mark.parametrize("world", [2])
-def test_tp_small_matches_golden(world, tmp_path, built_lib):
-    got = _run(world, "qwen3-small", tmp_path)
+@pytest.mark.parametrize("nccl_only", [False, True], ids=["peer-reduction", "nccl-allreduce"])
+def test_tp_small_matches_golden(world, nccl_only, tmp_path, built_lib):
+    got = _run(world, "qwen3-small", tmp_path, nccl_only)
     gold = np.load(os.path.join(GOLDEN, "qwen3_small_greedy.npz"))["tokens"].tolist()
     assert got["tokens"] == gold
     assert got["again"] == gold
