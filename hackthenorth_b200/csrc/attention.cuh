@@ -15,10 +15,9 @@
 // (dryft/engine/kernels/attention.py:49-57). Rows are (head-in-group, query)
 // pairs of one KV head, head-major, padded to 16 or 32. The 4 warps' states are
 // combined in a fixed order; splits are merged by log-sum-exp
-// (dryft/engine/kernels/attention.py:200-210). Decode launches one thread-block
-// cluster per KV head and merges through the leader CTA's shared memory
-// (attn_decode_cluster_kernel); other uses merge through global memory in the
-// CTA that arrives last for its KV head (attn_kernel).
+// (dryft/engine/kernels/attention.py:200-210) through global memory in the CTA
+// that arrives last for its KV head (attn_kernel). Batch-one decode has its own
+// cluster kernel (decode_attention.cuh), which reuses the helpers below.
 //
 // PRO (decode prologue) variant: the CTA computes its query rows from the
 // packed QKV row (per-head RMSNorm, bf16 x gain, rotate-half RoPE with the
@@ -608,85 +607,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (r0 + j < nrows) attn_store_out(a, kvh, r0 + j, d, acc[j] / den[j]);
   }
   if (ctid == 0) a.counters[kvh] = 0u;
-}
-
-// Decode attention (one query row, prologue fused) with the KV head's splits
-// launched as one thread-block cluster: each CTA writes its split's output and
-// log-sum-exp into the leader CTA's shared memory (distributed shared memory),
-// and the leader merges them after a cluster barrier. No global partials, no
-// atomics. Every thread of every CTA reaches both cluster barriers, including
-// CTAs without work and CTAs whose bounded waits gave up.
-// Cluster size = a.splits; the leader's ring holds [splits][rows][129] floats.
-__global__ void __launch_bounds__(kAttnThreads, 1)
-    attn_decode_cluster_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
-                               const AttnArgs a) {
-  constexpr int MT = 1;
-  constexpr int ROWS = 16;
-  extern __shared__ uint8_t smem_raw[];
-  const AttnSmem sm = attn_carve<MT>(smem_raw);
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5;
-  const int S = a.splits;
-  const int kvh = blockIdx.x / S;
-  const int split = blockIdx.x % S;  // == cluster rank
-  const int nrows = a.Hq / a.Hkv;
-  const AttnRange R = attn_setup<MT>(a, sm, split, true);
-  const int Se = R.Se;
-  const bool idle = split >= Se;
-  float val[ROWS], lsev[ROWS];
-  bool ok = false;
-  if (warp == kAttnWarps) {
-    if (!idle && (tid & 31) == 0) attn_produce<true>(&tmk, &tmv, a, sm, kvh, R.k0, R.nst);
-    else {
-      pdl_wait();
-      pdl_trigger();
-    }
-    __syncwarp();
-  } else if (!idle) {
-    ok = attn_consume<MT, true>(a, sm, kvh, R.last, R.n, R.k0, R.k1, R.nst, val, lsev);
-  } else {
-    pdl_wait();
-    pdl_trigger();
-  }
-  if (Se == 1) {  // uniform across the cluster: the single split is the answer
-    if (warp < kAttnWarps && split == 0 && ok)
-#pragma unroll
-      for (int r = 0; r < ROWS; ++r)
-        if (r < nrows) attn_store_out(a, kvh, r, tid, val[r]);
-    return;
-  }
-  // Barrier 1: every CTA is done with its own ring, so the leader's ring can
-  // receive the splits. Then each active CTA writes rows [nrows][128] + lse.
-  cluster_sync_all();
-  float* mbuf = reinterpret_cast<float*>(sm.ring);  // leader: [Se][nrows][128], then lse [Se][nrows]
-  float* mlse = mbuf + (size_t)S * nrows * kAttnD;
-  if (warp < kAttnWarps && !idle && ok) {
-    const uint32_t base = map_shared_rank(mbuf, 0);
-    const uint32_t lbase = map_shared_rank(mlse, 0);
-#pragma unroll
-    for (int r = 0; r < ROWS; ++r) {
-      if (r < nrows) {
-        st_cluster_f32(base + (uint32_t)(((split * nrows + r) * kAttnD + tid) * 4), val[r]);
-        if (tid == 0) st_cluster_f32(lbase + (uint32_t)((split * nrows + r) * 4), lsev[r]);
-      }
-    }
-  }
-  cluster_sync_all();
-  if (split != 0 || warp >= kAttnWarps) return;
-  // Leader: weights exp2(lse_s - max) / sum over the Se splits
-  // (dryft/engine/kernels/attention.py:204-206), summed in split order.
-  const int d = tid;
-  for (int r = 0; r < nrows; ++r) {
-    float mx = -INFINITY;
-    for (int sp = 0; sp < Se; ++sp) mx = fmaxf(mx, mlse[sp * nrows + r]);
-    float den = 0.f, acc = 0.f;
-    for (int sp = 0; sp < Se; ++sp) {
-      const float w = exp2f(mlse[sp * nrows + r] - mx);
-      den += w;
-      acc = fmaf(mbuf[(sp * nrows + r) * kAttnD + d], w, acc);
-    }
-    attn_store_out(a, kvh, r, d, acc / den);
-  }
 }
 
 }  // namespace qb

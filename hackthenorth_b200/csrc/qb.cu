@@ -22,6 +22,7 @@
 #include <vector>
 
 #include "attention.cuh"
+#include "decode_attention.cuh"
 #include "common.cuh"
 #include "gemv.cuh"
 
@@ -192,14 +193,15 @@ EncodeTiledFn encode_fn() {
 }
 
 // Tensor map over one layer's cache viewed as [Hkv*cap rows][128 dims] bf16,
-// box [64 rows][64 dims], 128-byte swizzle; out-of-range rows read as zero.
-bool make_kv_map(CUtensorMap* m, const void* base, int hkv, int cap) {
+// box [rows][64 dims] (64 rows for attn_kernel, 32 for attn_decode_kernel),
+// 128-byte swizzle; out-of-range rows read as zero.
+bool make_kv_map(CUtensorMap* m, const void* base, int hkv, int cap, int rows = kAttnKeys) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) return false;
   cuuint64_t dims[2] = {(cuuint64_t)kAttnD, (cuuint64_t)hkv * (cuuint64_t)cap};
   cuuint64_t strides[1] = {(cuuint64_t)kAttnD * 2};
-  cuuint32_t box[2] = {64, (cuuint32_t)kAttnKeys};
+  cuuint32_t box[2] = {64, (cuuint32_t)rows};
   cuuint32_t estr[2] = {1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -224,10 +226,11 @@ cudaError_t launch_attn_t(const CUtensorMap& tk, const CUtensorMap& tv, const At
   return launch_ex(attn_kernel<MT, PRO>, dim3(a.Hkv * a.splits), dim3(kAttnThreads), smem, st, tk, tv, a);
 }
 
-// Decode attention as one thread-block cluster per KV head (splits merged
-// through distributed shared memory). Returns the cluster size to use for
-// `hkv` heads of `rows` query rows, or 0 when clusters do not fit (then the
-// global-merge kernel is used). QB_ATTN_CLUSTER=0 disables clusters.
+// Batch-one decode attention as one thread-block cluster per KV head
+// (attn_decode_kernel). Returns the cluster size for `hkv` heads of `rows`
+// query rows (16 when 16-CTA clusters of this kernel fit `hkv` at once, else
+// 8), or 0 when the kernel does not apply (then attn_kernel is used).
+// QB_ATTN_CLUSTER=0 disables it.
 int decode_cluster_size(int hkv, int rows) {
   static int cached_hkv = -1, cached_rows = -1, cached = 0;
   if (hkv == cached_hkv && rows == cached_rows) return cached;
@@ -236,17 +239,17 @@ int decode_cluster_size(int hkv, int rows) {
   cached = 0;
   const char* e = std::getenv("QB_ATTN_CLUSTER");
   if (e && e[0] == '0') return 0;
-  const size_t smem = attn_smem_bytes(1);
-  if (cudaFuncSetAttribute(attn_decode_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+  if (rows > kDecRows) return 0;
+  const size_t smem = dec_smem_bytes();
+  if (cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
       cudaSuccess)
     return 0;
-  cudaFuncSetAttribute(attn_decode_cluster_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   const int sizes[2] = {16, 8};
   for (int cs : sizes) {
-    if ((size_t)cs * rows * (kAttnD + 1) * 4 > (size_t)kAttnStages * kAttnStageBytes) continue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(hkv * cs);
-    cfg.blockDim = dim3(kAttnThreads);
+    cfg.blockDim = dim3(kDecThreads);
     cfg.dynamicSmemBytes = smem;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -256,7 +259,7 @@ int decode_cluster_size(int hkv, int rows) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, attn_decode_cluster_kernel, &cfg) == cudaSuccess && n >= hkv) {
+    if (cudaOccupancyMaxActiveClusters(&n, attn_decode_kernel, &cfg) == cudaSuccess && n >= hkv) {
       cached = cs;
       break;
     }
@@ -265,12 +268,12 @@ int decode_cluster_size(int hkv, int rows) {
   return cached;
 }
 
-cudaError_t launch_attn_cluster(const CUtensorMap& tk, const CUtensorMap& tv, AttnArgs a, int cs, cudaStream_t st) {
+cudaError_t launch_attn_decode(const CUtensorMap& tk, const CUtensorMap& tv, AttnArgs a, int cs, cudaStream_t st) {
   a.splits = cs;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.Hkv * cs);
-  cfg.blockDim = dim3(kAttnThreads);
-  cfg.dynamicSmemBytes = attn_smem_bytes(1);
+  cfg.blockDim = dim3(kDecThreads);
+  cfg.dynamicSmemBytes = dec_smem_bytes();
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -281,13 +284,16 @@ cudaError_t launch_attn_cluster(const CUtensorMap& tk, const CUtensorMap& tv, At
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, attn_decode_cluster_kernel, tk, tv, a);
+  return cudaLaunchKernelEx(&cfg, attn_decode_kernel, tk, tv, a);
 }
 
-cudaError_t launch_attn(const CUtensorMap& tk, const CUtensorMap& tv, const AttnArgs& a, bool pro, cudaStream_t st) {
-  if (pro && a.Q == 1) {
+// tk/tv: 64-row-box maps (attn_kernel); dk/dv: 32-row-box maps of the same
+// caches (attn_decode_kernel), or null.
+cudaError_t launch_attn(const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap* dk, const CUtensorMap* dv,
+                        const AttnArgs& a, bool pro, cudaStream_t st) {
+  if (pro && a.Q == 1 && dk != nullptr && dv != nullptr) {
     const int cs = decode_cluster_size(a.Hkv, a.Hq / a.Hkv);
-    if (cs > 0) return launch_attn_cluster(tk, tv, a, cs, st);
+    if (cs > 0) return launch_attn_decode(*dk, *dv, a, cs, st);
   }
   const int rows = (a.Hq / a.Hkv) * a.Q;
   if (pro) return launch_attn_t<1, true>(tk, tv, a, st);
@@ -334,7 +340,8 @@ struct qb_ctx {
   float* part_o = nullptr;
   float* part_lse = nullptr;
   int splits = 1;
-  std::vector<CUtensorMap> tmk, tmv;
+  std::vector<CUtensorMap> tmk, tmv;  // 64-row boxes
+  std::vector<CUtensorMap> dmk, dmv;  // 32-row boxes (decode kernel)
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   std::string msg;
@@ -452,7 +459,7 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
     at.Q = 1;
     at.cap = c->cap;
     at.splits = c->splits;
-    if ((e = launch_attn(c->tmk[l], c->tmv[l], at, true, st)) != cudaSuccess)
+    if ((e = launch_attn(c->tmk[l], c->tmv[l], &c->dmk[l], &c->dmv[l], at, true, st)) != cudaSuccess)
       return cuda_fail(&c->msg, e, "attention launch");
     // 3. o-proj (+ residual): xb = xa + O . attn
     if (tp && !p2p) {
@@ -659,10 +666,14 @@ int qb_bind_state(qb_ctx* c, void* k_cache, void* v_cache, int capacity, const v
   const qb_config& g = c->lc;
   c->tmk.assign(g.n_layers, CUtensorMap());
   c->tmv.assign(g.n_layers, CUtensorMap());
+  c->dmk.assign(g.n_layers, CUtensorMap());
+  c->dmv.assign(g.n_layers, CUtensorMap());
   for (int l = 0; l < g.n_layers; ++l) {
     const size_t off = (size_t)l * g.n_kv_heads * capacity * g.head_dim;
     if (!make_kv_map(&c->tmk[l], c->kc + off, g.n_kv_heads, capacity) ||
-        !make_kv_map(&c->tmv[l], c->vc + off, g.n_kv_heads, capacity))
+        !make_kv_map(&c->tmv[l], c->vc + off, g.n_kv_heads, capacity) ||
+        !make_kv_map(&c->dmk[l], c->kc + off, g.n_kv_heads, capacity, kDecKeys) ||
+        !make_kv_map(&c->dmv[l], c->vc + off, g.n_kv_heads, capacity, kDecKeys))
       return set_err(&c->msg, QB_ERR_CUDA, "cuTensorMapEncodeTiled failed for the KV cache");
   }
   if (c->exec) {
@@ -902,8 +913,9 @@ static int op_attention(const void* qkv, const void* q, const void* q_norm, cons
   int splits = attn_splits_for(hkv, sms);
   if (hkv * splits > kMaxAttnCtas) splits = kMaxAttnCtas / hkv > 0 ? kMaxAttnCtas / hkv : 1;
   if ((size_t)hkv * splits * 32 * 4 > 65536) return set_err(nullptr, QB_ERR_UNSUPPORTED, "too many KV heads for the op scratch");
-  CUtensorMap tk, tv;
-  if (!make_kv_map(&tk, k_cache, hkv, cap) || !make_kv_map(&tv, v_cache, hkv, cap))
+  CUtensorMap tk, tv, dk, dv;
+  if (!make_kv_map(&tk, k_cache, hkv, cap) || !make_kv_map(&tv, v_cache, hkv, cap) ||
+      !make_kv_map(&dk, k_cache, hkv, cap, kDecKeys) || !make_kv_map(&dv, v_cache, hkv, cap, kDecKeys))
     return set_err(nullptr, QB_ERR_CUDA, "cuTensorMapEncodeTiled failed");
   uint8_t* s = static_cast<uint8_t*>(scratch);
   AttnArgs a;
@@ -928,7 +940,7 @@ static int op_attention(const void* qkv, const void* q, const void* q_norm, cons
   a.Q = queries;
   a.cap = cap;
   a.splits = splits;
-  cudaError_t e = launch_attn(tk, tv, a, pro, static_cast<cudaStream_t>(stream));
+  cudaError_t e = launch_attn(tk, tv, &dk, &dv, a, pro, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(nullptr, e, "attention launch");
   return QB_OK;
 }
@@ -1050,7 +1062,7 @@ extern "C" int qb_grouped_attention_noalloc(const void* q, const void* k_cache, 
   a.splits = splits;
   if (lse_bytes + (size_t)n_kv_heads * splits * padded * kAttnD * sizeof(float) > kStaticPartialBytes)
     return set_err(nullptr, QB_ERR_UNSUPPORTED, "static attention scratch too small for this call");
-  e = launch_attn(tk, tv, a, false, st);
+  e = launch_attn(tk, tv, nullptr, nullptr, a, false, st);
   if (e != cudaSuccess) return cuda_fail(nullptr, e, "attention launch");
   return QB_OK;
 }

@@ -171,7 +171,8 @@ def test_attention_matches_golden_sdpa():
 
 
 @pytest.mark.parametrize("hq,hkv,cap,position", [(32, 8, 41, 3), (32, 8, 41, 40), (16, 8, 4352, 4096),
-                                                 (32, 8, 300, 0), (32, 8, 8192, 5000)])
+                                                 (32, 8, 300, 0), (32, 8, 8192, 5000), (64, 8, 2048, 1500),
+                                                 (4, 1, 20000, 17000), (32, 8, 33000, 32767), (8, 2, 600, 511)])
 def test_rope_attention_matches_oracle_and_appends_cache(hq, hkv, cap, position):
     from hackthenorth_b200 import ops
     from hackthenorth_b200.config import ModelConfig
