@@ -347,8 +347,12 @@ def run_ours(args):
         "dtype": "bf16",
         "data": "synthetic (seeded random-init weights N(0,0.02); KV cache of seeded N(0,1) positions)",
         "config": {"workload": f"{cfg.name}-shaped batch-1 greedy decode at context {ctx}",
-                   "model": cfg.name, "global_batch": world, "seq_len": ctx, "context": ctx,
-                   "parallelism": "none" if world == 1 else f"tp{world} (NCCL all-reduce after o-proj and down)",
+                   "model": cfg.name, "global_batch": 1, "seq_len": ctx, "context": ctx,
+                   "parallelism": "none" if world == 1 else (
+                       f"tp{world} (NCCL all-reduce after o-proj and down)" if os.environ.get("QB_TP_NCCL") == "1"
+                       else f"tp{world} (peer-memory reduction fused into the o-proj and down epilogues over NVLink)"),
+                   "decode_path": os.environ.get("QB_STEP_KERNEL") == "1" and world == 1 and "step-kernel"
+                   or "per-sublayer",
                    "l2": "inputs larger than L2 (weights stream %.1f GB per step)" % (cfg.weight_bytes_per_token() / 1e9)},
         "roofline": {"bound": "hbm", "kernel": "gemv_kernel<EPI_SWIGLU> (post-norm + gate/up + SwiGLU)",
                      "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
@@ -478,7 +482,10 @@ def main(argv=None):
                     help="attention: the decode-attention op sweep (not the headline line)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: override the layer count (the line is marked profile_only)")
+    ap.add_argument("--decode-path", choices=("per-sublayer", "step-kernel"), default="per-sublayer",
+                    help="step-kernel: the opt-in persistent one-launch-per-step kernel (single GPU)")
     args = ap.parse_args(argv)
+    os.environ["QB_STEP_KERNEL"] = "1" if args.decode_path == "step-kernel" else "0"
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     if args.impl == "reference":

@@ -47,6 +47,7 @@ SIGNATURES = {
     "qb_capture_decode": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "qb_replay_decode": (c_int, [c_void_p, c_void_p]),
     "qb_check": (c_int, [c_void_p, c_void_p]),
+    "qb_decode_mode": (c_int, [c_void_p]),
     "qb_norm_projection": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_int, c_void_p]),
     "qb_projection_residual": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
     "qb_op_scratch_bytes": (c_size_t, []),

@@ -133,6 +133,15 @@ int qb_replay_decode(qb_ctx* ctx, void* stream);
  * up, out-of-range token ids). Clears the device error word. */
 int qb_check(qb_ctx* ctx, void* stream);
 
+/* How decode steps of this context run (a diagnostic; the reference has one
+ * path): 0 = one launch per sublayer (the default), 1 = one persistent
+ * cooperative kernel per step (single GPU, opt-in with QB_STEP_KERNEL=1 in the
+ * environment when the context is created; prefill rows and tensor-parallel
+ * contexts always use 0). Known after qb_bind_weights and qb_bind_state; a
+ * capture that cannot record the cooperative launch switches the context to
+ * 0. Returns -1 for NULL. */
+int qb_decode_mode(const qb_ctx* ctx);
+
 /* ---- op-level entry points (the reference's kernel wrappers) ------------- */
 
 /* RMSNorm(x; gain, eps) fused with y = W . x, fp32 accumulation, one bf16
