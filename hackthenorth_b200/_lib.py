@@ -48,6 +48,9 @@ SIGNATURES = {
     "qb_replay_decode": (c_int, [c_void_p, c_void_p]),
     "qb_check": (c_int, [c_void_p, c_void_p]),
     "qb_decode_mode": (c_int, [c_void_p]),
+    "qb_verify": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "qb_capture_verify": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "qb_replay_verify": (c_int, [c_void_p, c_void_p]),
     "qb_norm_projection": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_int, c_void_p]),
     "qb_projection_residual": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
     "qb_op_scratch_bytes": (c_size_t, []),

@@ -25,6 +25,8 @@
 #include "attention.cuh"
 #include "decode_attention.cuh"
 #include "step_kernel.cuh"
+#include "gemv_rows.cuh"
+#include "verify_attention.cuh"
 #include "common.cuh"
 #include "gemv.cuh"
 
@@ -289,6 +291,70 @@ cudaError_t launch_attn_decode(const CUtensorMap& tk, const CUtensorMap& tv, Att
   return cudaLaunchKernelEx(&cfg, attn_decode_kernel, tk, tv, a);
 }
 
+// Verify-pass attention (attn_rows_kernel, R = G * Q <= 24 rows) as one
+// cluster per KV head: the cluster size (16 or 8) or 0 when it does not fit.
+int rows_cluster_size(int hkv) {
+  static int cached_hkv = -1, cached = 0;
+  if (hkv == cached_hkv) return cached;
+  cached_hkv = hkv;
+  cached = 0;
+  const char* e = std::getenv("QB_ATTN_CLUSTER");
+  if (e && e[0] == '0') return 0;
+  const size_t smem = va_smem_bytes();
+  void (*kernels[3])(const CUtensorMap, const CUtensorMap, const AttnArgs) = {
+      attn_rows_kernel<1>, attn_rows_kernel<2>, attn_rows_kernel<3>};
+  for (auto k : kernels) {
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
+        cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+      cudaGetLastError();
+      return 0;
+    }
+  }
+  const int sizes[2] = {16, 8};
+  for (int cs : sizes) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(hkv * cs);
+    cfg.blockDim = dim3(kVaThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, attn_rows_kernel<3>, &cfg) == cudaSuccess && n >= hkv) {
+      cached = cs;
+      break;
+    }
+    cudaGetLastError();
+  }
+  return cached;
+}
+
+cudaError_t launch_attn_rows(const CUtensorMap& tk, const CUtensorMap& tv, AttnArgs a, int cs, cudaStream_t st) {
+  a.splits = cs;
+  const int rows = (a.Hq / a.Hkv) * a.Q;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.Hkv * cs);
+  cfg.blockDim = dim3(kVaThreads);
+  cfg.dynamicSmemBytes = va_smem_bytes();
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  if (rows <= 8) return cudaLaunchKernelEx(&cfg, attn_rows_kernel<1>, tk, tv, a);
+  if (rows <= 16) return cudaLaunchKernelEx(&cfg, attn_rows_kernel<2>, tk, tv, a);
+  return cudaLaunchKernelEx(&cfg, attn_rows_kernel<3>, tk, tv, a);
+}
+
 // tk/tv: 64-row-box maps (attn_kernel); dk/dv: 32-row-box maps of the same
 // caches (attn_decode_kernel), or null.
 cudaError_t launch_attn(const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap* dk, const CUtensorMap* dv,
@@ -350,6 +416,13 @@ struct qb_ctx {
   uint32_t *w_xa = nullptr, *w_xb = nullptr, *w_qkv = nullptr, *w_attn = nullptr, *w_act = nullptr;
   unsigned long long *w_part_o = nullptr, *w_part_lse = nullptr;
   unsigned* step_epoch = nullptr;   // tag step counter (in the error block, kept across counter resets)
+  // verify pass (k+1 rows)
+  bf16 *r_xa = nullptr, *r_xb = nullptr, *r_qkv = nullptr, *r_q = nullptr, *r_attn = nullptr, *r_act = nullptr;
+  int64_t* r_pos = nullptr;
+  float* r_val = nullptr;
+  int* r_idx = nullptr;
+  cudaGraph_t vgraph = nullptr;
+  cudaGraphExec_t vexec = nullptr;
   bool step_allowed = false;        // QB_STEP_KERNEL=1 at creation turns it on
   bool step_ready = false;          // descriptors built for the bound weights and state
   void* step_buf = nullptr;         // device: [2L tensor maps | 5L+1 phases]
@@ -364,7 +437,9 @@ namespace {
 struct WsLayout {
   size_t err, counters, head_val, head_idx, xa, xb, qkv, attn, act, part_lse, part_o, y32, pairs;
   // persistent step kernel: tagged activation words and split partials
-  size_t w_xa, w_xb, w_qkv, w_attn, w_act, w_part_o, w_part_lse, total;
+  size_t w_xa, w_xb, w_qkv, w_attn, w_act, w_part_o, w_part_lse;
+  // verify pass: up to kRowsMaxQ rows
+  size_t r_xa, r_xb, r_qkv, r_q, r_attn, r_act, r_pos, r_val, r_idx, total;
 };
 
 WsLayout ws_layout(const qb_ctx* c) {
@@ -394,6 +469,16 @@ WsLayout ws_layout(const qb_ctx* c) {
   const size_t wparts = (size_t)g.n_kv_heads * kStepMaxSplits * kDecRows;
   L.w_part_lse = o; o = align_up(o + wparts * 8, 256);
   L.w_part_o = o; o = align_up(o + wparts * kAttnD * 8, 256);
+  const size_t R = kRowsMaxQ;
+  L.r_xa = o; o = align_up(o + R * g.hidden * 2, 256);
+  L.r_xb = o; o = align_up(o + R * g.hidden * 2, 256);
+  L.r_qkv = o; o = align_up(o + R * nqkv * 2, 256);
+  L.r_q = o; o = align_up(o + R * g.n_heads * g.head_dim * 2, 256);
+  L.r_attn = o; o = align_up(o + R * g.n_heads * g.head_dim * 2, 256);
+  L.r_act = o; o = align_up(o + R * g.ffn * 2, 256);
+  L.r_pos = o; o = align_up(o + R * 8, 256);
+  L.r_val = o; o = align_up(o + R * 1024 * 4, 256);
+  L.r_idx = o; o = align_up(o + R * 1024 * 4, 256);
   L.total = o;
   return L;
 }
@@ -757,6 +842,128 @@ cudaError_t launch_step(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int6
   return cudaLaunchKernelEx(&cfg, step_kernel, a);
 }
 
+template <int EPI>
+cudaError_t launch_rows(const RowsArgs& a, int sm_count, cudaStream_t st) {
+  static bool attr_done = false;
+  const size_t smem = rows_smem_bytes();
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(gemv_rows_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr_done = true;
+  }
+  return launch_ex(gemv_rows_kernel<EPI>, dim3(sm_count), dim3(kRowsThreads), smem, st, a);
+}
+
+RowsArgs rows_args(const void* w, int K, int rows, int Q, const bf16* x, bf16* out, int* err) {
+  RowsArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.w = static_cast<const bf16*>(w);
+  a.K = K;
+  a.rows = rows;
+  a.Q = Q;
+  a.x = x;
+  a.out = out;
+  a.err = err;
+  return a;
+}
+
+// The verify pass (DecodeState.verify_step, dryft/engine/decode.py:168-179):
+// rows ids[0..n) at positions *pos .. *pos+n-1 through every layer, their K/V
+// appended, every row through the LM head; predictions[i] = greedy token after
+// row i. The position itself is left to the caller (logical rollback).
+int run_verify(qb_ctx* c, const int64_t* ids, int n, const int64_t* pos, int64_t* preds, void* logits,
+               cudaStream_t st) {
+  const qb_config& g = c->lc;
+  const int H = g.hidden, D = g.head_dim;
+  const int nqkv = (g.n_heads + 2 * g.n_kv_heads) * D;
+  cudaError_t e;
+  for (int l = 0; l < g.n_layers; ++l) {
+    const qb_layer_weights& w = c->layers[l];
+    RowsArgs a = rows_args(w.qkv, H, nqkv, n, l == 0 ? nullptr : c->r_xa, c->r_qkv, c->err);
+    a.gain = static_cast<const bf16*>(w.input_norm);
+    a.eps = g.rms_eps;
+    if (l == 0) {
+      a.embed = c->embed;
+      a.tokens = ids;
+      a.vocab = c->cfg.vocab;
+      a.x_copy = c->r_xa;
+    }
+    if ((e = launch_rows<EPI_STORE>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "verify qkv");
+    RopeRowsArgs ra;
+    std::memset(&ra, 0, sizeof(ra));
+    ra.qkv = c->r_qkv;
+    ra.q_norm = static_cast<const bf16*>(w.q_norm);
+    ra.k_norm = static_cast<const bf16*>(w.k_norm);
+    ra.cos = c->cos;
+    ra.sin = c->sin;
+    ra.eps = g.rms_eps;
+    ra.pos = pos;
+    ra.positions = c->r_pos;
+    ra.q_out = c->r_q;
+    const size_t layer_off = (size_t)l * g.n_kv_heads * c->cap * D;
+    ra.k_cache = c->kc + layer_off;
+    ra.v_cache = c->vc + layer_off;
+    ra.err = c->err;
+    ra.Q = n;
+    ra.Hq = g.n_heads;
+    ra.Hkv = g.n_kv_heads;
+    ra.cap = c->cap;
+    const int warps = n * (g.n_heads + 2 * g.n_kv_heads);
+    if ((e = launch_ex(rope_rows_kernel, dim3((warps + 3) / 4), dim3(128), 0, st, ra)) != cudaSuccess)
+      return cuda_fail(&c->msg, e, "verify rope");
+    AttnArgs at;
+    std::memset(&at, 0, sizeof(at));
+    at.q = c->r_q;
+    at.pos = c->r_pos;
+    at.k_cache = ra.k_cache;
+    at.v_cache = ra.v_cache;
+    at.out = c->r_attn;
+    at.part_o = c->part_o;
+    at.part_lse = c->part_lse;
+    at.counters = c->counters;
+    at.err = c->err;
+    at.Hq = g.n_heads;
+    at.Hkv = g.n_kv_heads;
+    at.Q = n;
+    at.cap = c->cap;
+    at.splits = c->splits;
+    const int vcs = (g.n_heads / g.n_kv_heads) * n <= kVaMaxRows ? rows_cluster_size(g.n_kv_heads) : 0;
+    e = vcs > 0 ? launch_attn_rows(c->dmk[l], c->dmv[l], at, vcs, st)
+                : launch_attn(c->tmk[l], c->tmv[l], nullptr, nullptr, at, false, st);
+    if (e != cudaSuccess) return cuda_fail(&c->msg, e, "verify attention");
+    a = rows_args(w.o, g.n_heads * D, H, n, c->r_attn, c->r_xb, c->err);
+    a.residual = c->r_xa;
+    if ((e = launch_rows<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "verify o");
+    a = rows_args(w.gate_up, H, 2 * g.ffn, n, c->r_xb, c->r_act, c->err);
+    a.gain = static_cast<const bf16*>(w.post_norm);
+    a.eps = g.rms_eps;
+    if ((e = launch_rows<EPI_SWIGLU>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "verify gu");
+    a = rows_args(w.down, g.ffn, H, n, c->r_act, c->r_xa, c->err);
+    a.residual = c->r_xb;
+    if ((e = launch_rows<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "verify down");
+  }
+  RowsArgs a = rows_args(c->lm_head, H, g.vocab, n, c->r_xa, nullptr, c->err);
+  a.gain = c->final_norm;
+  a.eps = g.rms_eps;
+  a.logits = static_cast<bf16*>(logits);
+  a.part_val = c->r_val;
+  a.part_idx = c->r_idx;
+  a.counter = c->counters + 66;
+  a.tokens_out = preds;
+  if ((e = launch_rows<EPI_ARGMAX>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "verify head");
+  return QB_OK;
+}
+
+int check_verify_args(qb_ctx* c, const int64_t* ids, int n, const int64_t* pos, const int64_t* preds) {
+  if (!ids || !pos || !preds) return set_err(&c->msg, QB_ERR_ARG, "ids/position/predictions are NULL");
+  if (n < 1 || n > kRowsMaxQ) return set_err(&c->msg, QB_ERR_UNSUPPORTED, "verify takes 1..8 rows");
+  if ((c->lc.n_heads / c->lc.n_kv_heads) * n > 32)
+    return set_err(&c->msg, QB_ERR_UNSUPPORTED, "GQA group x verify rows above 32");
+  if (c->tp_size != 1) return set_err(&c->msg, QB_ERR_UNSUPPORTED, "verify runs on one GPU");
+  if (c->sm_count > 1024) return set_err(&c->msg, QB_ERR_UNSUPPORTED, "more than 1024 SMs");
+  return QB_OK;
+}
+
 int require_ready(qb_ctx* c) {
   if (!c) return set_err(nullptr, QB_ERR_ARG, "ctx is NULL");
   if (!c->weights_bound) return set_err(&c->msg, QB_ERR_STATE, "weights not bound");
@@ -818,6 +1025,8 @@ int qb_destroy(qb_ctx* c) {
   if (!c) return QB_OK;
   if (c->exec) cudaGraphExecDestroy(c->exec);
   if (c->graph) cudaGraphDestroy(c->graph);
+  if (c->vexec) cudaGraphExecDestroy(c->vexec);
+  if (c->vgraph) cudaGraphDestroy(c->vgraph);
   release_step(c);
   if (c->p2p) {
     cudaSetDevice(c->device);
@@ -895,6 +1104,15 @@ int qb_bind_state(qb_ctx* c, void* k_cache, void* v_cache, int capacity, const v
   c->w_part_o = reinterpret_cast<unsigned long long*>(c->ws + L.w_part_o);
   c->w_part_lse = reinterpret_cast<unsigned long long*>(c->ws + L.w_part_lse);
   c->step_epoch = reinterpret_cast<unsigned*>(c->ws + L.err + 64);
+  c->r_xa = reinterpret_cast<bf16*>(c->ws + L.r_xa);
+  c->r_xb = reinterpret_cast<bf16*>(c->ws + L.r_xb);
+  c->r_qkv = reinterpret_cast<bf16*>(c->ws + L.r_qkv);
+  c->r_q = reinterpret_cast<bf16*>(c->ws + L.r_q);
+  c->r_attn = reinterpret_cast<bf16*>(c->ws + L.r_attn);
+  c->r_act = reinterpret_cast<bf16*>(c->ws + L.r_act);
+  c->r_pos = reinterpret_cast<int64_t*>(c->ws + L.r_pos);
+  c->r_val = reinterpret_cast<float*>(c->ws + L.r_val);
+  c->r_idx = reinterpret_cast<int*>(c->ws + L.r_idx);
   if ((e = cudaMemset(workspace, 0, L.total)) != cudaSuccess) return cuda_fail(&c->msg, e, "workspace memset");
   const qb_config& g = c->lc;
   c->tmk.assign(g.n_layers, CUtensorMap());
@@ -916,6 +1134,14 @@ int qb_bind_state(qb_ctx* c, void* k_cache, void* v_cache, int capacity, const v
   if (c->graph) {
     cudaGraphDestroy(c->graph);
     c->graph = nullptr;
+  }
+  if (c->vexec) {
+    cudaGraphExecDestroy(c->vexec);
+    c->vexec = nullptr;
+  }
+  if (c->vgraph) {
+    cudaGraphDestroy(c->vgraph);
+    c->vgraph = nullptr;
   }
   c->state_bound = true;
   prepare_step(c);
@@ -1054,6 +1280,54 @@ int qb_replay_decode(qb_ctx* c, void* stream) {
   if (!c) return set_err(nullptr, QB_ERR_ARG, "ctx is NULL");
   if (!c->exec) return set_err(&c->msg, QB_ERR_STATE, "no captured decode graph");
   cudaError_t e = cudaGraphLaunch(c->exec, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(&c->msg, e, "graph launch");
+  return QB_OK;
+}
+
+int qb_verify(qb_ctx* c, const int64_t* ids, int n, const int64_t* position, int64_t* predictions,
+              void* logits_out, void* stream) {
+  int rc = require_ready(c);
+  if (rc) return rc;
+  if ((rc = check_verify_args(c, ids, n, position, predictions))) return rc;
+  return run_verify(c, ids, n, position, predictions, logits_out, static_cast<cudaStream_t>(stream));
+}
+
+int qb_capture_verify(qb_ctx* c, const int64_t* ids, int n, const int64_t* position, int64_t* predictions,
+                      void* logits_out, void* stream) {
+  int rc = require_ready(c);
+  if (rc) return rc;
+  if ((rc = check_verify_args(c, ids, n, position, predictions))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (c->vexec) {
+    cudaGraphExecDestroy(c->vexec);
+    c->vexec = nullptr;
+  }
+  if (c->vgraph) {
+    cudaGraphDestroy(c->vgraph);
+    c->vgraph = nullptr;
+  }
+  cudaError_t e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+  if (e != cudaSuccess) return cuda_fail(&c->msg, e, "begin capture");
+  rc = run_verify(c, ids, n, position, predictions, logits_out, st);
+  cudaGraph_t graph = nullptr;
+  e = cudaStreamEndCapture(st, &graph);
+  if (rc) {
+    if (graph) cudaGraphDestroy(graph);
+    return rc;
+  }
+  if (e != cudaSuccess) return cuda_fail(&c->msg, e, "end capture");
+  if ((e = cudaGraphInstantiate(&c->vexec, graph, 0)) != cudaSuccess) {
+    cudaGraphDestroy(graph);
+    return cuda_fail(&c->msg, e, "graph instantiate");
+  }
+  c->vgraph = graph;
+  return QB_OK;
+}
+
+int qb_replay_verify(qb_ctx* c, void* stream) {
+  if (!c) return set_err(nullptr, QB_ERR_ARG, "ctx is NULL");
+  if (!c->vexec) return set_err(&c->msg, QB_ERR_STATE, "no captured verify graph");
+  cudaError_t e = cudaGraphLaunch(c->vexec, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(&c->msg, e, "graph launch");
   return QB_OK;
 }

@@ -121,6 +121,45 @@ class DecodeState:
         token or position out of range)."""
         _lib.check(_lib.load().qb_check(self.engine.ctx, _lib.stream_handle()), self.engine.ctx)
 
+    # -- speculative verification ------------------------------------------------
+    def verify(self, current_token: int, proposal: List[int]) -> List[int]:
+        """Verify ``proposal`` after ``current_token`` (``DecodeState.verify``,
+        ``dryft/engine/decode.py:194-206``): the ``len(proposal) + 1`` rows run
+        at positions ``position ..`` in one pass (a captured graph per row
+        count), the accepted prefix plus one target token is returned, and
+        ``token`` / ``position`` advance by that many; the K/V of rejected
+        rows stay in the cache as dead slots that later steps overwrite."""
+        from .speculate import verified_tokens
+
+        self._ensure_bound()
+        n = len(proposal) + 1
+        if n > 8:
+            raise ValueError("verify takes at most 7 draft tokens")
+        dev = self.token.device
+        if getattr(self, "_verify_n", None) != n:
+            if not hasattr(self, "verify_ids"):
+                self.verify_ids = torch.zeros(8, dtype=torch.int64, device=dev)
+                self.verify_out = torch.zeros(8, dtype=torch.int64, device=dev)
+                self._verify_host = torch.zeros(8, dtype=torch.int64).pin_memory()
+            self.verify_logits = (torch.zeros(n, self.engine.cfg.vocab, dtype=BF16, device=dev)
+                                  if self.logits is not None else None)
+            side = torch.cuda.Stream(device=dev)
+            side.wait_stream(torch.cuda.current_stream())
+            _lib.check(_lib.load().qb_capture_verify(self.engine.ctx, self.verify_ids.data_ptr(), n,
+                                                     self.position.data_ptr(), self.verify_out.data_ptr(),
+                                                     _lib.ptr(self.verify_logits), side.cuda_stream),
+                       self.engine.ctx)
+            torch.cuda.current_stream().wait_stream(side)
+            self._verify_n = n
+        self._verify_host[:n] = torch.tensor([current_token, *proposal], dtype=torch.int64)
+        self.verify_ids[:n].copy_(self._verify_host[:n], non_blocking=True)
+        _lib.check(_lib.load().qb_replay_verify(self.engine.ctx, _lib.stream_handle()), self.engine.ctx)
+        predictions = self.verify_out[:n].tolist()
+        emitted = verified_tokens(proposal, predictions)
+        self.token.fill_(emitted[-1])
+        self.position.add_(len(emitted))
+        return emitted
+
     @property
     def decode_mode(self) -> str:
         """``"per-sublayer"`` (default) or ``"step-kernel"`` (one persistent
@@ -198,10 +237,23 @@ class Engine:
         self.state = DecodeState(self, prompt_length, output_length, **kw)
         return self.state
 
-    def generate(self, input_ids: List[List[int]], max_new_tokens: int):
-        """Greedy continuation, one step at a time; yields ``[token]`` exactly
-        ``max_new_tokens`` times (``dryft/engine/engine.py:202-249``)."""
+    def generate(self, input_ids: List[List[int]], max_new_tokens: int, draft_tokens: int = 0,
+                 drafter=None):
+        """Greedy continuation; yields ``[token]`` exactly ``max_new_tokens``
+        times (``dryft/engine/engine.py:202-249``).
+
+        With ``draft_tokens`` k > 0 the loop speculates as the reference does:
+        a drafter (default: ``PromptLookup`` over the prompt and the emitted
+        tokens, the reference's draft source) proposes up to k tokens, one
+        verify pass checks them, and the accepted prefix plus one target token
+        is emitted; without a proposal it takes a plain decode step. The
+        emitted sequence is the plain greedy one (verification only accepts
+        tokens the target itself predicts). ``drafter`` may be any object with
+        ``propose() -> list | None`` and ``append(token)``."""
         if max_new_tokens <= 0:
+            return
+        if draft_tokens > 0:
+            yield from self._generate_speculative(input_ids, max_new_tokens, draft_tokens, drafter)
             return
         if len(input_ids) != 1:
             raise ValueError("this engine implements the batch-one decode path")
@@ -217,3 +269,39 @@ class Engine:
             state.prefill(ids.to(self.device, non_blocking=True))
             first = state.read_token()
             yield from stream_decode(state, first, max_new_tokens)
+
+    def _generate_speculative(self, input_ids, max_new_tokens: int, k: int, drafter):
+        from .speculate import PromptLookup
+
+        if len(input_ids) != 1:
+            raise ValueError("this engine implements the batch-one decode path")
+        prompt = list(input_ids[0])
+        if not prompt:
+            raise ValueError("the prompt must hold at least one token")
+        if not 1 <= k <= 7:
+            raise ValueError("draft_tokens must lie in 1..7")
+        with torch.inference_mode():
+            # capacity holds the draft scratch slots (dryft/engine/decode.py:102-118)
+            state = self.new_state(len(prompt), max_new_tokens, draft_tokens=k)
+            ids = torch.tensor(prompt, dtype=torch.int64).pin_memory()
+            state.prefill(ids.to(self.device, non_blocking=True))
+            tokens = state.read_token()
+            yield tokens
+            lookup = drafter if drafter is not None else PromptLookup(prompt, draft_length=k)
+            lookup.append(tokens[0])
+            emitted = 1
+            while emitted < max_new_tokens:
+                proposal = lookup.propose()
+                if proposal:
+                    verified = state.verify(tokens[0], list(proposal)[:k])
+                    for token in verified[:max_new_tokens - emitted]:
+                        tokens = [token]
+                        lookup.append(token)
+                        emitted += 1
+                        yield tokens
+                else:
+                    state.step()
+                    tokens = state.read_token()
+                    lookup.append(tokens[0])
+                    emitted += 1
+                    yield tokens

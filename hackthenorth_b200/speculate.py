@@ -83,14 +83,27 @@ class SyntheticDraft:
     """Draft token i = the target's greedy continuation with probability p
     (seeded Bernoulli), otherwise a uniform id in [0, vocab)."""
 
-    def __init__(self, reference_tokens: Sequence[int], vocab: int, p: float = 0.7, seed: int = 3):
+    def __init__(self, reference_tokens: Sequence[int], vocab: int, p: float = 0.7, seed: int = 3,
+                 draft_length: int = DRAFT_TOKENS):
         self.reference = list(reference_tokens)
         self.vocab = vocab
         self.p = p
         self.rng = random.Random(seed)
+        self.draft_length = draft_length
+        self.emitted = 0
 
-    def propose(self, emitted: int, k: int) -> List[int]:
-        """k draft tokens continuing after ``emitted`` already-emitted tokens."""
+    def append(self, token: int) -> None:
+        """Drafter interface: one more emitted token."""
+        self.emitted += 1
+
+    def propose(self, emitted: Optional[int] = None, k: Optional[int] = None) -> List[int]:
+        """k draft tokens continuing after ``emitted`` already-emitted tokens.
+        Without arguments (the drafter interface of ``Engine.generate``): after
+        the tokens passed to ``append`` so far, ``draft_length`` tokens."""
+        if emitted is None:
+            emitted = self.emitted
+        if k is None:
+            k = self.draft_length
         out = []
         for j in range(k):
             idx = emitted + j

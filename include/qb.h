@@ -129,6 +129,20 @@ int qb_capture_decode(qb_ctx* ctx, int64_t* token, int64_t* position, void* logi
                       void* stream);
 int qb_replay_decode(qb_ctx* ctx, void* stream);
 
+/* The verify pass of speculative decoding: DecodeState.verify_step /
+ * capture_verifier (dryft/engine/decode.py:168-192). ids: device int64 [n]
+ * (the current token, then n-1 draft tokens), n in 1..8, run at positions
+ * *position .. *position+n-1 (device int64, not modified: the caller applies
+ * the accepted count, dryft/engine/decode.py:194-206); their K/V are written
+ * to the cache. predictions (device int64 [n]): the greedy token after each
+ * row; logits_out (device bf16 [n][V]) may be NULL. Every weight is streamed
+ * once for all n rows. Single GPU (tp_size 1); QB_ERR_UNSUPPORTED otherwise. */
+int qb_verify(qb_ctx* ctx, const int64_t* ids, int n, const int64_t* position, int64_t* predictions,
+              void* logits_out, void* stream);
+int qb_capture_verify(qb_ctx* ctx, const int64_t* ids, int n, const int64_t* position,
+                      int64_t* predictions, void* logits_out, void* stream);
+int qb_replay_verify(qb_ctx* ctx, void* stream);
+
 /* Synchronise `stream` and report device-side errors (bounded waits that gave
  * up, out-of-range token ids). Clears the device error word. */
 int qb_check(qb_ctx* ctx, void* stream);

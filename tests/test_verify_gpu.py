@@ -1,0 +1,141 @@
+"""Speculative verify pass (qb_verify / DecodeState.verify) against the CPU
+oracle and the plain greedy path.
+
+The reference's verify (dryft/engine/decode.py:168-206) runs the current
+token and k draft tokens at consecutive positions through every layer and the
+LM head; its tests require the emitted stream to equal plain greedy decoding
+(dryft/tests/test_speculate.py: accepted prefixes never change the output).
+"""
+import dataclasses
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+BF16 = torch.bfloat16
+LOGIT_ATOL = 0.0625
+
+
+def _verify_rows(engine, state, current, proposal):
+    """Run one verify pass without applying it; returns (predictions, logits)."""
+    from hackthenorth_b200 import _lib
+
+    n = len(proposal) + 1
+    dev = engine.device
+    ids = torch.tensor([current, *proposal], dtype=torch.int64, device=dev)
+    preds = torch.zeros(n, dtype=torch.int64, device=dev)
+    logits = torch.zeros(n, engine.cfg.vocab, dtype=BF16, device=dev)
+    L = _lib.load()
+    _lib.check(L.qb_verify(engine.ctx, ids.data_ptr(), n, state.position.data_ptr(), preds.data_ptr(),
+                           logits.data_ptr(), _lib.stream_handle()), engine.ctx)
+    state.check()
+    return preds.cpu().tolist(), logits.float().cpu()
+
+
+@pytest.mark.parametrize("shape", ["small", "8b-layer"])
+@pytest.mark.parametrize("n_rows", [2, 5, 8])
+def test_verify_rows_match_oracle(built_lib, cpu_threads, shape, n_rows):
+    from hackthenorth_b200.config import QWEN3_8B, QWEN3_SMALL
+    from hackthenorth_b200.engine import Engine
+    from hackthenorth_b200.weights import random_state_dict
+    from oracle.qwen3_oracle import OracleQwen3
+
+    cfg = QWEN3_SMALL if shape == "small" else dataclasses.replace(QWEN3_8B, n_layers=1)
+    state = random_state_dict(cfg, 5)
+    engine = Engine(None, "cuda:0", cfg=cfg, state=state)
+    rng = torch.Generator().manual_seed(17 + n_rows)
+    prompt = torch.randint(0, cfg.vocab, (37,), generator=rng).tolist()
+    drafts = torch.randint(0, cfg.vocab, (n_rows - 1,), generator=rng).tolist()
+    st = engine.new_state(len(prompt), 4, draft_tokens=8)
+    st.prefill(torch.tensor(prompt, device=engine.device))
+    current = st.read_token()[0]
+    preds, logits = _verify_rows(engine, st, current, drafts)
+    assert int(st.position.item()) == len(prompt)  # verify leaves the position to the caller
+
+    o = OracleQwen3(cfg, state, st.capacity)
+    o.forward_rows(prompt, 0)
+    ref, ref_tok = o.forward_rows([current, *drafts], len(prompt))
+    ref = ref.float()
+    d = (logits - ref).abs()
+    assert d.max() <= LOGIT_ATOL and d.mean() <= 0.01, (float(d.max()), float(d.mean()))
+    for i in range(n_rows):
+        if preds[i] != int(ref_tok[i]):
+            top2 = ref[i].topk(2).values
+            assert float(top2[0] - top2[1]) <= LOGIT_ATOL, f"row {i}"
+    # the rows' K/V are in the cache at positions len(prompt) ..
+    p0 = len(prompt)
+    for l in range(cfg.n_layers):
+        torch.testing.assert_close(st.keys[l, :, p0:p0 + n_rows].float().cpu(), o.keys[l, :, p0:p0 + n_rows].float(),
+                                   atol=0.0625, rtol=0.02)
+        torch.testing.assert_close(st.values[l, :, p0:p0 + n_rows].float().cpu(),
+                                   o.values[l, :, p0:p0 + n_rows].float(), atol=0.0625, rtol=0.02)
+
+
+def test_verify_row0_matches_decode_step(built_lib):
+    """Row 0 of a verify pass is the decode step of the same token: same
+    greedy token, logits within LOGIT_ATOL (different summation order)."""
+    from hackthenorth_b200.config import QWEN3_SMALL
+    from hackthenorth_b200.engine import Engine
+
+    engine = Engine.from_random(QWEN3_SMALL, seed=2)
+    prompt = list(range(3, 40))
+    st = engine.new_state(len(prompt), 4, draft_tokens=4, keep_logits=True)
+    st.prefill(torch.tensor(prompt, device=engine.device))
+    current = st.read_token()[0]
+    preds, logits = _verify_rows(engine, st, current, [5, 6, 7])
+    st.step_eager()
+    st.check()
+    assert st.read_token()[0] == preds[0]
+    assert (st.logits.float().cpu() - logits[0]).abs().max() <= LOGIT_ATOL
+
+
+def test_speculative_generate_equals_plain_greedy(built_lib):
+    """Synthetic drafts (target continuation with p = 0.7, else uniform) and
+    prompt lookup: the emitted stream is the golden greedy stream, every
+    length is exact, and proposals were actually verified."""
+    from hackthenorth_b200.config import QWEN3_SMALL
+    from hackthenorth_b200.engine import Engine
+    from hackthenorth_b200.speculate import PromptLookup, SyntheticDraft
+
+    g = np.load(os.path.join(GOLDEN, "qwen3_small_greedy.npz"))
+    prompt, gold = g["prompt"].tolist(), g["tokens"].tolist()
+    engine = Engine.from_random(QWEN3_SMALL, seed=0)
+    for k in (1, 4, 7):
+        draft = SyntheticDraft(gold, QWEN3_SMALL.vocab, p=0.7, seed=3, draft_length=k)
+        out = [s[0] for s in engine.generate([prompt], len(gold), draft_tokens=k, drafter=draft)]
+        assert out == gold, f"k={k}"
+        assert engine.state._verify_n == k + 1
+    # prompt lookup on a repetitive prompt proposes continuations
+    rep = (prompt[:6] * 5)[:30]
+    plain = [s[0] for s in engine.generate([rep], 24)]
+    spec = [s[0] for s in engine.generate([rep], 24, draft_tokens=4, drafter=PromptLookup(rep, draft_length=4))]
+    assert spec == plain
+    for n in (1, 2, 3):
+        assert len(list(engine.generate([rep], n, draft_tokens=4))) == n
+
+
+def test_verify_rejects_bad_arguments(built_lib):
+    from hackthenorth_b200 import _lib
+    from hackthenorth_b200.config import QWEN3_SMALL
+    from hackthenorth_b200.engine import Engine
+
+    engine = Engine.from_random(QWEN3_SMALL, seed=0)
+    st = engine.new_state(8, 4, draft_tokens=8)
+    ids = torch.zeros(9, dtype=torch.int64, device=engine.device)
+    preds = torch.zeros(9, dtype=torch.int64, device=engine.device)
+    L = _lib.load()
+    assert L.qb_verify(engine.ctx, ids.data_ptr(), 9, st.position.data_ptr(), preds.data_ptr(), None,
+                       _lib.stream_handle()) == _lib.QB_ERR_UNSUPPORTED
+    assert L.qb_verify(engine.ctx, ids.data_ptr(), 0, st.position.data_ptr(), preds.data_ptr(), None,
+                       _lib.stream_handle()) == _lib.QB_ERR_UNSUPPORTED
+    assert L.qb_replay_verify(engine.ctx, _lib.stream_handle()) == _lib.QB_ERR_STATE
+    # a verify past the capacity is reported on the device, not faulted
+    st.position.fill_(st.capacity - 2)
+    assert L.qb_verify(engine.ctx, ids.data_ptr(), 5, st.position.data_ptr(), preds.data_ptr(), None,
+                       _lib.stream_handle()) == 0
+    with pytest.raises(ValueError, match="capacity"):
+        st.check()
