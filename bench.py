@@ -435,6 +435,130 @@ def run_attention_sweep(args):
                       "config": {"q_heads": 32, "kv_heads": 8, "head_dim": 128}, "cases": cases}), flush=True)
 
 
+def run_speculative(args):
+    """Speculative decoding line (not the headline): the 8B target verifies
+    k = 4 draft tokens per cycle on one GPU, the 0.6B draft model runs its k
+    decode steps every cycle (timed, its tokens unused), and each draft token is
+    the target's greedy token for the current prefix with seeded Bernoulli(0.7)
+    probability, else uniform (expected 2.773 emitted per cycle).
+
+    The target's greedy continuation comes from its plain decode path. The
+    verify pass sums in a different order, so at a near tie of the plain
+    logits it may pick the other token; the emitted stream then leaves the
+    precomputed continuation, and the harness recomputes the continuation from
+    that point with plain decode steps (untimed), recording the plain top-2
+    margin there. Only the draft + verify cycles are timed (CUDA events on the
+    stream, plus the host read of each cycle's predictions)."""
+    from hackthenorth_b200 import build as qbuild
+    from hackthenorth_b200.config import QWEN3_0P6B, get_config
+    from hackthenorth_b200.engine import Engine
+    from hackthenorth_b200.speculate import SyntheticDraft
+
+    qbuild.build()
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(0)
+    cfg = get_config(args.config)
+    ctx, k, n_out = args.context, 4, 256
+    target = Engine.from_random(cfg, seed=0, device=str(dev), init_device=str(dev))
+    draft = Engine.from_random(QWEN3_0P6B, seed=0, device=str(dev), init_device=str(dev))
+    cap = ctx + 2 * n_out + 2 * k + 8
+    ts = target.new_state(ctx, n_out + 1, draft_tokens=k, capacity=cap, keep_logits=True)
+    ds = draft.new_state(ctx, n_out + 1, draft_tokens=k, capacity=cap)
+    gen = torch.Generator(device=dev).manual_seed(2)
+    for st, c in ((ts, cfg), (ds, QWEN3_0P6B)):
+        for t in (st.keys, st.values):
+            for l in range(c.n_layers):
+                t[l, :, :ctx].normal_(generator=gen)
+    first = 1
+    ts.capture()
+    ds.capture()
+
+    def plain_from(token, position, count):
+        """Plain greedy continuation and each step's top-2 margin (untimed)."""
+        ts.token.fill_(token)
+        ts.position.fill_(position)
+        toks, margins = [], []
+        for _ in range(count):
+            ts.step()
+            toks += ts.read_token()
+            top2 = ts.logits.float().topk(2).values
+            margins.append(float(top2[0] - top2[1]))
+        return toks, margins
+
+    # warm-up of both graphs and the plain timing
+    plain_from(first, ctx, 3)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    plain, plain_margins = plain_from(first, ctx, n_out)
+    plain_s = time.perf_counter() - t0
+    ts.check()
+
+    split_ms = [0.0, 0.0]  # draft steps, verify (+ host read) per run
+
+    def run_spec(timed):
+        drafter = SyntheticDraft([], cfg.vocab, p=0.7, seed=3, draft_length=k)
+        ref, margins = list(plain), list(plain_margins)
+        out, cur, cycles, spent, anchors = [], first, 0, 0.0, []
+        split_ms[0] = split_ms[1] = 0.0
+        ts.token.fill_(first)
+        ts.position.fill_(ctx)
+        stream = torch.cuda.current_stream()
+        while len(out) < n_out:
+            drafter.reference = ref
+            e0, em, e1 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            e0.record(stream)
+            ds.position.fill_(ctx + len(out))  # the draft model follows the accepted prefix
+            for _ in range(k):
+                ds.step()
+            em.record(stream)
+            proposal = drafter.propose(len(out), k)
+            emitted = ts.verify(cur, proposal)
+            e1.record(stream)
+            e1.synchronize()
+            spent += e0.elapsed_time(e1) / 1000.0
+            split_ms[0] += e0.elapsed_time(em)
+            split_ms[1] += em.elapsed_time(e1)
+            cycles += 1
+            base = len(out)
+            out += emitted
+            cur = emitted[-1]
+            bad = next((j for j, tok in enumerate(emitted) if base + j >= len(ref) or ref[base + j] != tok), None)
+            if bad is not None and len(out) < n_out:
+                # re-anchor: the plain continuation after the emitted prefix (untimed)
+                if base + bad < len(margins):
+                    anchors.append(round(margins[base + bad], 4))
+                pos = int(ts.position.item())
+                tail, tail_m = plain_from(cur, pos, n_out - len(out) + k + 1)
+                ref = out + tail
+                margins = margins[:len(out)] + tail_m
+                ts.token.fill_(cur)
+                ts.position.fill_(pos)
+        return out[:n_out], cycles, spent, anchors
+
+    run_spec(False)  # warm-up (captures the verify graph)
+    torch.cuda.synchronize()
+    spec, cycles, spec_s, anchors = run_spec(True)
+    ts.check()
+    ds.check()
+    line = {
+        "metric": "speculative decode tok/s (target verify k=4 + 0.6B draft steps, synthetic p=0.7 drafts)",
+        "value": round(n_out / spec_s, 3), "unit": "tok/s", "n_gpus": 1, "higher_is_better": True,
+        "mode": "speculative", "dtype": "bf16",
+        "data": "synthetic (seeded random-init weights; KV prefix of seeded N(0,1) values; drafts = target "
+                "greedy continuation with Bernoulli(0.7), else uniform, seed 3)",
+        "config": {"workload": f"{cfg.name} target, qwen3-0.6b draft, context {ctx}, k={k}, {n_out} tokens",
+                   "parallelism": "none (the TP8 form of this configuration needs a tensor-parallel verify pass)"},
+        "emitted_per_cycle": round(n_out / cycles, 3), "expected_emitted_per_cycle": 2.773, "cycles": cycles,
+        "plain_tok_s": round(n_out / plain_s, 3), "speedup_vs_plain": round(plain_s / spec_s, 3),
+        "draft_ms_per_cycle": round(split_ms[0] / cycles, 3), "verify_ms_per_cycle": round(split_ms[1] / cycles, 3),
+        "reanchors": len(anchors), "reanchor_plain_top2_margins": anchors,
+        "tokens_equal_plain_greedy": spec == plain,
+        "timing": "sum of per-cycle CUDA-event times (draft steps + verify + the host read of its predictions); "
+                  "re-anchoring after a near-tie disagreement is untimed",
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -478,8 +602,9 @@ def main(argv=None):
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--op", choices=("decode", "attention"), default="decode",
-                    help="attention: the decode-attention op sweep (not the headline line)")
+    ap.add_argument("--op", choices=("decode", "attention", "speculative"), default="decode",
+                    help="attention: the decode-attention op sweep; speculative: verify + draft cycles "
+                         "(neither is the headline line)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: override the layer count (the line is marked profile_only)")
     ap.add_argument("--decode-path", choices=("per-sublayer", "step-kernel"), default="per-sublayer",
@@ -492,6 +617,8 @@ def main(argv=None):
         run_reference(args)
     elif args.op == "attention":
         run_attention_sweep(args)
+    elif args.op == "speculative":
+        run_speculative(args)
     else:
         run_ours(args)
 
