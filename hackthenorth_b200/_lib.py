@@ -48,6 +48,8 @@ SIGNATURES = {
     "qb_replay_decode": (c_int, [c_void_p, c_void_p]),
     "qb_check": (c_int, [c_void_p, c_void_p]),
     "qb_decode_mode": (c_int, [c_void_p]),
+    "qb_gemm_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,
+                             c_void_p]),
     "qb_verify": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
     "qb_capture_verify": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
     "qb_replay_verify": (c_int, [c_void_p, c_void_p]),

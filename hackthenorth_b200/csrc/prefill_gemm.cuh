@@ -1,0 +1,227 @@
+// prefill_gemm.cuh — dense bf16 GEMM for prompt prefill on sm_100a's 5th-gen
+// tensor cores: D[T][N] = X[T][K] . W[N][K]^T with fp32 accumulation in tensor
+// memory (TMEM) and one bf16 rounding, plus the projection epilogues of the
+// decode path (store, + residual, SwiGLU over gate/up-interleaved rows).
+//
+// This is the prefill counterpart of the reference's dense projections
+// (dryft/engine/attention.py:92-98 uses torch linear for prompt rows; the
+// roundings are those of kernels/projection.py:13-83 and down.py:8-35).
+//
+// Per CTA one 128 x 256 output tile (128 prompt rows x 256 weight rows):
+//  * warp 0, one lane: TMA producer. X tile [128 rows][64 cols] and W tile
+//    [256 rows][64 cols] per K block (128-byte swizzle, no multicast) into a
+//    4-stage ring of 48 KB;
+//  * warp 1: allocates 256 TMEM columns (128 lanes x 256 fp32 accumulators);
+//    one lane issues 4 tcgen05.mma.cta_group::1.kind::f16 (M 128, N 256, K 16)
+//    per K block with shared-memory descriptors of both operands (K-major,
+//    128-byte swizzle), and tcgen05.commit frees each stage once its MMAs
+//    have read it; a last commit signals the accumulators complete;
+//  * warps 2-5: each reads its 32 TMEM lanes (32 prompt rows) with
+//    tcgen05.ld.32x32b and runs the epilogue on 8 columns at a time.
+// Every wait is bounded (the kernel records an error and returns), and TMEM is
+// released by warp 1 after all readers are done, on every path.
+#pragma once
+#include "common.cuh"
+
+namespace qb {
+
+constexpr int kPgBM = 128;                       // prompt rows per tile (MMA M)
+constexpr int kPgBN = 256;                       // weight rows per tile (MMA N)
+constexpr int kPgBK = 64;                        // K per stage (one 128-byte swizzle row)
+constexpr int kPgStages = 4;
+constexpr int kPgABytes = kPgBM * kPgBK * 2;     // 16 KB
+constexpr int kPgBBytes = kPgBN * kPgBK * 2;     // 32 KB
+constexpr int kPgStageBytes = kPgABytes + kPgBBytes;
+constexpr int kPgThreads = 6 * 32;
+constexpr int kPgTmemCols = 256;
+
+enum PrefillEpi : int { PG_STORE = 0, PG_RESIDUAL = 1, PG_SWIGLU = 2 };
+
+struct PgArgs {
+  int T, N, K;              // rows of X, rows of W, shared K
+  bf16* out;                // STORE/RESIDUAL: [T][N]; SWIGLU: [T][N/2]
+  const bf16* residual;     // RESIDUAL: [T][N]
+  int* err;
+};
+
+__host__ inline size_t pg_smem_bytes() { return 1024 + (size_t)kPgStages * kPgStageBytes + 256; }
+
+// Shared-memory matrix descriptor, K-major operand with 128-byte swizzle:
+// start address >> 4 at [0,14), leading byte offset (unused for swizzled
+// K-major, 1) at [16,30), stride byte offset between 8-row groups (1024 B) >> 4
+// at [32,46), descriptor version 1 at [46,48), layout type 2 (128-byte
+// swizzle) at [61,64).
+__device__ __forceinline__ uint64_t pg_desc(const void* smem_tile) {
+  const uint64_t addr = smem_u32(smem_tile);
+  return ((addr >> 4) & 0x3FFFull) | (1ull << 16) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor of kind::f16: fp32 accumulator, bf16 A and B, both
+// K-major, N >> 3 at [17,23), M >> 4 at [24,29).
+__host__ __device__ constexpr uint32_t pg_idesc(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+      ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(kPgThreads, 1)
+    prefill_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
+                        const PgArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + kPgStages * kPgStageBytes);
+  uint64_t* empty = full + kPgStages;
+  uint64_t* done = empty + kPgStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * kPgBM;
+  const int n0 = blockIdx.y * kPgBN;
+  const int nkb = (a.K + kPgBK - 1) / kPgBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPgStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(done, 1);
+    fence_mbar_init();
+    flags[0] = 0;
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kPgTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  pdl_wait();  // X is written by the previous kernel
+  pdl_trigger();
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    if (lane == 0) {
+      prefetch_tensormap(&tmx);
+      prefetch_tensormap(&tmw);
+      int issued = 0;
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % kPgStages;
+        if (kb >= kPgStages &&
+            !mbar_wait(&empty[s], ((kb / kPgStages) - 1) & 1, a.err, DEV_TIMEOUT_GEMV_EMPTY)) {
+          flags[0] = 1;
+          break;
+        }
+        uint8_t* st = ring + s * kPgStageBytes;
+        mbar_arrive_expect_tx(&full[s], kPgStageBytes);
+        tma_load_2d(st, &tmx, kb * kPgBK, m0, &full[s]);
+        tma_load_2d(st + kPgABytes, &tmw, kb * kPgBK, n0, &full[s]);
+        issued = kb + 1;
+      }
+      // keep shared memory alive until every issued copy has landed
+      for (int kb = (issued > kPgStages ? issued - kPgStages : 0); kb < issued; ++kb)
+        mbar_wait(&full[kb % kPgStages], (kb / kPgStages) & 1, nullptr, 0);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = pg_idesc(kPgBM, kPgBN);
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % kPgStages;
+        if (!mbar_wait(&full[s], (kb / kPgStages) & 1, a.err, DEV_TIMEOUT_GEMV_FULL)) {
+          flags[0] = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint8_t* st = ring + s * kPgStageBytes;
+        const uint64_t ad = pg_desc(st), bd = pg_desc(st + kPgABytes);
+#pragma unroll
+        for (int k = 0; k < kPgBK / 16; ++k)  // K 16 per MMA = 32 bytes along the swizzled row
+          tc_mma(tmem, ad + (uint64_t)(k * 2), bd + (uint64_t)(k * 2), idesc, (kb | k) != 0 ? 1u : 0u);
+        tc_commit(&empty[s]);  // the stage is free once these MMAs have read it
+      }
+      tc_commit(done);  // all issued MMAs complete (also after an early stop)
+    }
+    __syncwarp();
+  } else {
+    // --------------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lanes 32q .. 32q+31
+    const int row = m0 + 32 * q + lane;
+    const bool ok = mbar_wait(done, 0, a.err, DEV_TIMEOUT_ATTN_FULL) && flags[0] == 0;
+    tc_fence_after();
+    if (ok) {
+      for (int c = 0; c < kPgBN; c += 8) {
+        float v[8];
+        tc_ld8(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c, v);
+        const int n = n0 + c;
+        if (row >= a.T || n >= a.N) continue;
+        if constexpr (EPI == PG_STORE) {
+          uint4 o;
+          o.x = pack_bf16(v[0], v[1]);
+          o.y = pack_bf16(v[2], v[3]);
+          o.z = pack_bf16(v[4], v[5]);
+          o.w = pack_bf16(v[6], v[7]);
+          *reinterpret_cast<uint4*>(a.out + (size_t)row * a.N + n) = o;
+        } else if constexpr (EPI == PG_RESIDUAL) {
+          const uint4 r = *reinterpret_cast<const uint4*>(a.residual + (size_t)row * a.N + n);
+          const uint32_t* pr = reinterpret_cast<const uint32_t*>(&r);
+          uint4 o;
+          uint32_t* po = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            po[j] = pack_bf16(round_bf16(v[2 * j]) + bf_lo(pr[j]), round_bf16(v[2 * j + 1]) + bf_hi(pr[j]));
+          *reinterpret_cast<uint4*>(a.out + (size_t)row * a.N + n) = o;
+        } else {  // PG_SWIGLU: columns (2j, 2j+1) = (gate j, up j)
+          float h[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float act = round_bf16(silu_f32(round_bf16(v[2 * j])));
+            h[j] = act * round_bf16(v[2 * j + 1]);
+          }
+          uint2 o;
+          o.x = pack_bf16(h[0], h[1]);
+          o.y = pack_bf16(h[2], h[3]);
+          *reinterpret_cast<uint2*>(a.out + (size_t)row * (a.N / 2) + n / 2) = o;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPgTmemCols) : "memory");
+  }
+}
+
+}  // namespace qb

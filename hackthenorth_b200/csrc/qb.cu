@@ -27,6 +27,7 @@
 #include "step_kernel.cuh"
 #include "gemv_rows.cuh"
 #include "verify_attention.cuh"
+#include "prefill_gemm.cuh"
 #include "common.cuh"
 #include "gemv.cuh"
 
@@ -210,6 +211,47 @@ bool make_kv_map(CUtensorMap* m, const void* base, int hkv, int cap, int rows = 
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Tensor map over a row-major [rows][cols] bf16 matrix, box [box_rows][64
+// cols], 128-byte swizzle (the K-major operand tiles of the prefill GEMM).
+bool make_rows_map(CUtensorMap* m, const void* base, long long rows, long long cols, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (cols * 2) % 16 != 0) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// D[T][N] = X[T][K] . W[N][K]^T on tcgen05 (prefill_gemm_kernel).
+cudaError_t launch_prefill_gemm(int epi, const bf16* x, const bf16* w, bf16* out, const bf16* residual, int T, int N,
+                                int K, int* err, cudaStream_t st) {
+  CUtensorMap tx, tw;
+  if (!make_rows_map(&tx, x, T, K, kPgBM) || !make_rows_map(&tw, w, N, K, kPgBN)) return cudaErrorInvalidValue;
+  PgArgs a;
+  a.T = T;
+  a.N = N;
+  a.K = K;
+  a.out = out;
+  a.residual = residual;
+  a.err = err;
+  const size_t smem = pg_smem_bytes();
+  static bool attr[3] = {false, false, false};
+  void (*k)(const CUtensorMap, const CUtensorMap, const PgArgs) =
+      epi == PG_STORE ? prefill_gemm_kernel<PG_STORE> : epi == PG_RESIDUAL ? prefill_gemm_kernel<PG_RESIDUAL>
+                                                                           : prefill_gemm_kernel<PG_SWIGLU>;
+  if (!attr[epi]) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    attr[epi] = true;
+  }
+  const dim3 grid((T + kPgBM - 1) / kPgBM, (N + kPgBN - 1) / kPgBN);
+  return launch_ex(k, grid, dim3(kPgThreads), smem, st, tx, tw, a);
 }
 
 int attn_splits_for(int hkv, int sm_count) {
@@ -1363,6 +1405,22 @@ int qb_check(qb_ctx* c, void* stream) {
       return cuda_fail(&c->msg, e, "step epoch advance");
   }
   return rc;
+}
+
+int qb_gemm_bf16(const void* x, const void* w, void* out, const void* residual, int T, int N, int K, int epilogue,
+                 void* scratch, void* stream) {
+  if (!ptr_ok(x) || !ptr_ok(w) || !ptr_ok(out) || !ptr_ok(scratch))
+    return set_err(nullptr, QB_ERR_ARG, "x, w, out and scratch must be 16-byte aligned device pointers");
+  if (T <= 0 || N <= 0 || K <= 0 || K % 64 != 0 || N % 16 != 0)
+    return set_err(nullptr, QB_ERR_UNSUPPORTED, "K must be a multiple of 64 and N of 16");
+  if (epilogue < 0 || epilogue > 2) return set_err(nullptr, QB_ERR_ARG, "epilogue must be 0, 1 or 2");
+  if (epilogue == 1 && !ptr_ok(residual)) return set_err(nullptr, QB_ERR_ARG, "residual must be an aligned pointer");
+  int* err = reinterpret_cast<int*>(static_cast<uint8_t*>(scratch) + kScrErr);
+  cudaError_t e = launch_prefill_gemm(epilogue, static_cast<const bf16*>(x), static_cast<const bf16*>(w),
+                                      static_cast<bf16*>(out), static_cast<const bf16*>(residual), T, N, K, err,
+                                      static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, "gemm launch");
+  return QB_OK;
 }
 
 int qb_decode_mode(const qb_ctx* c) {

@@ -158,6 +158,17 @@ int qb_decode_mode(const qb_ctx* ctx);
 
 /* ---- op-level entry points (the reference's kernel wrappers) ------------- */
 
+/* Prefill projection on tcgen05 tensor cores: out = epilogue(x . w^T) for
+ * x [T][K], w [N][K] bf16 row-major, fp32 accumulation, one bf16 rounding
+ * (the dense prompt-row projections of dryft/engine/attention.py:92-98 with the
+ * roundings of kernels/projection.py:13-83). epilogue 0: out [T][N] = bf16(y);
+ * 1: out = bf16(bf16(y) + residual) (residual [T][N]); 2: out [T][N/2] =
+ * bf16(bf16(silu(bf16 y[2j])) * bf16 y[2j+1]) over gate/up-interleaved rows.
+ * K multiple of 64, N multiple of 16. scratch: qb_op_scratch_bytes() bytes
+ * (device error word). */
+int qb_gemm_bf16(const void* x, const void* w, void* out, const void* residual, int T, int N, int K,
+                 int epilogue, void* scratch, void* stream);
+
 /* RMSNorm(x; gain, eps) fused with y = W . x, fp32 accumulation, one bf16
  * rounding. gain == NULL skips the norm. swiglu != 0: W is [2N, K] with gate
  * and up rows interleaved and y[j] = bf16(bf16(silu(gate_j)) * up_j).
