@@ -408,7 +408,8 @@ __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const RowsAr
 
 // Per-head q/k RMSNorm + RoPE for Q consecutive positions, K/V appended to the
 // cache (dryft/engine/kernels/fused.py:9-30,47-82 with several rows). One warp
-// per (row, head); also writes the rows' positions for the attention kernel.
+// per (row, head); also writes the rows' positions for the attention kernel
+// (verify) when asked. Used for the verify rows and for prompt rows.
 struct RopeRowsArgs {
   const bf16* qkv;        // [Q][Hq*D + 2*Hkv*D]
   const bf16* q_norm;
@@ -416,8 +417,9 @@ struct RopeRowsArgs {
   const bf16* cos;
   const bf16* sin;
   float eps;
-  const int64_t* pos;     // first position
-  int64_t* positions;     // [Q] out
+  const int64_t* pos;     // first position (device), or NULL: p0
+  int p0;
+  int64_t* positions;     // [Q] out, or NULL
   bf16* q_out;            // [Q][Hq][D]
   bf16* k_cache;          // this layer's [Hkv][cap][D]
   bf16* v_cache;
@@ -463,13 +465,13 @@ __global__ void __launch_bounds__(128) rope_rows_kernel(const RopeRowsArgs a) {
   const int heads = a.Hq + 2 * a.Hkv;
   if (gw >= a.Q * heads) return;
   const int q = gw / heads, h = gw - q * heads;
-  const long long p0 = *a.pos;
+  const long long p0 = a.pos ? *a.pos : (long long)a.p0;
   const long long pos = p0 + q;
   if (p0 < 0 || p0 + a.Q > a.cap) {
     if (gw == 0 && lane == 0) report_error(a.err, DEV_BAD_POSITION);
     return;
   }
-  if (gw == 0 && lane < a.Q) a.positions[lane] = p0 + lane;
+  if (a.positions != nullptr && gw == 0 && lane < a.Q) a.positions[lane] = p0 + lane;
   const bf16* src = a.qkv + (size_t)q * heads * kAttnD + (size_t)h * kAttnD;
   const bf16* cos_row = a.cos + (size_t)pos * kAttnD;
   const bf16* sin_row = a.sin + (size_t)pos * kAttnD;

@@ -28,6 +28,7 @@
 #include "gemv_rows.cuh"
 #include "verify_attention.cuh"
 #include "prefill_gemm.cuh"
+#include "prefill_attention.cuh"
 #include "common.cuh"
 #include "gemv.cuh"
 
@@ -996,6 +997,137 @@ int run_verify(qb_ctx* c, const int64_t* ids, int n, const int64_t* pos, int64_t
   return QB_OK;
 }
 
+// Batched prefill scratch: per prompt row xa, xb, xn [H]; qkv; q, attn [Hq*D];
+// act [F] (bf16).
+struct PrefillLayout {
+  size_t xa, xb, xn, qkv, q, attn, act, total;
+};
+PrefillLayout prefill_layout(const qb_ctx* c, int n) {
+  const qb_config& g = c->lc;
+  const size_t T = (size_t)n;
+  const size_t nqkv = (size_t)(g.n_heads + 2 * g.n_kv_heads) * g.head_dim;
+  PrefillLayout L;
+  size_t o = 0;
+  L.xa = o; o = align_up(o + T * g.hidden * 2, 256);
+  L.xb = o; o = align_up(o + T * g.hidden * 2, 256);
+  L.xn = o; o = align_up(o + T * g.hidden * 2, 256);
+  L.qkv = o; o = align_up(o + T * nqkv * 2, 256);
+  L.q = o; o = align_up(o + T * g.n_heads * g.head_dim * 2, 256);
+  L.attn = o; o = align_up(o + T * g.n_heads * g.head_dim * 2, 256);
+  L.act = o; o = align_up(o + T * g.ffn * 2, 256);
+  L.total = o;
+  return L;
+}
+
+// Prompt rows ids[0..n) at positions 0..n-1 through every layer as dense
+// blocks (tcgen05 GEMMs, causal flash attention), K/V appended; the last row
+// through the LM head; *position = n (DecodeState.prefill,
+// dryft/engine/decode.py:157-166, dryft/engine/prefill.py:6-26).
+int run_prefill_batched(qb_ctx* c, const int64_t* ids, int n, uint8_t* scratch, int64_t* tok_out, int64_t* pos,
+                        void* logits, cudaStream_t st) {
+  const qb_config& g = c->lc;
+  const int H = g.hidden, D = g.head_dim;
+  const int nqkv = (g.n_heads + 2 * g.n_kv_heads) * D;
+  const PrefillLayout P = prefill_layout(c, n);
+  bf16* xa = reinterpret_cast<bf16*>(scratch + P.xa);
+  bf16* xb = reinterpret_cast<bf16*>(scratch + P.xb);
+  bf16* xn = reinterpret_cast<bf16*>(scratch + P.xn);
+  bf16* qkv = reinterpret_cast<bf16*>(scratch + P.qkv);
+  bf16* q = reinterpret_cast<bf16*>(scratch + P.q);
+  bf16* attn = reinterpret_cast<bf16*>(scratch + P.attn);
+  bf16* act = reinterpret_cast<bf16*>(scratch + P.act);
+  cudaError_t e;
+  auto norm = [&](const bf16* x, const bf16* gain, bool gather) {
+    NormRowsArgs na;
+    std::memset(&na, 0, sizeof(na));
+    na.x = gather ? nullptr : x;
+    na.embed = c->embed;
+    na.ids = ids;
+    na.vocab = c->cfg.vocab;
+    na.x_out = xa;
+    na.gain = gain;
+    na.xn = xn;
+    na.K = H;
+    na.eps = g.rms_eps;
+    na.err = c->err;
+    return launch_ex(norm_rows_kernel, dim3(n), dim3(128), 0, st, na);
+  };
+  for (int l = 0; l < g.n_layers; ++l) {
+    const qb_layer_weights& w = c->layers[l];
+    if ((e = norm(xa, static_cast<const bf16*>(w.input_norm), l == 0)) != cudaSuccess)
+      return cuda_fail(&c->msg, e, "prefill norm");
+    if ((e = launch_prefill_gemm(PG_STORE, xn, static_cast<const bf16*>(w.qkv), qkv, nullptr, n, nqkv, H, c->err,
+                                 st)) != cudaSuccess)
+      return cuda_fail(&c->msg, e, "prefill qkv");
+    RopeRowsArgs ra;
+    std::memset(&ra, 0, sizeof(ra));
+    ra.qkv = qkv;
+    ra.q_norm = static_cast<const bf16*>(w.q_norm);
+    ra.k_norm = static_cast<const bf16*>(w.k_norm);
+    ra.cos = c->cos;
+    ra.sin = c->sin;
+    ra.eps = g.rms_eps;
+    ra.pos = nullptr;
+    ra.p0 = 0;
+    ra.positions = nullptr;
+    ra.q_out = q;
+    const size_t layer_off = (size_t)l * g.n_kv_heads * c->cap * D;
+    ra.k_cache = c->kc + layer_off;
+    ra.v_cache = c->vc + layer_off;
+    ra.err = c->err;
+    ra.Q = n;
+    ra.Hq = g.n_heads;
+    ra.Hkv = g.n_kv_heads;
+    ra.cap = c->cap;
+    const long long warps = (long long)n * (g.n_heads + 2 * g.n_kv_heads);
+    if ((e = launch_ex(rope_rows_kernel, dim3((unsigned)((warps + 3) / 4)), dim3(128), 0, st, ra)) != cudaSuccess)
+      return cuda_fail(&c->msg, e, "prefill rope");
+    FpArgs fa;
+    fa.q = q;
+    fa.out = attn;
+    fa.T = n;
+    fa.p0 = 0;
+    fa.Hq = g.n_heads;
+    fa.Hkv = g.n_kv_heads;
+    fa.cap = c->cap;
+    fa.err = c->err;
+    static bool fp_attr = false;
+    if (!fp_attr) {
+      if ((e = cudaFuncSetAttribute(flash_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    (int)fp_smem_bytes())) != cudaSuccess)
+        return cuda_fail(&c->msg, e, "prefill attention attribute");
+      fp_attr = true;
+    }
+    if ((e = launch_ex(flash_prefill_kernel, dim3((n + kFpRows - 1) / kFpRows, g.n_heads), dim3(kFpThreads),
+                       fp_smem_bytes(), st, c->tmk[l], c->tmv[l], fa)) != cudaSuccess)
+      return cuda_fail(&c->msg, e, "prefill attention");
+    if ((e = launch_prefill_gemm(PG_RESIDUAL, attn, static_cast<const bf16*>(w.o), xb, xa, n, H, g.n_heads * D,
+                                 c->err, st)) != cudaSuccess)
+      return cuda_fail(&c->msg, e, "prefill o");
+    if ((e = norm(xb, static_cast<const bf16*>(w.post_norm), false)) != cudaSuccess)
+      return cuda_fail(&c->msg, e, "prefill norm");
+    if ((e = launch_prefill_gemm(PG_SWIGLU, xn, static_cast<const bf16*>(w.gate_up), act, nullptr, n, 2 * g.ffn, H,
+                                 c->err, st)) != cudaSuccess)
+      return cuda_fail(&c->msg, e, "prefill gate/up");
+    if ((e = launch_prefill_gemm(PG_RESIDUAL, act, static_cast<const bf16*>(w.down), xa, xb, n, H, g.ffn, c->err,
+                                 st)) != cudaSuccess)
+      return cuda_fail(&c->msg, e, "prefill down");
+  }
+  // The last row through the final norm, the LM head and the argmax.
+  GemvArgs a = gemv_args(c->lm_head, H, g.vocab, xa + (size_t)(n - 1) * H, nullptr, c->err);
+  a.gain = c->final_norm;
+  a.eps = g.rms_eps;
+  a.logits = static_cast<bf16*>(logits);
+  a.part_val = c->head_val;
+  a.part_idx = c->head_idx;
+  a.counter = c->counters + 64;
+  a.token_out = tok_out;
+  if ((e = launch_gemv<EPI_ARGMAX>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "prefill head");
+  if ((e = launch_ex(set_i64_kernel, dim3(1), dim3(1), 0, st, pos, (long long)n)) != cudaSuccess)
+    return cuda_fail(&c->msg, e, "prefill position");
+  return QB_OK;
+}
+
 int check_verify_args(qb_ctx* c, const int64_t* ids, int n, const int64_t* pos, const int64_t* preds) {
   if (!ids || !pos || !preds) return set_err(&c->msg, QB_ERR_ARG, "ids/position/predictions are NULL");
   if (n < 1 || n > kRowsMaxQ) return set_err(&c->msg, QB_ERR_UNSUPPORTED, "verify takes 1..8 rows");
@@ -1277,6 +1409,26 @@ int qb_prefill(qb_ctx* c, const int64_t* ids, int n, int64_t* token, int64_t* po
     if (rc) return rc;
   }
   return QB_OK;
+}
+
+int qb_prefill_scratch_bytes(const qb_ctx* c, int n, size_t* bytes) {
+  if (!c || !bytes) return set_err(nullptr, QB_ERR_ARG, "NULL argument");
+  if (n <= 0) return set_err(nullptr, QB_ERR_ARG, "n must be positive");
+  *bytes = prefill_layout(c, n).total;
+  return QB_OK;
+}
+
+int qb_prefill_batched(qb_ctx* c, const int64_t* ids, int n, void* scratch, size_t scratch_bytes, int64_t* token,
+                       int64_t* position, void* logits_out, void* stream) {
+  int rc = require_ready(c);
+  if (rc) return rc;
+  if (!ids || !token || !position || n <= 0) return set_err(&c->msg, QB_ERR_ARG, "bad prefill arguments");
+  if (n > c->cap) return set_err(&c->msg, QB_ERR_CAPACITY, "prompt longer than the KV capacity");
+  if (c->tp_size != 1) return set_err(&c->msg, QB_ERR_UNSUPPORTED, "batched prefill runs on one GPU");
+  if (!ptr_ok(scratch) || scratch_bytes < prefill_layout(c, n).total)
+    return set_err(&c->msg, QB_ERR_ARG, "scratch smaller than qb_prefill_scratch_bytes(n) or unaligned");
+  return run_prefill_batched(c, ids, n, static_cast<uint8_t*>(scratch), token, position, logits_out,
+                             static_cast<cudaStream_t>(stream));
 }
 
 int qb_capture_decode(qb_ctx* c, int64_t* token, int64_t* position, void* logits_out, void* stream) {

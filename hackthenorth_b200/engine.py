@@ -76,9 +76,15 @@ class DecodeState:
         self.captured = False
 
     # -- the four entry points --------------------------------------------------
-    def prefill(self, ids: torch.Tensor) -> torch.Tensor:
+    # Prompts of at least this many rows run as dense blocks (tensor-core
+    # GEMMs and flash attention); shorter ones through the decode kernels.
+    BATCHED_PREFILL_MIN = 64
+
+    def prefill(self, ids: torch.Tensor, batched: Optional[bool] = None) -> torch.Tensor:
         """Write K/V for the prompt, emit the first token into ``self.token``
-        and set ``position = len(prompt)``."""
+        and set ``position = len(prompt)``. ``batched`` forces (True) or
+        forbids (False) the dense-block path; by default it is used for
+        prompts of ``BATCHED_PREFILL_MIN`` rows or more on one GPU."""
         n = ids.numel()
         if n > self.capacity:
             raise ValueError("prompt longer than the KV capacity")
@@ -86,9 +92,23 @@ class DecodeState:
             self.prompt = torch.zeros(n, dtype=torch.int64, device=self.token.device)
         self.prompt[:n].copy_(ids.reshape(-1), non_blocking=True)
         self._ensure_bound()
-        _lib.check(_lib.load().qb_prefill(self.engine.ctx, self.prompt.data_ptr(), n, self.token.data_ptr(),
-                                          self.position.data_ptr(), _lib.ptr(self.logits), _lib.stream_handle()),
-                   self.engine.ctx)
+        L = _lib.load()
+        if batched is None:
+            batched = n >= self.BATCHED_PREFILL_MIN and self.engine.tp_size == 1
+        if batched:
+            need = _lib.c_size_t()
+            _lib.check(L.qb_prefill_scratch_bytes(self.engine.ctx, n, _lib.ctypes.byref(need)), self.engine.ctx)
+            scratch = getattr(self, "_prefill_scratch", None)
+            if scratch is None or scratch.numel() < need.value:
+                self._prefill_scratch = scratch = torch.empty(need.value, dtype=torch.uint8,
+                                                              device=self.token.device)
+            _lib.check(L.qb_prefill_batched(self.engine.ctx, self.prompt.data_ptr(), n, scratch.data_ptr(),
+                                            scratch.numel(), self.token.data_ptr(), self.position.data_ptr(),
+                                            _lib.ptr(self.logits), _lib.stream_handle()), self.engine.ctx)
+        else:
+            _lib.check(L.qb_prefill(self.engine.ctx, self.prompt.data_ptr(), n, self.token.data_ptr(),
+                                    self.position.data_ptr(), _lib.ptr(self.logits), _lib.stream_handle()),
+                       self.engine.ctx)
         return self.token
 
     def capture(self) -> None:

@@ -123,6 +123,16 @@ int qb_decode_step(qb_ctx* ctx, int64_t* token, int64_t* position, void* logits_
 int qb_prefill(qb_ctx* ctx, const int64_t* ids, int n, int64_t* token, int64_t* position,
                void* logits_out, void* stream);
 
+/* Batched prefill: the prompt rows as dense blocks (tcgen05 projection GEMMs,
+ * causal flash attention), the path the reference takes for prompt rows
+ * (dryft/engine/attention.py:92-98, dryft/engine/prefill.py:6-26). Same
+ * contract as qb_prefill (K/V for positions 0..n-1, first token to *token,
+ * *position = n); scratch: a device buffer of qb_prefill_scratch_bytes(n)
+ * bytes (prompt-row activations). Single GPU (tp_size 1). */
+int qb_prefill_scratch_bytes(const qb_ctx* ctx, int n, size_t* bytes);
+int qb_prefill_batched(qb_ctx* ctx, const int64_t* ids, int n, void* scratch, size_t scratch_bytes,
+                       int64_t* token, int64_t* position, void* logits_out, void* stream);
+
 /* Capture qb_decode_step(token, position, logits_out) into a CUDA graph owned
  * by ctx (dryft/engine/decode.py:140-155), and replay it. */
 int qb_capture_decode(qb_ctx* ctx, int64_t* token, int64_t* position, void* logits_out,

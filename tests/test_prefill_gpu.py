@@ -90,3 +90,70 @@ def test_gemm_throughput_report(built_lib):
     tflops = 2 * T * N * K / ms / 1e9
     print(f"prefill GEMM {T}x{N}x{K}: {ms:.3f} ms, {tflops:.1f} TFLOP/s")
     assert tflops > 50
+
+
+LOGIT_ATOL = 0.0625
+
+
+@pytest.mark.parametrize("shape,T", [("small", 64), ("small", 300), ("8b-layer", 64), ("8b-layer", 700)])
+def test_batched_prefill_matches_oracle(built_lib, cpu_threads, shape, T):
+    """Prompt rows as dense blocks (tcgen05 GEMMs + causal flash attention):
+    last-row logits within LOGIT_ATOL of the oracle, the first token equal
+    unless the oracle holds a near tie, every appended K/V row within bf16
+    rounding, position = T."""
+    import dataclasses
+
+    from hackthenorth_b200.config import QWEN3_8B, QWEN3_SMALL
+    from hackthenorth_b200.engine import Engine
+    from hackthenorth_b200.weights import random_state_dict
+    from oracle.qwen3_oracle import OracleQwen3
+
+    cfg = QWEN3_SMALL if shape == "small" else dataclasses.replace(QWEN3_8B, n_layers=1)
+    state = random_state_dict(cfg, 9)
+    engine = Engine(None, DEV, cfg=cfg, state=state)
+    prompt = torch.randint(0, cfg.vocab, (T,), generator=torch.Generator().manual_seed(T)).tolist()
+    st = engine.new_state(T, 4, keep_logits=True)
+    st.prefill(torch.tensor(prompt, device=DEV), batched=True)
+    st.check()
+    assert int(st.position.item()) == T
+    o = OracleQwen3(cfg, state, st.capacity)
+    ref, ref_tok = o.forward_rows(prompt, 0)
+    last = ref[-1].float()
+    d = (st.logits.float().cpu() - last).abs()
+    assert d.max() <= LOGIT_ATOL and d.mean() <= 0.01, (float(d.max()), float(d.mean()))
+    if st.read_token()[0] != int(ref_tok[-1]):
+        top2 = last.topk(2).values
+        assert float(top2[0] - top2[1]) <= LOGIT_ATOL
+    for l in range(cfg.n_layers):
+        torch.testing.assert_close(st.keys[l, :, :T].float().cpu(), o.keys[l, :, :T].float(), atol=0.0625, rtol=0.02)
+        torch.testing.assert_close(st.values[l, :, :T].float().cpu(), o.values[l, :, :T].float(), atol=0.0625,
+                                   rtol=0.02)
+
+
+def test_batched_prefill_then_decode_matches_row_prefill(built_lib):
+    """The same 200-token prompt prefilled as dense blocks and row by row: the
+    same first token and 16 decode tokens (up to a near tie of the row path's
+    logits), logits within LOGIT_ATOL."""
+    from hackthenorth_b200.config import QWEN3_SMALL
+    from hackthenorth_b200.engine import Engine
+
+    engine = Engine.from_random(QWEN3_SMALL, seed=0)
+    prompt = torch.randint(0, QWEN3_SMALL.vocab, (200,), generator=torch.Generator().manual_seed(4)).tolist()
+    runs = {}
+    for batched in (True, False):
+        st = engine.new_state(len(prompt), 17, keep_logits=True)
+        st.prefill(torch.tensor(prompt, device=DEV), batched=batched)
+        toks, logits = st.read_token(), [st.logits.float().cpu().clone()]
+        for _ in range(16):
+            st.step()
+            toks += st.read_token()
+            logits.append(st.logits.float().cpu().clone())
+        st.check()
+        runs[batched] = (toks, torch.stack(logits))
+    (ta, la), (tb, lb) = runs[True], runs[False]
+    for i in range(len(ta)):
+        assert (la[i] - lb[i]).abs().max() <= LOGIT_ATOL, f"step {i}"
+        if ta[i] != tb[i]:
+            top2 = lb[i].topk(2).values
+            assert float(top2[0] - top2[1]) <= LOGIT_ATOL
+            break
