@@ -78,7 +78,7 @@ class DecodeState:
     # -- the four entry points --------------------------------------------------
     # Prompts of at least this many rows run as dense blocks (tensor-core
     # GEMMs and flash attention); shorter ones through the decode kernels.
-    BATCHED_PREFILL_MIN = 64
+    BATCHED_PREFILL_MIN = 8
 
     def prefill(self, ids: torch.Tensor, batched: Optional[bool] = None) -> torch.Tensor:
         """Write K/V for the prompt, emit the first token into ``self.token``
