@@ -273,17 +273,35 @@ def run_ours(args):
     ctx = args.context
     total_steps = args.warmup + args.steps
     state = engine.new_state(ctx, total_steps + 2, capacity=ctx + 2 * total_steps + 8)
-    gen = torch.Generator(device=dev).manual_seed(2)
-    for t in (state.keys, state.values):
-        for l in range(cfg.n_layers):
-            t[l, :, :ctx].normal_(generator=gen)
-    state.token.fill_(1)
+    prefill_ms = None
+    if args.real_prefill and world == 1:
+        # the configuration's random prompt (seed 1) prefilled as dense blocks,
+        # timed with CUDA events after one untimed prefill of the same prompt
+        prompt = torch.randint(0, cfg.vocab, (ctx,), generator=torch.Generator().manual_seed(1)).to(dev)
+        state.prefill(prompt)
+        state.check()
+        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        p0.record()
+        state.prefill(prompt)
+        p1.record()
+        torch.cuda.synchronize()
+        state.check()
+        prefill_ms = p0.elapsed_time(p1)
+        first_token = state.read_token()[0]
+    else:
+        gen = torch.Generator(device=dev).manual_seed(2)
+        for t in (state.keys, state.values):
+            for l in range(cfg.n_layers):
+                t[l, :, :ctx].normal_(generator=gen)
+        first_token = 1
+    state.token.fill_(first_token)
     state.position.fill_(ctx)
     state.capture()
     stream = torch.cuda.current_stream()
     for _ in range(args.warmup):
         state.step()
     state.check()
+    state.token.fill_(first_token)
     state.position.fill_(ctx)
     torch.cuda.synchronize()
 
@@ -305,7 +323,7 @@ def run_ours(args):
     # e2e: the same steps with host buffers (pinned H2D of the token, replay,
     # D2H of the result, sync) — the per-token loop of generate().
     state.position.fill_(ctx)
-    host_in = torch.tensor([1], dtype=torch.int64).pin_memory()
+    host_in = torch.tensor([first_token], dtype=torch.int64).pin_memory()
     host_out = torch.empty(1, dtype=torch.int64).pin_memory()
     torch.cuda.synchronize()
     barrier(world)
@@ -345,7 +363,9 @@ def run_ours(args):
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic (seeded random-init weights N(0,0.02); KV cache of seeded N(0,1) positions)",
+        "data": ("synthetic (seeded random-init weights N(0,0.02); context = a real prefill of a seeded "
+                 "random prompt)" if prefill_ms is not None else
+                 "synthetic (seeded random-init weights N(0,0.02); KV cache of seeded N(0,1) positions)"),
         "config": {"workload": f"{cfg.name}-shaped batch-1 greedy decode at context {ctx}",
                    "model": cfg.name, "global_batch": 1, "seq_len": ctx, "context": ctx,
                    "parallelism": "none" if world == 1 else (
@@ -368,6 +388,7 @@ def run_ours(args):
                 "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
                 "d2h_bytes_per_step": host_out.numel() * host_out.element_size()},
         "gpu_launches": launches_per_step * args.steps,
+        "prefill_ms": None if prefill_ms is None else round(prefill_ms, 3),
         "profile_only": bool(args.layers),
         "clocks": clk,
     }
@@ -607,6 +628,9 @@ def main(argv=None):
                          "(neither is the headline line)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: override the layer count (the line is marked profile_only)")
+    ap.add_argument("--real-prefill", action="store_true",
+                    help="fill the context with a real prefill of a seeded random prompt (timed, reported as "
+                         "prefill_ms) instead of seeded random K/V values")
     ap.add_argument("--decode-path", choices=("per-sublayer", "step-kernel"), default="per-sublayer",
                     help="step-kernel: the opt-in persistent one-launch-per-step kernel (single GPU)")
     args = ap.parse_args(argv)
