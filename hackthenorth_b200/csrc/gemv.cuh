@@ -32,6 +32,7 @@ constexpr int kGemvThreads = kGemvConsumers + 32;
 // producer lanes in parallel.
 __host__ __device__ inline int gemv_stage_bytes(int kc) { return kGemvConsumerWarps * kc * 2; }
 constexpr int kGemvBarrierId = 1;  // named barrier of the consumer threads
+constexpr int kGemvL2Ahead = 2;    // stages of the next GEMV brought into L2 by each CTA
 
 enum GemvEpilogue : int { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3, EPI_PARTIAL = 4 };
 
@@ -90,6 +91,12 @@ struct GemvArgs {
   int stages;           // ring stages
   int max_rows;         // max rows any CTA owns (size of rowsum)
   int kc;               // columns per row piece: 1024 or 2048
+  // The next GEMV of the chain (weights [nx_rows][nx_K], nx_rpu rows per unit,
+  // pieces of nx_kc columns): once this CTA has issued its last stage it asks
+  // L2 for the first stages of the rows the same CTA index streams next, so
+  // they come from L2 across the kernel boundary. NULL: nothing to prefetch.
+  const bf16* nx_w;
+  int nx_K, nx_rows, nx_rpu, nx_kc, nx_grid;
 };
 
 __host__ __device__ inline int gemv_rows_per_unit(int epi) { return epi == EPI_SWIGLU ? 2 : 1; }
@@ -193,6 +200,26 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
         bulk_g2s(ring + (size_t)s * stage_bytes + lane * (KC * 2),
                  a.w + (size_t)(r0 + blk * kGemvConsumerWarps + lane) * K + c0, piece, &full[s], policy);
       issued = c + 1;
+    }
+    if (ok && a.nx_w != nullptr && b < a.nx_grid) {
+      // first kGemvL2Ahead stages of the next GEMV's rows for CTA b (16 rows x
+      // one piece per stage, one lane per row)
+      const int nunits = a.nx_rows / a.nx_rpu;
+      const int nu0 = (int)(((long long)nunits * b) / a.nx_grid);
+      const int nu1 = (int)(((long long)nunits * (b + 1)) / a.nx_grid);
+      const int nr0 = nu0 * a.nx_rpu, nrows_n = (nu1 - nu0) * a.nx_rpu;
+      const int nkc_n = (a.nx_K + a.nx_kc - 1) / a.nx_kc;
+      for (int c = 0; c < kGemvL2Ahead; ++c) {
+        const int blk = c / nkc_n, kc = c - blk * nkc_n;
+        const int row = blk * kGemvConsumerWarps + lane;
+        if (lane < kGemvConsumerWarps && row < nrows_n) {
+          const int c0 = kc * a.nx_kc;
+          const uint32_t bytes = (uint32_t)min(a.nx_kc, a.nx_K - c0) * 2;
+          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.nx_w + (size_t)(nr0 + row) * a.nx_K + c0),
+                       "r"(bytes)
+                       : "memory");
+        }
+      }
     }
     if (!waited) {
       pdl_wait();

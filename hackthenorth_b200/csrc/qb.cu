@@ -166,6 +166,20 @@ cudaError_t launch_gemv(GemvArgs a, int sm_count, cudaStream_t st) {
   return launch_ex(gemv_kernel<EPI>, dim3(p.grid), dim3(kGemvThreads), p.smem, st, a);
 }
 
+// The GEMV launched after `a` in the step (its weights, shape and epilogue):
+// `a`'s CTAs bring its first stages into L2 (gemv.cuh).
+void set_next_gemv(GemvArgs& a, int epi, const void* w, int K, int rows, int sm_count) {
+  GemvPlan p;
+  if (std::getenv("QB_GEMV_L2_NEXT") && std::getenv("QB_GEMV_L2_NEXT")[0] == '0') return;
+  if (!plan_gemv(epi, K, rows, sm_count, &p)) return;
+  a.nx_w = static_cast<const bf16*>(w);
+  a.nx_K = K;
+  a.nx_rows = rows;
+  a.nx_rpu = gemv_rows_per_unit(epi);
+  a.nx_kc = p.kc;
+  a.nx_grid = p.grid;
+}
+
 GemvArgs gemv_args(const void* w, int K, int rows, const void* x, void* out, int* err) {
   GemvArgs a;
   std::memset(&a, 0, sizeof(a));
@@ -594,6 +608,7 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
     } else if (tp && !p2p) {
       consume(a, c->xb, c->xa);
     }
+    set_next_gemv(a, EPI_RESIDUAL, w.o, g.n_heads * D, H, c->sm_count);  // across the attention launch
     if ((e = launch_gemv<EPI_STORE>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "qkv launch");
     // 2. attention with the norm/rope/append prologue
     AttnArgs at;
@@ -624,6 +639,7 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
     if (tp && !p2p) {
       a = gemv_args(w.o, g.n_heads * D, H, c->attn, nullptr, c->err);
       a.out32 = c->y32;
+      set_next_gemv(a, EPI_SWIGLU, w.gate_up, H, 2 * g.ffn, c->sm_count);
       if ((e = launch_gemv<EPI_PARTIAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "o launch");
       if ((nr = ncclAllReduce(c->y32, c->y32, H, ncclFloat32, ncclSum, c->comm, st)) != ncclSuccess)
         return set_err(&c->msg, QB_ERR_CUDA, std::string("ncclAllReduce: ") + ncclGetErrorString(nr));
@@ -631,6 +647,7 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
       a = gemv_args(w.o, g.n_heads * D, H, c->attn, c->xb, c->err);
       a.residual = c->xa;
       if (p2p) peer_reduce(a, 2 * l, 0);
+      set_next_gemv(a, EPI_SWIGLU, w.gate_up, H, 2 * g.ffn, c->sm_count);
       if ((e = launch_gemv<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "o launch");
     }
     // 4. RMSNorm + gate/up + SwiGLU
@@ -638,12 +655,18 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
     a.gain = static_cast<const bf16*>(w.post_norm);
     a.eps = g.rms_eps;
     if (tp && !p2p) consume(a, c->xa, c->xb);
+    set_next_gemv(a, EPI_RESIDUAL, w.down, g.ffn, H, c->sm_count);
     if ((e = launch_gemv<EPI_SWIGLU>(a, c->sm_count, st)) != cudaSuccess)
       return cuda_fail(&c->msg, e, "gate/up launch");
     // 5. down (+ residual): xa = xb + Down . act
+    auto next_of_down = [&](GemvArgs& d) {
+      if (l + 1 < g.n_layers) set_next_gemv(d, EPI_STORE, c->layers[l + 1].qkv, H, nqkv, c->sm_count);
+      else if (head) set_next_gemv(d, EPI_ARGMAX, c->lm_head, H, g.vocab, c->sm_count);
+    };
     if (tp && !p2p) {
       a = gemv_args(w.down, g.ffn, H, c->act, nullptr, c->err);
       a.out32 = c->y32;
+      next_of_down(a);
       if ((e = launch_gemv<EPI_PARTIAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "down launch");
       if ((nr = ncclAllReduce(c->y32, c->y32, H, ncclFloat32, ncclSum, c->comm, st)) != ncclSuccess)
         return set_err(&c->msg, QB_ERR_CUDA, std::string("ncclAllReduce: ") + ncclGetErrorString(nr));
@@ -652,6 +675,7 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
       a.residual = c->xb;
       if (p2p) peer_reduce(a, 2 * l + 1, 1);
       else if (!head && l == g.n_layers - 1) a.pos_inc = pos;
+      next_of_down(a);
       if ((e = launch_gemv<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess)
         return cuda_fail(&c->msg, e, "down launch");
     }
