@@ -64,6 +64,9 @@ struct AttnArgs {
   unsigned* counters;    // [Hkv]
   int* err;
   int Hq, Hkv, Q, cap, splits;
+  int clusters;          // decode cluster kernel: clusters per KV head (<= 1: one)
+  int part_splits;       // decode cluster kernel: second extent of part_o / part_lse
+  unsigned* tickets;     // decode cluster kernel: [Hkv][splits] cross-cluster merge tickets
 };
 
 __host__ inline size_t attn_smem_bytes(int mt) {

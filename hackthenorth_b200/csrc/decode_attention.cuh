@@ -1,5 +1,6 @@
-// Batch-one decode attention (one query token, GQA group G <= 8) as one
-// thread-block cluster of S CTAs per KV head, S = the cluster size (8 or 16).
+// Batch-one decode attention (one query token, GQA group G <= 8) as C
+// thread-block clusters of S CTAs per KV head (S = the cluster size, 16, 8 or
+// 4; C = 1 at short capacities, more when the GPU has room for them).
 //
 // Follows the split-KV decode of dryft/engine/kernels/attention.py (per-split
 // online softmax in base 2 with P rounded to bf16 for the P.V product, splits
@@ -26,6 +27,11 @@
 //    before the first remote store (all CTAs of the cluster are then running);
 //    the receive buffers lie outside the ring, so no CTA has to wait for the
 //    others to finish streaming before the exchange.
+//  * With C > 1 clusters per head, cluster c takes splits [c*S, c*S+S) of the
+//    head's C*S; each CTA writes its merged dim slice and the cluster's lse to
+//    global partial rows, and the CTA of the same slice index that takes the
+//    last merge ticket merges the C clusters in cluster order and resets the
+//    ticket.
 #pragma once
 #include "attention.cuh"
 
@@ -42,6 +48,9 @@ constexpr int kDecRows = 8;                          // query rows per KV head (
 constexpr int kDecMaxCluster = 16;
 constexpr int kDecObStride = kAttnD + 4;             // padded fp32 row of the in-CTA merge
 constexpr int kDecBarrierId = 3;
+constexpr int kDecMultiClusterKeys = 8192;  // live keys from which a KV head may use all its clusters
+constexpr int kDecShortSplits = 8;          // splits per KV head below that (clusters of 4: two clusters)
+constexpr int kDecMaxClusters = 8;          // clusters per KV head
 
 __host__ inline size_t dec_smem_bytes() {
   return 1024 + (size_t)kDecStages * kDecStageBytes     // ring
@@ -101,7 +110,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int S = a.splits;  // cluster size
-  const int kvh = blockIdx.x / S;
+  const int C = max(1, a.clusters);  // clusters per KV head
+  const int kvh = blockIdx.x / (C * S);
+  const int cl = (blockIdx.x / S) % C;
   const int split = blockIdx.x % S;  // == cluster rank
   const int G = a.Hq / a.Hkv;        // query rows, <= kDecRows
 
@@ -125,16 +136,26 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     last = -1;
   }
   const int n = (int)last + 1;
-  const int Se = max(1, min(S, (n + kAttnMinSplitKeys - 1) / kAttnMinSplitKeys));
-  int per = (n + Se - 1) / Se;
+  // Splits over the whole head: about kAttnMinSplitKeys keys each, at most
+  // kDecShortSplits (at least one cluster's worth) below kDecMultiClusterKeys
+  // live keys, up to C clusters' worth above. Cluster cl takes global splits [cl*S, cl*S+S).
+  const int cmax = n >= kDecMultiClusterKeys ? C : min(C, max(1, kDecShortSplits / S));
+  const int SeT = max(1, min(cmax * S, (n + kAttnMinSplitKeys - 1) / kAttnMinSplitKeys));
+  const int Cact = (SeT + S - 1) / S;           // clusters with work (uniform over the grid)
+  const int Se = max(0, min(S, SeT - cl * S));  // active splits of this cluster
+  int per = (n + SeT - 1) / SeT;
   per = (per + kAttnSub - 1) & ~(kAttnSub - 1);
-  const int k0 = min(n, split * per);
+  const int k0 = min(n, (cl * S + split) * per);
   const int k1 = min(n, k0 + per);
   const int nst = (k1 - k0 + kDecKeys - 1) / kDecKeys;
   const bool active = split < Se && nst > 0;
 
   float val[4], lsev[4];  // this thread's rows (tid >> 7) + 2i, dim tid & 127
   bool ok = true;
+  if (Se == 0) {  // a cluster without work leaves at once (it reads nothing of the previous kernel)
+    cluster_wait();
+    return;
+  }
 
   if (warp == kDecWarps) {
     // ---------------------------------------------------------------- producer
@@ -389,7 +410,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
 
   // ------------------------------------------------------------ cluster merge
   cluster_wait();  // every CTA of the cluster is running
-  if (Se == 1) {   // uniform across the cluster: the single split is the answer
+  if (Se == 1 && Cact == 1) {  // uniform: the single split is the answer
     if (warp < kDecWarps && split == 0 && active && ok) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -415,8 +436,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     }
   }
   cluster_sync_all();
-  // Merge dims [split*W, split*W + W) of every row over the Se splits, in
-  // split order (dryft/engine/kernels/attention.py:204-206).
+  // Merge dims [split*W, split*W + W) of every row over the cluster's Se
+  // splits, in split order (dryft/engine/kernels/attention.py:204-206).
+  float cval = 0.f, clse = -INFINITY;
   if (tid < G * W) {
     const int r = tid / W, off = tid % W;
     float mx = -INFINITY;
@@ -427,8 +449,41 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       den += w;
       acc = fmaf(sm.rbuf[(sp * kDecRows + r) * W + off], w, acc);
     }
+    cval = acc / den;
+    clse = mx + log2f(den);
+    if (Cact == 1) attn_store_out(a, kvh, r, split * W + off, cval);
+  }
+  if (Cact == 1) return;
+  // Several clusters per head: each CTA publishes its slice of the cluster's
+  // result (normalised rows + log-sum-exp) and the CTA of the same slice
+  // index that arrives last merges the clusters in cluster order.
+  float* po = a.part_o + (size_t)kvh * a.part_splits * kDecRows * kAttnD;
+  float* pl = a.part_lse + (size_t)kvh * a.part_splits * kDecRows;
+  if (tid < G * W) {
+    const int r = tid / W, off = tid % W;
+    po[((size_t)cl * kDecRows + r) * kAttnD + split * W + off] = cval;
+    if (off == 0) pl[cl * kDecRows + r] = clse;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned t = atomic_add_acq_rel_gpu(a.tickets + kvh * S + split, 1u);
+    sm.flags[1] = (t == (unsigned)(Cact - 1)) ? 1 : 0;
+  }
+  __syncthreads();
+  if (sm.flags[1] == 0) return;
+  if (tid < G * W) {
+    const int r = tid / W, off = tid % W;
+    float mx = -INFINITY;
+    for (int c = 0; c < Cact; ++c) mx = fmaxf(mx, __ldcg(pl + c * kDecRows + r));
+    float den = 0.f, acc = 0.f;
+    for (int c = 0; c < Cact; ++c) {
+      const float w = exp2f(__ldcg(pl + c * kDecRows + r) - mx);
+      den += w;
+      acc = fmaf(__ldcg(po + ((size_t)c * kDecRows + r) * kAttnD + split * W + off), w, acc);
+    }
     attn_store_out(a, kvh, r, split * W + off, acc / den);
   }
+  if (tid == 0) a.tickets[kvh * S + split] = 0u;
 }
 
 }  // namespace qb

@@ -287,11 +287,16 @@ cudaError_t launch_attn_t(const CUtensorMap& tk, const CUtensorMap& tv, const At
   return launch_ex(attn_kernel<MT, PRO>, dim3(a.Hkv * a.splits), dim3(kAttnThreads), smem, st, tk, tv, a);
 }
 
-// Batch-one decode attention as one thread-block cluster per KV head
+// Batch-one decode attention as thread-block clusters per KV head
 // (attn_decode_kernel). Returns the cluster size for `hkv` heads of `rows`
 // query rows (16 when 16-CTA clusters of this kernel fit `hkv` at once, else
 // 8), or 0 when the kernel does not apply (then attn_kernel is used).
-// QB_ATTN_CLUSTER=0 disables it.
+// QB_ATTN_CLUSTER=0 disables it. Also records how many clusters of 16, 8 and 4
+// CTAs the GPU holds at once (g_dec_active), for launch_attn_decode's
+// long-context choice.
+constexpr int kDecSizes[3] = {16, 8, 4};
+int g_dec_active[3] = {0, 0, 0};
+
 int decode_cluster_size(int hkv, int rows) {
   static int cached_hkv = -1, cached_rows = -1, cached = 0;
   if (hkv == cached_hkv && rows == cached_rows) return cached;
@@ -306,8 +311,8 @@ int decode_cluster_size(int hkv, int rows) {
       cudaSuccess)
     return 0;
   cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-  const int sizes[2] = {16, 8};
-  for (int cs : sizes) {
+  for (int i = 0; i < 3; ++i) {
+    const int cs = kDecSizes[i];
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(hkv * cs);
     cfg.blockDim = dim3(kDecThreads);
@@ -320,19 +325,44 @@ int decode_cluster_size(int hkv, int rows) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, attn_decode_kernel, &cfg) == cudaSuccess && n >= hkv) {
-      cached = cs;
-      break;
+    if (cudaOccupancyMaxActiveClusters(&n, attn_decode_kernel, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
     }
-    cudaGetLastError();
+    g_dec_active[i] = n;
+    if (cached == 0 && cs >= 8 && n >= hkv) cached = cs;
   }
   return cached;
 }
 
 cudaError_t launch_attn_decode(const CUtensorMap& tk, const CUtensorMap& tv, AttnArgs a, int cs, cudaStream_t st) {
   a.splits = cs;
+  a.clusters = 1;
+  // Long contexts: the cluster size and clusters per KV head that put the
+  // most CTAs to work at once (several clusters merge through tickets and
+  // partial rows in global memory), e.g. 8 heads x 4 clusters x 4 CTAs.
+  if (a.tickets != nullptr && a.part_splits >= 2 && a.cap >= kDecMultiClusterKeys) {
+    int best = a.Hkv * cs;
+    for (int i = 0; i < 3; ++i) {
+      const int s = kDecSizes[i];
+      const int c = std::min({kDecMaxClusters, a.part_splits, g_dec_active[i] / a.Hkv,
+                              current_sm_count() / (a.Hkv * s)});
+      if (c >= 1 && a.Hkv * c * s > best) {
+        best = a.Hkv * c * s;
+        a.splits = s;
+        a.clusters = c;
+      }
+    }
+  }
+  static bool reported = false;
+  if (!reported && std::getenv("QB_VERBOSE")) {
+    reported = true;
+    std::fprintf(stderr, "qb: decode attention: %d KV heads x %d clusters x %d CTAs (GPU holds %d/%d/%d clusters of 16/8/4)\n",
+                 a.Hkv, a.clusters, a.splits, g_dec_active[0], g_dec_active[1], g_dec_active[2]);
+  }
+  cs = a.splits;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.Hkv * cs);
+  cfg.gridDim = dim3(a.Hkv * a.clusters * cs);
   cfg.blockDim = dim3(kDecThreads);
   cfg.dynamicSmemBytes = dec_smem_bytes();
   cfg.stream = st;
@@ -504,7 +534,7 @@ WsLayout ws_layout(const qb_ctx* c) {
   WsLayout L;
   size_t o = 0;
   L.err = o; o += 256;
-  L.counters = o; o += 1024;
+  L.counters = o; o += 4096;  // [0,64) attention, 64/66 heads, [128,194) step kernel, [512,..) decode clusters
   L.head_val = o; o = align_up(o + 4 * 1024, 256);
   L.head_idx = o; o = align_up(o + 4 * 1024, 256);
   L.xa = o; o = align_up(o + (size_t)g.hidden * 2, 256);
@@ -633,6 +663,8 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
     at.Q = 1;
     at.cap = c->cap;
     at.splits = c->splits;
+    at.part_splits = c->splits;
+    at.tickets = c->counters + 512;
     if ((e = launch_attn(c->tmk[l], c->tmv[l], &c->dmk[l], &c->dmv[l], at, true, st)) != cudaSuccess)
       return cuda_fail(&c->msg, e, "attention launch");
     // 3. o-proj (+ residual): xb = xa + O . attn
@@ -1572,7 +1604,7 @@ int qb_check(qb_ctx* c, void* stream) {
   if (rc == QB_ERR_TIMEOUT) {
     // A kernel that gave up left its merge tickets and arrival counters
     // mid-count: restore them so the next step starts clean.
-    cudaError_t e = cudaMemset(c->counters, 0, 1024);
+    cudaError_t e = cudaMemset(c->counters, 0, 4096);
     if (e != cudaSuccess) return cuda_fail(&c->msg, e, "counter reset");
     // Words written by the abandoned step carry its tag: move to a new one.
     unsigned ep = 0;

@@ -157,8 +157,8 @@ def test_0p6b_engine_matches_native_greedy_128(built_lib, cpu_threads):
     assert float(deficits.max()) <= LOGIT_ATOL, f"worst deficit {float(deficits.max())} at {int(deficits.argmax())}"
 
 
-@pytest.mark.parametrize("context", [200, 4096])
-def test_step_kernel_and_per_sublayer_launches_match_oracle(built_lib, cpu_threads, context):
+@pytest.mark.parametrize("context,capacity", [(200, None), (4096, None), (9000, None), (3000, 16384)])
+def test_step_kernel_and_per_sublayer_launches_match_oracle(built_lib, cpu_threads, context, capacity):
     """One Qwen3-8B-shaped layer (full vocabulary) over a seeded N(0, 1) cache
     prefix: the persistent step kernel and the per-sublayer launches each
     match the CPU oracle's logits within LOGIT_ATOL (mean difference below
@@ -167,7 +167,10 @@ def test_step_kernel_and_per_sublayer_launches_match_oracle(built_lib, cpu_threa
     within bf16 rounding of the projection.
     Context 200 runs one attention split per KV head, 4096 about 17 (merged
     through global memory by the last split in the step kernel, through
-    distributed shared memory in the per-sublayer path)."""
+    distributed shared memory in the per-sublayer path). A capacity above 8192
+    gives the per-sublayer path several clusters per KV head (four clusters of
+    four CTAs on a B200), merged across clusters by the last-arriving CTA of
+    each dim slice: context 9000 uses all of them, context 3000 two (8 splits)."""
     import dataclasses
 
     from hackthenorth_b200.config import QWEN3_8B
@@ -188,7 +191,7 @@ def test_step_kernel_and_per_sublayer_launches_match_oracle(built_lib, cpu_threa
     got = {}
     for mode in ("step-kernel", "per-sublayer"):
         engine = _with_mode(mode, lambda: Engine(None, "cuda:0", cfg=cfg, state=state))
-        st = engine.new_state(context, 4, keep_logits=True)
+        st = engine.new_state(context, 4, keep_logits=True, capacity=capacity)
         assert st.decode_mode == mode
         st.keys[:, :, :context] = kp.to(engine.device)
         st.values[:, :, :context] = vp.to(engine.device)
