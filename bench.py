@@ -413,7 +413,7 @@ def run_ours(args):
 
 
 def run_attention_sweep(args):
-    """Op sweep of SURVEY config 2 (GQA 32/8, D 128, bf16 N(0,1), batch 1):
+    """Decode-attention op sweep (GQA 32/8, D 128, bf16 N(0,1), batch 1):
     KV lengths 512..131072, 1 query row and the 5-row causal verify variant.
     Each timed launch reads a different KV buffer (>= 256 MB cycled), so the
     K/V bytes come from HBM. One JSON line with a per-case list."""
@@ -458,10 +458,12 @@ def run_attention_sweep(args):
 
 def run_speculative(args):
     """Speculative decoding line (not the headline): the 8B target verifies
-    k = 4 draft tokens per cycle on one GPU, the 0.6B draft model runs its k
-    decode steps every cycle (timed, its tokens unused), and each draft token is
-    the target's greedy token for the current prefix with seeded Bernoulli(0.7)
-    probability, else uniform (expected 2.773 emitted per cycle).
+    k = 4 draft tokens per cycle (tensor parallel over the ranks under
+    torchrun), the 0.6B draft model runs its k decode steps every cycle on each
+    rank (a replica; timed, its tokens unused), and each draft token is the
+    target's greedy token for the current prefix with seeded Bernoulli(0.7)
+    probability, else uniform (expected 2.773 emitted per cycle). Every rank
+    takes the same cycles; the line reports the slowest rank's time.
 
     The target's greedy continuation comes from its plain decode path. The
     verify pass sums in a different order, so at a near tie of the plain
@@ -475,12 +477,17 @@ def run_speculative(args):
     from hackthenorth_b200.engine import Engine
     from hackthenorth_b200.speculate import SyntheticDraft
 
+    world, rank, local = dist_setup(args.gpus)
     qbuild.build()
-    dev = torch.device("cuda:0")
-    torch.cuda.set_device(0)
+    dev = torch.device(f"cuda:{local}")
     cfg = get_config(args.config)
     ctx, k, n_out = args.context, 4, 256
-    target = Engine.from_random(cfg, seed=0, device=str(dev), init_device=str(dev))
+    if world > 1:
+        from hackthenorth_b200 import tp
+
+        target = tp.engine_from_random(cfg, seed=0)  # this rank's shard
+    else:
+        target = Engine.from_random(cfg, seed=0, device=str(dev), init_device=str(dev))
     draft = Engine.from_random(QWEN3_0P6B, seed=0, device=str(dev), init_device=str(dev))
     cap = ctx + 2 * n_out + 2 * k + 8
     ts = target.new_state(ctx, n_out + 1, draft_tokens=k, capacity=cap, keep_logits=True)
@@ -494,6 +501,17 @@ def run_speculative(args):
     ts.capture()
     ds.capture()
 
+    def margin():
+        """Top-2 margin of the last step's logits (over all vocabulary shards)."""
+        top2 = ts.logits.float().topk(2).values
+        if world > 1:
+            import torch.distributed as dist
+
+            parts = [torch.empty_like(top2) for _ in range(world)]
+            dist.all_gather(parts, top2)
+            top2 = torch.cat(parts).topk(2).values
+        return float(top2[0] - top2[1])
+
     def plain_from(token, position, count):
         """Plain greedy continuation and each step's top-2 margin (untimed)."""
         ts.token.fill_(token)
@@ -502,16 +520,16 @@ def run_speculative(args):
         for _ in range(count):
             ts.step()
             toks += ts.read_token()
-            top2 = ts.logits.float().topk(2).values
-            margins.append(float(top2[0] - top2[1]))
+            margins.append(margin())
         return toks, margins
 
     # warm-up of both graphs and the plain timing
     plain_from(first, ctx, 3)
     torch.cuda.synchronize()
+    barrier(world)
     t0 = time.perf_counter()
     plain, plain_margins = plain_from(first, ctx, n_out)
-    plain_s = time.perf_counter() - t0
+    plain_s = max_over_ranks(time.perf_counter() - t0, world)
     ts.check()
 
     split_ms = [0.0, 0.0]  # draft steps, verify (+ host read) per run
@@ -558,26 +576,44 @@ def run_speculative(args):
 
     run_spec(False)  # warm-up (captures the verify graph)
     torch.cuda.synchronize()
+    barrier(world)
     spec, cycles, spec_s, anchors = run_spec(True)
     ts.check()
     ds.check()
+    spec_s = max_over_ranks(spec_s, world)
+    split_ms[0] = max_over_ranks(split_ms[0], world)
+    split_ms[1] = max_over_ranks(split_ms[1], world)
+    par = (f"tp{world} target (NCCL all-reduce of fp32 partial rows in verify), draft replica per rank"
+           if world > 1 else "none")
     line = {
         "metric": "speculative decode tok/s (target verify k=4 + 0.6B draft steps, synthetic p=0.7 drafts)",
-        "value": round(n_out / spec_s, 3), "unit": "tok/s", "n_gpus": 1, "higher_is_better": True,
+        "value": round(n_out / spec_s, 3), "unit": "tok/s", "n_gpus": world, "higher_is_better": True,
         "mode": "speculative", "dtype": "bf16",
         "data": "synthetic (seeded random-init weights; KV prefix of seeded N(0,1) values; drafts = target "
                 "greedy continuation with Bernoulli(0.7), else uniform, seed 3)",
         "config": {"workload": f"{cfg.name} target, qwen3-0.6b draft, context {ctx}, k={k}, {n_out} tokens",
-                   "parallelism": "none (the TP8 form of this configuration needs a tensor-parallel verify pass)"},
+                   "parallelism": par},
         "emitted_per_cycle": round(n_out / cycles, 3), "expected_emitted_per_cycle": 2.773, "cycles": cycles,
         "plain_tok_s": round(n_out / plain_s, 3), "speedup_vs_plain": round(plain_s / spec_s, 3),
         "draft_ms_per_cycle": round(split_ms[0] / cycles, 3), "verify_ms_per_cycle": round(split_ms[1] / cycles, 3),
         "reanchors": len(anchors), "reanchor_plain_top2_margins": anchors,
         "tokens_equal_plain_greedy": spec == plain,
-        "timing": "sum of per-cycle CUDA-event times (draft steps + verify + the host read of its predictions); "
-                  "re-anchoring after a near-tie disagreement is untimed",
+        "timing": "sum of per-cycle CUDA-event times (draft steps + verify + the host read of its predictions), "
+                  "max over ranks; re-anchoring after a near-tie disagreement is untimed",
     }
-    print(json.dumps(line), flush=True)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import gc
+
+        import torch.distributed as dist
+
+        # the verify and decode graphs hold NCCL calls: release them first
+        ts = ds = target = draft = None
+        gc.collect()
+        torch.cuda.synchronize()
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_reference(args):

@@ -67,6 +67,10 @@ struct RowsArgs {
   int* part_idx;
   unsigned* counter;        // ARGMAX: arrival counter (restored to 0)
   int64_t* tokens_out;      // ARGMAX: [Q] greedy tokens
+  float* pair_out;          // ARGMAX, tensor parallel: [Q][2] (bf16 max logit, global index bits)
+                            // instead of tokens_out, for the cross-rank pick
+  int row_base;             // ARGMAX: global index of this shard's first row
+  float* out32;             // EPI_PARTIAL: [Q][rows] fp32 sums (reduced across ranks next)
   int* err;
 };
 
@@ -331,6 +335,8 @@ __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const RowsAr
         if (q < Q && row < nr)
           a.out[(size_t)q * a.rows + R] =
               __float2bfloat16_rn(round_bf16(v) + __bfloat162float(a.residual[(size_t)q * a.rows + R]));
+      } else if constexpr (EPI == EPI_PARTIAL) {
+        if (q < Q && row < nr) a.out32[(size_t)q * a.rows + R] = v;
       } else if constexpr (EPI == EPI_SWIGLU) {
         // rows are interleaved (gate, up); the up sum sits 8 threads further
         const float u = __shfl_down_sync(0xffffffffu, v, 8);
@@ -399,7 +405,14 @@ __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const RowsAr
           const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
           if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
         }
-        if (lane == 0) a.tokens_out[q] = (bi == 0x7fffffff) ? 0 : (int64_t)bi;
+        if (lane == 0) {
+          if (a.pair_out != nullptr) {
+            a.pair_out[2 * q] = bv;
+            a.pair_out[2 * q + 1] = __int_as_float(bi == 0x7fffffff ? bi : bi + a.row_base);
+          } else {
+            a.tokens_out[q] = (bi == 0x7fffffff) ? 0 : (int64_t)bi;
+          }
+        }
       }
       if (ctid == 0) *a.counter = 0u;
     }
@@ -485,6 +498,44 @@ __global__ void __launch_bounds__(128) rope_rows_kernel(const RopeRowsArgs a) {
     *reinterpret_cast<uint2*>(a.v_cache + ((size_t)kvh * a.cap + pos) * kAttnD + 4 * lane) =
         *reinterpret_cast<const uint2*>(src + 4 * lane);
   }
+}
+
+// Tensor-parallel rows, after the fp32 all-reduce of a projection's partial
+// sums: out = bf16(bf16(sum) + residual), the one rounding of the single-GPU
+// epilogue (dryft/engine/kernels/projection.py:57-83, down.py:8-35). n is a
+// multiple of 8; 8 values per thread.
+__global__ void tp_finish_rows_kernel(const float* __restrict__ sum, const bf16* __restrict__ res,
+                                      bf16* __restrict__ out, int n) {
+  pdl_wait();
+  const int i = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (i >= n) return;
+  const float4 p0 = __ldcg(reinterpret_cast<const float4*>(sum + i));
+  const float4 p1 = __ldcg(reinterpret_cast<const float4*>(sum + i + 4));
+  const uint4 rv = *reinterpret_cast<const uint4*>(res + i);
+  const bf16* r = reinterpret_cast<const bf16*>(&rv);
+  const float s[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+  uint4 ov;
+  bf16* o = reinterpret_cast<bf16*>(&ov);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o[j] = __float2bfloat16_rn(round_bf16(s[j]) + __bfloat162float(r[j]));
+  *reinterpret_cast<uint4*>(out + i) = ov;
+}
+
+// Tensor-parallel LM head over Q rows: pairs [tp][Q][2] hold each rank's
+// (bf16 max logit, global index bits) per row; the prediction is the largest
+// value, lowest global index on exact ties (dryft/engine/kernels/greedy.py:27-31).
+__global__ void tp_pick_rows_kernel(const float* __restrict__ pairs, int tp, int Q, int64_t* __restrict__ preds) {
+  pdl_wait();
+  const int q = threadIdx.x;
+  if (q >= Q) return;
+  float best = -INFINITY;
+  int best_i = 0x7fffffff;
+  for (int r = 0; r < tp; ++r) {
+    const float v = pairs[((size_t)r * Q + q) * 2];
+    const int i = __float_as_int(pairs[((size_t)r * Q + q) * 2 + 1]);
+    if (v > best || (v == best && i < best_i)) { best = v; best_i = i; }
+  }
+  preds[q] = (best_i == 0x7fffffff) ? 0 : (int64_t)best_i;
 }
 
 }  // namespace qb

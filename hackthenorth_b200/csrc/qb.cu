@@ -508,6 +508,8 @@ struct qb_ctx {
   int64_t* r_pos = nullptr;
   float* r_val = nullptr;
   int* r_idx = nullptr;
+  float* r_y32 = nullptr;    // tensor parallel verify: [rows][H] fp32 partial sums
+  float* r_pairs = nullptr;  // tensor parallel verify: [rows][2] + [tp][rows][2]
   cudaGraph_t vgraph = nullptr;
   cudaGraphExec_t vexec = nullptr;
   bool step_allowed = false;        // QB_STEP_KERNEL=1 at creation turns it on
@@ -526,7 +528,7 @@ struct WsLayout {
   // persistent step kernel: tagged activation words and split partials
   size_t w_xa, w_xb, w_qkv, w_attn, w_act, w_part_o, w_part_lse;
   // verify pass: up to kRowsMaxQ rows
-  size_t r_xa, r_xb, r_qkv, r_q, r_attn, r_act, r_pos, r_val, r_idx, total;
+  size_t r_xa, r_xb, r_qkv, r_q, r_attn, r_act, r_pos, r_val, r_idx, r_y32, r_pairs, total;
 };
 
 WsLayout ws_layout(const qb_ctx* c) {
@@ -566,6 +568,8 @@ WsLayout ws_layout(const qb_ctx* c) {
   L.r_pos = o; o = align_up(o + R * 8, 256);
   L.r_val = o; o = align_up(o + R * 1024 * 4, 256);
   L.r_idx = o; o = align_up(o + R * 1024 * 4, 256);
+  L.r_y32 = o; o = align_up(o + (c->tp_size > 1 ? R * g.hidden * 4 : 0), 256);
+  L.r_pairs = o; o = align_up(o + R * 2 * (1 + (size_t)c->tp_size) * 4, 256);
   L.total = o;
   return L;
 }
@@ -970,12 +974,29 @@ RowsArgs rows_args(const void* w, int K, int rows, int Q, const bf16* x, bf16* o
 // rows ids[0..n) at positions *pos .. *pos+n-1 through every layer, their K/V
 // appended, every row through the LM head; predictions[i] = greedy token after
 // row i. The position itself is left to the caller (logical rollback).
+// Tensor parallel: this rank's heads, FFN columns and vocabulary rows; the
+// o-proj and down sums are fp32 partial rows, all-reduced by NCCL and rounded
+// once with the residual added (tp_finish_rows_kernel); the head's per-row
+// (max, global index) pairs are all-gathered and picked per row.
 int run_verify(qb_ctx* c, const int64_t* ids, int n, const int64_t* pos, int64_t* preds, void* logits,
                cudaStream_t st) {
   const qb_config& g = c->lc;
   const int H = g.hidden, D = g.head_dim;
   const int nqkv = (g.n_heads + 2 * g.n_kv_heads) * D;
+  const bool tp = c->tp_size > 1;
   cudaError_t e;
+  ncclResult_t nr;
+  // fp32 partial rows -> all-reduce -> out = bf16(bf16(sum) + res)
+  auto reduce_rows = [&](const bf16* res, bf16* out, const char* what) -> int {
+    if ((nr = ncclAllReduce(c->r_y32, c->r_y32, (size_t)n * H, ncclFloat32, ncclSum, c->comm, st)) != ncclSuccess)
+      return set_err(&c->msg, QB_ERR_CUDA, std::string("ncclAllReduce: ") + ncclGetErrorString(nr));
+    const int threads = n * H / 8;
+    if ((e = launch_ex(tp_finish_rows_kernel, dim3((threads + 255) / 256), dim3(256), 0, st, (const float*)c->r_y32,
+                       res, out, n * H)) != cudaSuccess)
+      return cuda_fail(&c->msg, e, what);
+    return QB_OK;
+  };
+  int rc;
   for (int l = 0; l < g.n_layers; ++l) {
     const qb_layer_weights& w = c->layers[l];
     RowsArgs a = rows_args(w.qkv, H, nqkv, n, l == 0 ? nullptr : c->r_xa, c->r_qkv, c->err);
@@ -1031,15 +1052,31 @@ int run_verify(qb_ctx* c, const int64_t* ids, int n, const int64_t* pos, int64_t
                 : launch_attn(c->tmk[l], c->tmv[l], nullptr, nullptr, at, false, st);
     if (e != cudaSuccess) return cuda_fail(&c->msg, e, "verify attention");
     a = rows_args(w.o, g.n_heads * D, H, n, c->r_attn, c->r_xb, c->err);
-    a.residual = c->r_xa;
-    if ((e = launch_rows<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "verify o");
+    if (tp) {
+      a.out = nullptr;
+      a.out32 = c->r_y32;
+      if ((e = launch_rows<EPI_PARTIAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "verify o");
+      if ((rc = reduce_rows(c->r_xa, c->r_xb, "verify o finish")) != QB_OK) return rc;
+    } else {
+      a.residual = c->r_xa;
+      if ((e = launch_rows<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "verify o");
+    }
     a = rows_args(w.gate_up, H, 2 * g.ffn, n, c->r_xb, c->r_act, c->err);
     a.gain = static_cast<const bf16*>(w.post_norm);
     a.eps = g.rms_eps;
     if ((e = launch_rows<EPI_SWIGLU>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "verify gu");
     a = rows_args(w.down, g.ffn, H, n, c->r_act, c->r_xa, c->err);
-    a.residual = c->r_xb;
-    if ((e = launch_rows<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "verify down");
+    if (tp) {
+      a.out = nullptr;
+      a.out32 = c->r_y32;
+      if ((e = launch_rows<EPI_PARTIAL>(a, c->sm_count, st)) != cudaSuccess)
+        return cuda_fail(&c->msg, e, "verify down");
+      if ((rc = reduce_rows(c->r_xb, c->r_xa, "verify down finish")) != QB_OK) return rc;
+    } else {
+      a.residual = c->r_xb;
+      if ((e = launch_rows<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess)
+        return cuda_fail(&c->msg, e, "verify down");
+    }
   }
   RowsArgs a = rows_args(c->lm_head, H, g.vocab, n, c->r_xa, nullptr, c->err);
   a.gain = c->final_norm;
@@ -1049,7 +1086,19 @@ int run_verify(qb_ctx* c, const int64_t* ids, int n, const int64_t* pos, int64_t
   a.part_idx = c->r_idx;
   a.counter = c->counters + 66;
   a.tokens_out = preds;
+  if (tp) {
+    a.tokens_out = nullptr;
+    a.pair_out = c->r_pairs;
+    a.row_base = c->tp_rank * g.vocab;
+  }
   if ((e = launch_rows<EPI_ARGMAX>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "verify head");
+  if (tp) {
+    if ((nr = ncclAllGather(c->r_pairs, c->r_pairs + 2 * n, 2 * n, ncclFloat32, c->comm, st)) != ncclSuccess)
+      return set_err(&c->msg, QB_ERR_CUDA, std::string("ncclAllGather: ") + ncclGetErrorString(nr));
+    if ((e = launch_ex(tp_pick_rows_kernel, dim3(1), dim3(32), 0, st, (const float*)(c->r_pairs + 2 * n),
+                       c->tp_size, n, preds)) != cudaSuccess)
+      return cuda_fail(&c->msg, e, "verify pick");
+  }
   return QB_OK;
 }
 
@@ -1189,7 +1238,7 @@ int check_verify_args(qb_ctx* c, const int64_t* ids, int n, const int64_t* pos, 
   if (n < 1 || n > kRowsMaxQ) return set_err(&c->msg, QB_ERR_UNSUPPORTED, "verify takes 1..8 rows");
   if ((c->lc.n_heads / c->lc.n_kv_heads) * n > 32)
     return set_err(&c->msg, QB_ERR_UNSUPPORTED, "GQA group x verify rows above 32");
-  if (c->tp_size != 1) return set_err(&c->msg, QB_ERR_UNSUPPORTED, "verify runs on one GPU");
+  if (c->tp_size != 1 && c->comm == nullptr) return set_err(&c->msg, QB_ERR_STATE, "tensor parallel communicator not initialised");
   if (c->sm_count > 1024) return set_err(&c->msg, QB_ERR_UNSUPPORTED, "more than 1024 SMs");
   return QB_OK;
 }
@@ -1343,6 +1392,8 @@ int qb_bind_state(qb_ctx* c, void* k_cache, void* v_cache, int capacity, const v
   c->r_pos = reinterpret_cast<int64_t*>(c->ws + L.r_pos);
   c->r_val = reinterpret_cast<float*>(c->ws + L.r_val);
   c->r_idx = reinterpret_cast<int*>(c->ws + L.r_idx);
+  c->r_y32 = reinterpret_cast<float*>(c->ws + L.r_y32);
+  c->r_pairs = reinterpret_cast<float*>(c->ws + L.r_pairs);
   if ((e = cudaMemset(workspace, 0, L.total)) != cudaSuccess) return cuda_fail(&c->msg, e, "workspace memset");
   const qb_config& g = c->lc;
   c->tmk.assign(g.n_layers, CUtensorMap());

@@ -68,7 +68,8 @@ class DecodeState:
         self.token = torch.zeros(1, dtype=torch.int64, device=dev)
         self.position = torch.zeros(1, dtype=torch.int64, device=dev)
         self.prompt = torch.zeros(max(prompt_length, 1), dtype=torch.int64, device=dev)
-        self.logits = torch.zeros(cfg.vocab, dtype=BF16, device=dev) if keep_logits else None
+        # this rank's vocabulary shard under tensor parallelism
+        self.logits = torch.zeros(cfg.vocab // engine.tp_size, dtype=BF16, device=dev) if keep_logits else None
         _lib.check(L.qb_bind_state(engine.ctx, self.keys.data_ptr(), self.values.data_ptr(), self.capacity,
                                    self.cos.data_ptr(), self.sin.data_ptr(), self.workspace.data_ptr(),
                                    self.workspace.numel()), engine.ctx)
@@ -161,7 +162,7 @@ class DecodeState:
                 self.verify_ids = torch.zeros(8, dtype=torch.int64, device=dev)
                 self.verify_out = torch.zeros(8, dtype=torch.int64, device=dev)
                 self._verify_host = torch.zeros(8, dtype=torch.int64).pin_memory()
-            self.verify_logits = (torch.zeros(n, self.engine.cfg.vocab, dtype=BF16, device=dev)
+            self.verify_logits = (torch.zeros(n, self.engine.cfg.vocab // self.engine.tp_size, dtype=BF16, device=dev)
                                   if self.logits is not None else None)
             side = torch.cuda.Stream(device=dev)
             side.wait_stream(torch.cuda.current_stream())

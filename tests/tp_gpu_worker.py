@@ -1,6 +1,11 @@
 """Worker for test_tp_gpu.py (launched by torchrun, one process per GPU): a
 tensor-parallel Engine on seeded random weights decodes the golden prompt;
-rank 0 writes the tokens to the path given on the command line."""
+rank 0 writes the tokens to the path given on the command line.
+
+With a third argument ``verify``: the speculative stream (verify passes with a
+seeded synthetic draft of the golden continuation) and one 5-row verify pass
+(predictions, the full logits gathered from the vocabulary shards, the rows'
+K/V gathered from the head shards), written by rank 0 as .npz."""
 import json
 import os
 import sys
@@ -15,6 +20,7 @@ sys.path.insert(0, ROOT)
 
 def main():
     out_path, config = sys.argv[1], sys.argv[2]
+    mode = sys.argv[3] if len(sys.argv) > 3 else "decode"
     local = int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
     import datetime
@@ -37,6 +43,12 @@ def main():
     state = random_state_dict(cfg, 0)  # CPU draw, identical on every rank and in the golden vectors
     engine = Engine(None, f"cuda:{local}", cfg=cfg, state=state, tp_rank=dist.get_rank(),
                     tp_size=dist.get_world_size(), unique_id=uid)
+    if mode == "verify":
+        verify_case(engine, cfg, prompt, g["tokens"].tolist(), out_path)
+        del engine
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
+        return
     toks = [s[0] for s in engine.generate([prompt], n_new)]
     engine.state.check()
     toks2 = [s[0] for s in engine.generate([prompt], n_new)]  # graph replay with a fresh prompt state
@@ -46,6 +58,45 @@ def main():
     del engine
     torch.cuda.synchronize()
     dist.destroy_process_group()
+
+
+def _gather(t, dim):
+    parts = [torch.empty_like(t) for _ in range(dist.get_world_size())]
+    dist.all_gather(parts, t.contiguous())
+    return torch.cat(parts, dim=dim)
+
+
+def verify_case(engine, cfg, prompt, gold, out_path):
+    from hackthenorth_b200 import _lib
+    from hackthenorth_b200.speculate import SyntheticDraft
+
+    drafter = SyntheticDraft(gold, cfg.vocab, p=0.7, seed=3, draft_length=4)
+    spec = [s[0] for s in engine.generate([prompt], len(gold), draft_tokens=4, drafter=drafter)]
+    engine.state.check()
+    # one verify pass: current token + 2 golden drafts + 2 seeded random drafts
+    st = engine.new_state(len(prompt), 4, draft_tokens=8)
+    st.prefill(torch.tensor(prompt, dtype=torch.int64, device=engine.device))
+    current = st.read_token()[0]
+    rng = torch.Generator().manual_seed(21)
+    drafts = gold[1:3] + torch.randint(0, cfg.vocab, (2,), generator=rng).tolist()
+    n = len(drafts) + 1
+    dev = engine.device
+    ids = torch.tensor([current, *drafts], dtype=torch.int64, device=dev)
+    preds = torch.zeros(n, dtype=torch.int64, device=dev)
+    logits = torch.zeros(n, cfg.vocab // engine.tp_size, dtype=torch.bfloat16, device=dev)
+    L = _lib.load()
+    _lib.check(L.qb_verify(engine.ctx, ids.data_ptr(), n, st.position.data_ptr(), preds.data_ptr(),
+                           logits.data_ptr(), _lib.stream_handle()), engine.ctx)
+    st.check()
+    p0 = len(prompt)
+    full = _gather(logits, 1)
+    keys = _gather(st.keys[:, :, p0:p0 + n], 1)
+    values = _gather(st.values[:, :, p0:p0 + n], 1)
+    if dist.get_rank() == 0:
+        np.savez(out_path, spec=np.array(spec), preds=preds.cpu().numpy(), current=current,
+                 drafts=np.array(drafts), position=int(st.position.item()),
+                 logits=full.float().cpu().numpy(), keys=keys.float().cpu().numpy(),
+                 values=values.float().cpu().numpy())
 
 
 if __name__ == "__main__":
