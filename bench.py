@@ -583,8 +583,9 @@ def run_speculative(args):
     spec_s = max_over_ranks(spec_s, world)
     split_ms[0] = max_over_ranks(split_ms[0], world)
     split_ms[1] = max_over_ranks(split_ms[1], world)
-    par = (f"tp{world} target (NCCL all-reduce of fp32 partial rows in verify), draft replica per rank"
-           if world > 1 else "none")
+    reduction = ("NCCL all-reduce of fp32 partial rows" if os.environ.get("QB_TP_NCCL") == "1"
+                 else "peer-memory reduction fused into the o-proj and down epilogues over NVLink")
+    par = f"tp{world} target ({reduction}), draft replica per rank" if world > 1 else "none"
     line = {
         "metric": "speculative decode tok/s (target verify k=4 + 0.6B draft steps, synthetic p=0.7 drafts)",
         "value": round(n_out / spec_s, 3), "unit": "tok/s", "n_gpus": world, "higher_is_better": True,

@@ -71,8 +71,22 @@ struct RowsArgs {
                             // instead of tokens_out, for the cross-rank pick
   int row_base;             // ARGMAX: global index of this shard's first row
   float* out32;             // EPI_PARTIAL: [Q][rows] fp32 sums (reduced across ranks next)
+  TpPeers tp;               // EPI_RESIDUAL across ranks (tp.size > 1): peer-memory reduction
+  int tp_sub;               // sublayer id of the reduction (0..255)
+  int tp_parity;            // receive buffer half (0: o-proj, 1: down)
+  int hidden;               // H (rows of the reduced projection)
   int* err;
 };
+
+// Receive words of the rows reduction: after the decode rows' [2][n][H], a
+// region [2][n][kRowsMaxQ][H] (parity, sender rank, input row, output row).
+__host__ __device__ inline size_t rows_tp_words(int tp, int hidden) {
+  return (size_t)2 * tp * hidden + (size_t)2 * tp * kRowsMaxQ * hidden;
+}
+__device__ __forceinline__ size_t rows_tp_slot(const RowsArgs& a, int sender, int q) {
+  return (size_t)2 * a.tp.size * a.hidden +
+         (((size_t)a.tp_parity * a.tp.size + sender) * kRowsMaxQ + q) * a.hidden;
+}
 
 // ring, two reduction buffers, row factors, barriers, scratch.
 __host__ inline size_t rows_smem_bytes() {
@@ -332,9 +346,17 @@ __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const RowsAr
       if constexpr (EPI == EPI_STORE) {
         if (q < Q && row < nr) a.out[(size_t)q * a.rows + R] = __float2bfloat16_rn(v);
       } else if constexpr (EPI == EPI_RESIDUAL) {
-        if (q < Q && row < nr)
-          a.out[(size_t)q * a.rows + R] =
-              __float2bfloat16_rn(round_bf16(v) + __bfloat162float(a.residual[(size_t)q * a.rows + R]));
+        if (q < Q && row < nr) {
+          if (a.tp.size > 1) {
+            // tensor parallel: {token, partial} into every rank's words for
+            // (this rank, q, R); summed after the loop
+            const unsigned long long word = ((unsigned long long)tp_token(a.tp, a.tp_sub) << 32) | __float_as_uint(v);
+            for (int p = 0; p < a.tp.size; ++p) st_relaxed_sys_u64(a.tp.recv[p] + rows_tp_slot(a, a.tp.rank, q) + R, word);
+          } else {
+            a.out[(size_t)q * a.rows + R] =
+                __float2bfloat16_rn(round_bf16(v) + __bfloat162float(a.residual[(size_t)q * a.rows + R]));
+          }
+        }
       } else if constexpr (EPI == EPI_PARTIAL) {
         if (q < Q && row < nr) a.out32[(size_t)q * a.rows + R] = v;
       } else if constexpr (EPI == EPI_SWIGLU) {
@@ -356,6 +378,32 @@ __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const RowsAr
   }
   named_barrier(kRowsBarrierId, kRowsWarps * 32);
   if (!ok) return;
+
+  if constexpr (EPI == EPI_RESIDUAL) {
+    if (a.tp.size > 1) {
+      // Every rank partitions the rows across CTAs the same way: gather the
+      // n partials of this CTA's rows (bounded waits on their tokens), add
+      // them in rank order and finish as on one GPU: bf16(bf16(sum) + residual).
+      const uint32_t tok = tp_token(a.tp, a.tp_sub);
+      const unsigned long long* mine = a.tp.recv[a.tp.rank];
+      for (int i = ctid; i < nrows * Q; i += kRowsWarps * 32) {
+        const int q = i / nrows, R = r0 + (i - q * nrows);
+        unsigned long long w[kMaxTp];
+#pragma unroll
+        for (int p = 0; p < kMaxTp; ++p)
+          if (p < a.tp.size) w[p] = ld_relaxed_sys_u64(mine + rows_tp_slot(a, p, q) + R);
+        float sum = 0.f;
+#pragma unroll
+        for (int p = 0; p < kMaxTp; ++p)
+          if (p < a.tp.size)
+            sum += ((uint32_t)(w[p] >> 32) == tok)
+                       ? __uint_as_float((uint32_t)w[p])
+                       : wait_tagged(mine + rows_tp_slot(a, p, q) + R, tok, a.err, DEV_TIMEOUT_PEER_FLAG);
+        a.out[(size_t)q * a.rows + R] =
+            __float2bfloat16_rn(round_bf16(sum) + __bfloat162float(a.residual[(size_t)q * a.rows + R]));
+      }
+    }
+  }
 
   if constexpr (EPI == EPI_ARGMAX) {
     // Per input row: the best of this CTA (threads t with t & 7 == q), then
@@ -524,9 +572,13 @@ __global__ void tp_finish_rows_kernel(const float* __restrict__ sum, const bf16*
 // Tensor-parallel LM head over Q rows: pairs [tp][Q][2] hold each rank's
 // (bf16 max logit, global index bits) per row; the prediction is the largest
 // value, lowest global index on exact ties (dryft/engine/kernels/greedy.py:27-31).
-__global__ void tp_pick_rows_kernel(const float* __restrict__ pairs, int tp, int Q, int64_t* __restrict__ preds) {
+// epoch (peer-memory reductions): advanced once per verify pass, as after a
+// decode row, so the next pass's tokens are new.
+__global__ void tp_pick_rows_kernel(const float* __restrict__ pairs, int tp, int Q, int64_t* __restrict__ preds,
+                                    unsigned long long* epoch) {
   pdl_wait();
   const int q = threadIdx.x;
+  if (q == 0 && epoch != nullptr) *epoch += 1;
   if (q >= Q) return;
   float best = -INFINITY;
   int best_i = 0x7fffffff;

@@ -975,8 +975,9 @@ RowsArgs rows_args(const void* w, int K, int rows, int Q, const bf16* x, bf16* o
 // appended, every row through the LM head; predictions[i] = greedy token after
 // row i. The position itself is left to the caller (logical rollback).
 // Tensor parallel: this rank's heads, FFN columns and vocabulary rows; the
-// o-proj and down sums are fp32 partial rows, all-reduced by NCCL and rounded
-// once with the residual added (tp_finish_rows_kernel); the head's per-row
+// o-proj and down sums are exchanged as fp32 partial rows through peer memory
+// inside the rows GEMV (NCCL all-reduce + tp_finish_rows_kernel without peer
+// mappings) and rounded once with the residual added; the head's per-row
 // (max, global index) pairs are all-gathered and picked per row.
 int run_verify(qb_ctx* c, const int64_t* ids, int n, const int64_t* pos, int64_t* preds, void* logits,
                cudaStream_t st) {
@@ -984,9 +985,10 @@ int run_verify(qb_ctx* c, const int64_t* ids, int n, const int64_t* pos, int64_t
   const int H = g.hidden, D = g.head_dim;
   const int nqkv = (g.n_heads + 2 * g.n_kv_heads) * D;
   const bool tp = c->tp_size > 1;
+  const bool p2p = tp && c->p2p;
   cudaError_t e;
   ncclResult_t nr;
-  // fp32 partial rows -> all-reduce -> out = bf16(bf16(sum) + res)
+  // NCCL fallback: fp32 partial rows -> all-reduce -> out = bf16(bf16(sum) + res)
   auto reduce_rows = [&](const bf16* res, bf16* out, const char* what) -> int {
     if ((nr = ncclAllReduce(c->r_y32, c->r_y32, (size_t)n * H, ncclFloat32, ncclSum, c->comm, st)) != ncclSuccess)
       return set_err(&c->msg, QB_ERR_CUDA, std::string("ncclAllReduce: ") + ncclGetErrorString(nr));
@@ -1052,7 +1054,14 @@ int run_verify(qb_ctx* c, const int64_t* ids, int n, const int64_t* pos, int64_t
                 : launch_attn(c->tmk[l], c->tmv[l], nullptr, nullptr, at, false, st);
     if (e != cudaSuccess) return cuda_fail(&c->msg, e, "verify attention");
     a = rows_args(w.o, g.n_heads * D, H, n, c->r_attn, c->r_xb, c->err);
-    if (tp) {
+    if (p2p) {
+      a.residual = c->r_xa;
+      a.tp = c->peers;
+      a.tp_sub = 2 * l;
+      a.tp_parity = 0;
+      a.hidden = H;
+      if ((e = launch_rows<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "verify o");
+    } else if (tp) {
       a.out = nullptr;
       a.out32 = c->r_y32;
       if ((e = launch_rows<EPI_PARTIAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "verify o");
@@ -1066,7 +1075,15 @@ int run_verify(qb_ctx* c, const int64_t* ids, int n, const int64_t* pos, int64_t
     a.eps = g.rms_eps;
     if ((e = launch_rows<EPI_SWIGLU>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "verify gu");
     a = rows_args(w.down, g.ffn, H, n, c->r_act, c->r_xa, c->err);
-    if (tp) {
+    if (p2p) {
+      a.residual = c->r_xb;
+      a.tp = c->peers;
+      a.tp_sub = 2 * l + 1;
+      a.tp_parity = 1;
+      a.hidden = H;
+      if ((e = launch_rows<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess)
+        return cuda_fail(&c->msg, e, "verify down");
+    } else if (tp) {
       a.out = nullptr;
       a.out32 = c->r_y32;
       if ((e = launch_rows<EPI_PARTIAL>(a, c->sm_count, st)) != cudaSuccess)
@@ -1096,7 +1113,7 @@ int run_verify(qb_ctx* c, const int64_t* ids, int n, const int64_t* pos, int64_t
     if ((nr = ncclAllGather(c->r_pairs, c->r_pairs + 2 * n, 2 * n, ncclFloat32, c->comm, st)) != ncclSuccess)
       return set_err(&c->msg, QB_ERR_CUDA, std::string("ncclAllGather: ") + ncclGetErrorString(nr));
     if ((e = launch_ex(tp_pick_rows_kernel, dim3(1), dim3(32), 0, st, (const float*)(c->r_pairs + 2 * n),
-                       c->tp_size, n, preds)) != cudaSuccess)
+                       c->tp_size, n, preds, p2p ? c->tp_epoch() : nullptr)) != cudaSuccess)
       return cuda_fail(&c->msg, e, "verify pick");
   }
   return QB_OK;
@@ -1454,8 +1471,9 @@ int qb_tp_init(qb_ctx* c, const void* unique_id) {
   if (c->tp_size > kMaxTp) return QB_OK;  // NCCL path only
   const char* env = std::getenv("QB_TP_NCCL");
   if (env && env[0] == '1') return QB_OK;
-  // Peer-memory reduction buffers: tagged words [2][n][H] u64 | epoch.
-  const size_t recv_bytes = align_up((size_t)2 * c->tp_size * c->cfg.hidden * 8, 256);
+  // Peer-memory reduction buffers: tagged words [2][n][H] (decode rows) and
+  // [2][n][kRowsMaxQ][H] (verify rows) u64 | epoch.
+  const size_t recv_bytes = align_up(rows_tp_words(c->tp_size, c->cfg.hidden) * 8, 256);
   const size_t flag_bytes = 0;
   const size_t total = recv_bytes + flag_bytes + 256;
   if ((e = cudaMalloc(&c->tp_base, total)) != cudaSuccess) return cuda_fail(&c->msg, e, "peer buffer cudaMalloc");

@@ -62,9 +62,11 @@ LOGIT_ATOL = 0.0625
 
 
 @pytest.mark.parametrize("world", [2])
-def test_tp_verify_matches_oracle_and_golden(world, tmp_path, built_lib, cpu_threads):
-    """Tensor-parallel verify (fp32 partial rows all-reduced by NCCL, per-row
-    (max, index) pairs gathered across the vocabulary shards): the speculative
+@pytest.mark.parametrize("nccl_only", [False, True], ids=["peer-reduction", "nccl-allreduce"])
+def test_tp_verify_matches_oracle_and_golden(world, nccl_only, tmp_path, built_lib, cpu_threads):
+    """Tensor-parallel verify (fp32 partial rows exchanged through peer memory
+    inside the rows GEMV, or all-reduced by NCCL; per-row (max, index) pairs
+    gathered across the vocabulary shards): the speculative
     stream equals the golden greedy tokens up to the first near tie of the
     golden logits; one 5-row pass matches the CPU oracle's teacher-forced
     logits within LOGIT_ATOL, its predictions the oracle's tokens (up to near
@@ -74,7 +76,7 @@ def test_tp_verify_matches_oracle_and_golden(world, tmp_path, built_lib, cpu_thr
     from hackthenorth_b200.weights import random_state_dict
     from oracle.qwen3_oracle import OracleQwen3
 
-    got = _run(world, "qwen3-small", tmp_path, mode="verify")
+    got = _run(world, "qwen3-small", tmp_path, nccl_only, mode="verify")
     g = np.load(os.path.join(GOLDEN, "qwen3_small_greedy.npz"))
     gold, gl = g["tokens"].tolist(), torch.from_numpy(g["logits_bf16"].astype(np.float32))
     top2 = gl.topk(2, dim=1).values
