@@ -60,7 +60,7 @@ __device__ __forceinline__ uint32_t tp_token(const TpPeers& t, int sub_id) {
 
 struct GemvArgs {
   const bf16* w;        // [rows][K]
-  int K;                // multiple of 256
+  int K;                // multiple of 128
   int rows;             // weight rows (2F for SwiGLU)
   const bf16* x;        // [K] input row, or NULL with embed
   const bf16* embed;    // [vocab][K] embedding table (layer-0 gather) or NULL
@@ -335,7 +335,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
           a2 = dot8_bf16(w2, x2, a2);
           a3 = dot8_bf16(w3, x3, a3);
         }
-        for (; j < ncols; j += 256) a0 = dot8_bf16(lds128(piece + j * 2), lds128(xp + j), a0);
+        for (; j < ncols; j += 256)  // K a multiple of 128: the last chunk may be half a warp wide
+          if (j + lane * 8 < ncols) a0 = dot8_bf16(lds128(piece + j * 2), lds128(xp + j), a0);
         rowacc += (a0 + a1) + (a2 + a3);
         if (kc == nkc - 1) {
           const float t = warp_sum(rowacc);

@@ -1296,8 +1296,8 @@ int qb_create(const qb_config* cfg, int device, int tp_rank, int tp_size, qb_ctx
   lc.n_kv_heads = cfg->n_kv_heads / tp_size;
   lc.ffn = cfg->ffn / tp_size;
   lc.vocab = cfg->vocab / tp_size;
-  if ((lc.n_heads * lc.head_dim) % 256 || lc.ffn % 256)
-    return set_err(nullptr, QB_ERR_UNSUPPORTED, "per-rank Hq*D and ffn must be multiples of 256");
+  if ((lc.n_heads * lc.head_dim) % 128 || lc.ffn % 128)
+    return set_err(nullptr, QB_ERR_UNSUPPORTED, "per-rank Hq*D and ffn must be multiples of 128");
   cudaError_t e = cudaSetDevice(device);
   if (e != cudaSuccess) return cuda_fail(nullptr, e, "cudaSetDevice");
   qb_ctx* c = new qb_ctx();
@@ -1718,7 +1718,7 @@ int qb_norm_projection(const void* x, const void* gain, const void* w, void* out
                        int swiglu, void* stream) {
   if (!ptr_ok(x) || !ptr_ok(w) || !ptr_ok(out) || (gain && !ptr_ok(gain)))
     return set_err(nullptr, QB_ERR_ARG, "x, w, out (and gain) must be 16-byte aligned device pointers");
-  if (K <= 0 || K % 256 != 0) return set_err(nullptr, QB_ERR_UNSUPPORTED, "K must be a positive multiple of 256");
+  if (K <= 0 || K % 128 != 0) return set_err(nullptr, QB_ERR_UNSUPPORTED, "K must be a positive multiple of 128");
   if (rows <= 0 || (swiglu && rows % 2 != 0)) return set_err(nullptr, QB_ERR_ARG, "packed gate/up width must be even");
   GemvArgs a = gemv_args(w, K, rows, x, out, nullptr);
   a.gain = static_cast<const bf16*>(gain);
@@ -1734,7 +1734,7 @@ int qb_projection_residual(const void* x, const void* w, const void* residual, v
                            void* stream) {
   if (!ptr_ok(x) || !ptr_ok(w) || !ptr_ok(out) || !residual)
     return set_err(nullptr, QB_ERR_ARG, "x, w, residual, out must be device pointers (16-byte aligned)");
-  if (K <= 0 || K % 256 != 0) return set_err(nullptr, QB_ERR_UNSUPPORTED, "K must be a positive multiple of 256");
+  if (K <= 0 || K % 128 != 0) return set_err(nullptr, QB_ERR_UNSUPPORTED, "K must be a positive multiple of 128");
   if (N <= 0) return set_err(nullptr, QB_ERR_ARG, "N must be positive");
   GemvArgs a = gemv_args(w, K, N, x, out, nullptr);
   a.residual = static_cast<const bf16*>(residual);
@@ -1748,7 +1748,7 @@ int qb_norm_greedy_head(const void* x, const void* gain, const void* w, int K, i
   if (!ptr_ok(x) || !ptr_ok(w) || !token_out || (gain && !ptr_ok(gain)) || !ptr_ok(scratch))
     return set_err(nullptr, QB_ERR_ARG, "x, w, gain, scratch must be 16-byte aligned device pointers");
   if (scratch_bytes < kOpScratchBytes) return set_err(nullptr, QB_ERR_ARG, "scratch smaller than qb_op_scratch_bytes()");
-  if (K <= 0 || K % 256 != 0) return set_err(nullptr, QB_ERR_UNSUPPORTED, "K must be a positive multiple of 256");
+  if (K <= 0 || K % 128 != 0) return set_err(nullptr, QB_ERR_UNSUPPORTED, "K must be a positive multiple of 128");
   if (V <= 0) return set_err(nullptr, QB_ERR_ARG, "V must be positive");
   uint8_t* s = static_cast<uint8_t*>(scratch);
   GemvArgs a = gemv_args(w, K, V, x, nullptr, reinterpret_cast<int*>(s + kScrErr));

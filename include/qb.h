@@ -111,8 +111,9 @@ int qb_bind_state(qb_ctx* ctx, void* k_cache, void* v_cache, int capacity,
 /* One batch-one decode step: DecodeState.step (dryft/engine/decode.py:126-138).
  * Reads *token (int64, device) at *position (int64, device), appends its K/V,
  * writes the greedy next token to *token and increments *position.
- * logits_out (device bf16 [V]) may be NULL. Graph-capturable: no host sync,
- * no allocation. Fails with QB_ERR_CAPACITY only when detectable on the host. */
+ * logits_out (device bf16 [V], this rank's [V/tp_size] shard under tensor
+ * parallelism) may be NULL. Graph-capturable: no host sync, no allocation.
+ * Fails with QB_ERR_CAPACITY only when detectable on the host. */
 int qb_decode_step(qb_ctx* ctx, int64_t* token, int64_t* position, void* logits_out,
                    void* stream);
 
@@ -145,8 +146,11 @@ int qb_replay_decode(qb_ctx* ctx, void* stream);
  * *position .. *position+n-1 (device int64, not modified: the caller applies
  * the accepted count, dryft/engine/decode.py:194-206); their K/V are written
  * to the cache. predictions (device int64 [n]): the greedy token after each
- * row; logits_out (device bf16 [n][V]) may be NULL. Every weight is streamed
- * once for all n rows. Single GPU (tp_size 1); QB_ERR_UNSUPPORTED otherwise. */
+ * row; logits_out (device bf16 [n][V], [n][V/tp_size] of this rank's
+ * vocabulary shard under tensor parallelism) may be NULL. Every weight is
+ * streamed once for all n rows. Tensor parallel: every rank calls it in the
+ * same order (peer-memory reduction of the o-proj and down rows, or NCCL with
+ * QB_TP_NCCL=1); predictions are identical on all ranks. */
 int qb_verify(qb_ctx* ctx, const int64_t* ids, int n, const int64_t* position, int64_t* predictions,
               void* logits_out, void* stream);
 int qb_capture_verify(qb_ctx* ctx, const int64_t* ids, int n, const int64_t* position,
@@ -183,13 +187,14 @@ int qb_gemm_bf16(const void* x, const void* w, void* out, const void* residual, 
  * rounding. gain == NULL skips the norm. swiglu != 0: W is [2N, K] with gate
  * and up rows interleaved and y[j] = bf16(bf16(silu(gate_j)) * up_j).
  * Replaces norm_projection (dryft/engine/kernels/projection.py:36-53).
- * x [K], W [rows, K], out [N]; K a multiple of 256. */
+ * x [K], W [rows, K], out [N]; K a multiple of 128. */
 int qb_norm_projection(const void* x, const void* gain, const void* w, void* out,
                        int K, int rows, float eps, int swiglu, void* stream);
 
 /* out = bf16(bf16(W . x) + residual). Replaces output_projection_residual
  * (dryft/engine/kernels/projection.py:70-83) and down_residual
- * (dryft/engine/kernels/down.py:288-296). x [K], W [N, K], residual/out [N]. */
+ * (dryft/engine/kernels/down.py:288-296). x [K], W [N, K], residual/out [N];
+ * K a multiple of 128. */
 int qb_projection_residual(const void* x, const void* w, const void* residual, void* out,
                            int K, int N, void* stream);
 

@@ -43,7 +43,7 @@ def _lib_ready(built_lib):
     ops.check_device_errors(DEV)
 
 
-@pytest.mark.parametrize("K,N", [(1024, 4096), (2560, 6144), (4096, 6144), (256, 96), (12288, 512)])
+@pytest.mark.parametrize("K,N", [(1024, 4096), (2560, 6144), (4096, 6144), (256, 96), (12288, 512), (384, 1024), (128, 300)])
 def test_norm_projection_matches_oracle(K, N):
     from hackthenorth_b200 import ops
     from oracle.qwen3_oracle import norm_projection
@@ -83,7 +83,7 @@ def test_output_projection_halfway_rounding_known_answer():
     assert bool((ops.output_projection_residual(x, w, res) == 0).all())
 
 
-@pytest.mark.parametrize("K,N", [(4096, 2560), (9728, 2560), (12288, 4096), (2048, 1024)])
+@pytest.mark.parametrize("K,N", [(4096, 2560), (9728, 2560), (12288, 4096), (2048, 1024), (384, 1024)])
 def test_projection_residual_matches_oracle(K, N):
     from hackthenorth_b200 import ops
     from oracle.qwen3_oracle import linear

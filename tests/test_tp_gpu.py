@@ -49,7 +49,7 @@ def test_tp_small_matches_golden(world, nccl_only, tmp_path, built_lib):
     assert got["again"] == gold
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_tp_0p6b_matches_golden_until_reference_tie(world, tmp_path, built_lib):
     got = _run(world, "qwen3-0.6b", tmp_path)
     with open(os.path.join(GOLDEN, "qwen3_0p6b_greedy.json")) as f:
