@@ -33,7 +33,9 @@ def _run(world, config, tmp_path, nccl_only=False, mode="decode"):
            f"--nproc-per-node={world}", "--master-addr", "127.0.0.1", "--master-port", str(_port()),
            os.path.join(ROOT, "tests", "tp_gpu_worker.py"), out, config, mode]
     res = subprocess.run(cmd, capture_output=True, text=True, env=env)
-    assert res.returncode == 0, res.stdout[-2000:] + res.stderr[-4000:]
+    if res.returncode != 0:  # the first traceback is the failing rank's own
+        tb = res.stderr.find("Traceback")
+        pytest.fail(res.stdout[-2000:] + (res.stderr[tb:tb + 6000] if tb >= 0 else "") + res.stderr[-3000:])
     if mode == "verify":
         return dict(np.load(out))
     with open(out) as f:
