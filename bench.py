@@ -272,7 +272,10 @@ def run_ours(args):
     torch.cuda.empty_cache()
     ctx = args.context
     total_steps = args.warmup + args.steps
-    state = engine.new_state(ctx, total_steps + 2, capacity=ctx + 2 * total_steps + 8)
+    B = args.batch
+    if B > 1 and (world > 1 or args.real_prefill):
+        raise SystemExit("--batch > 1 runs on one GPU over seeded K/V (no --real-prefill)")
+    state = engine.new_state(ctx, total_steps + 2, capacity=ctx + 2 * total_steps + 8, batch=B)
     prefill_ms = None
     if args.real_prefill and world == 1:
         # the configuration's random prompt (seed 1) prefilled as dense blocks,
@@ -292,7 +295,7 @@ def run_ours(args):
         gen = torch.Generator(device=dev).manual_seed(2)
         for t in (state.keys, state.values):
             for l in range(cfg.n_layers):
-                t[l, :, :ctx].normal_(generator=gen)
+                t[l, ..., :ctx, :].normal_(generator=gen)  # [Hkv, cap, D] or [B, Hkv, cap, D]
         first_token = 1
     state.token.fill_(first_token)
     state.position.fill_(ctx)
@@ -323,8 +326,8 @@ def run_ours(args):
     # e2e: the same steps with host buffers (pinned H2D of the token, replay,
     # D2H of the result, sync) — the per-token loop of generate().
     state.position.fill_(ctx)
-    host_in = torch.tensor([first_token], dtype=torch.int64).pin_memory()
-    host_out = torch.empty(1, dtype=torch.int64).pin_memory()
+    host_in = torch.tensor([first_token] * B, dtype=torch.int64).pin_memory()
+    host_out = torch.empty(B, dtype=torch.int64).pin_memory()
     torch.cuda.synchronize()
     barrier(world)
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -346,13 +349,16 @@ def run_ours(args):
     t_dev = max_over_ranks(dev_s, world)
     t_e2e = max_over_ranks(e2e_s, world)
     ms_step = 1000.0 * t_dev / args.steps
-    value = args.steps / t_dev  # one sequence; with N GPUs it is sharded across them
+    value = B * args.steps / t_dev  # B sequences; with N GPUs one sequence sharded across them
     mean_ctx = ctx + (args.steps - 1) / 2.0
-    step_bytes = cfg.step_bytes(int(round(mean_ctx))) // world  # per GPU
+    wbytes = cfg.weight_bytes_per_token()
+    # weights once per step, K/V of every sequence; per GPU under tensor parallelism
+    step_bytes = (wbytes + B * (cfg.step_bytes(int(round(mean_ctx))) - wbytes)) // world
     achieved = kern_bytes / kern_s / 1e9
-    launches_per_step = 5 * cfg.n_layers + 1 + (1 if world > 1 else 0)  # + the cross-rank pick
+    launches_per_step = (5 * cfg.n_layers + 1 + (1 if world > 1 else 0) if B == 1
+                         else 6 * cfg.n_layers + 2)  # batched: + rope rows per layer, + position update
     out = {
-        "metric": METRIC,
+        "metric": METRIC if B == 1 else f"batch-{B} decode tok/s (all sequences) and % of HBM roofline",
         "value": round(value, 3),
         "unit": "tok/s",
         "n_gpus": world,
@@ -366,8 +372,8 @@ def run_ours(args):
         "data": ("synthetic (seeded random-init weights N(0,0.02); context = a real prefill of a seeded "
                  "random prompt)" if prefill_ms is not None else
                  "synthetic (seeded random-init weights N(0,0.02); KV cache of seeded N(0,1) positions)"),
-        "config": {"workload": f"{cfg.name}-shaped batch-1 greedy decode at context {ctx}",
-                   "model": cfg.name, "global_batch": 1, "seq_len": ctx, "context": ctx,
+        "config": {"workload": f"{cfg.name}-shaped batch-{B} greedy decode at context {ctx}",
+                   "model": cfg.name, "global_batch": B, "seq_len": ctx, "context": ctx,
                    "parallelism": "none" if world == 1 else (
                        f"tp{world} (NCCL all-reduce after o-proj and down)" if os.environ.get("QB_TP_NCCL") == "1"
                        else f"tp{world} (peer-memory reduction fused into the o-proj and down epilogues over NVLink)"),
@@ -383,7 +389,7 @@ def run_ours(args):
         "step_roofline": {"bytes_per_step": step_bytes, "achieved": round(step_bytes / (t_dev / args.steps) / 1e9, 1),
                           "peak": peak_gbs, "unit": "GB/s",
                           "frac": round(step_bytes / (t_dev / args.steps) / 1e9 / peak_gbs, 4),
-                          "roofline_tok_s": round(peak_gbs * 1e9 / step_bytes, 1)},
+                          "roofline_tok_s": round(B * peak_gbs * 1e9 / step_bytes, 1)},
         "e2e": {"value": round(args.steps / t_e2e, 3), "unit": "tok/s",
                 "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
                 "d2h_bytes_per_step": host_out.numel() * host_out.element_size()},
@@ -392,7 +398,12 @@ def run_ours(args):
         "profile_only": bool(args.layers),
         "clocks": clk,
     }
-    if world == 1 and not args.no_cpu_baseline:
+    if B > 1:
+        # the dominant kernels of a batched step are the rows GEMVs: the step's
+        # own bytes over its time are the roofline figure
+        out["roofline"] = dict(out["step_roofline"], bound="hbm", kernel="whole batched step (rows kernels)",
+                               traffic=None, peak_source=peak_kind)
+    if world == 1 and not args.no_cpu_baseline and B == 1:
         del state, engine
         torch.cuda.empty_cache()
         out["cpu_baseline"] = cpu_reference_decode(cfg, ctx, budget_s=args.cpu_budget)
@@ -668,6 +679,8 @@ def main(argv=None):
     ap.add_argument("--real-prefill", action="store_true",
                     help="fill the context with a real prefill of a seeded random prompt (timed, reported as "
                          "prefill_ms) instead of seeded random K/V values")
+    ap.add_argument("--batch", type=int, default=1,
+                    help="sequences decoded together (1..8, one GPU; the line's value is their total tok/s)")
     ap.add_argument("--decode-path", choices=("per-sublayer", "step-kernel"), default="per-sublayer",
                     help="step-kernel: the opt-in persistent one-launch-per-step kernel (single GPU)")
     args = ap.parse_args(argv)

@@ -43,6 +43,7 @@ SIGNATURES = {
     "qb_workspace_bytes": (c_int, [c_void_p, ctypes.POINTER(c_size_t)]),
     "qb_bind_state": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_size_t]),
     "qb_decode_step": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "qb_set_batch": (c_int, [c_void_p, c_int]),
     "qb_prefill": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
     "qb_capture_decode": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "qb_replay_decode": (c_int, [c_void_p, c_void_p]),

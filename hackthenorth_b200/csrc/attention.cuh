@@ -67,6 +67,9 @@ struct AttnArgs {
   int clusters;          // decode cluster kernel: clusters per KV head (<= 1: one)
   int part_splits;       // decode cluster kernel: second extent of part_o / part_lse
   unsigned* tickets;     // decode cluster kernel: [Hkv][splits] cross-cluster merge tickets
+  int batch_hkv;         // rows kernel, batched decode: KV heads per sequence (KV head h of the
+                         // launch belongs to sequence h / batch_hkv, whose position is pos[h / batch_hkv]);
+                         // 0: one sequence, pos[i] is query i's position
 };
 
 __host__ inline size_t attn_smem_bytes(int mt) {

@@ -470,7 +470,8 @@ __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const RowsAr
 // Per-head q/k RMSNorm + RoPE for Q consecutive positions, K/V appended to the
 // cache (dryft/engine/kernels/fused.py:9-30,47-82 with several rows). One warp
 // per (row, head); also writes the rows' positions for the attention kernel
-// (verify) when asked. Used for the verify rows and for prompt rows.
+// (verify) when asked. Used for the verify rows and for prompt rows; batched,
+// row q is the next token of sequence q (its own position and cache slice).
 struct RopeRowsArgs {
   const bf16* qkv;        // [Q][Hq*D + 2*Hkv*D]
   const bf16* q_norm;
@@ -482,10 +483,11 @@ struct RopeRowsArgs {
   int p0;
   int64_t* positions;     // [Q] out, or NULL
   bf16* q_out;            // [Q][Hq][D]
-  bf16* k_cache;          // this layer's [Hkv][cap][D]
+  bf16* k_cache;          // this layer's [Hkv][cap][D] ([Q][Hkv][cap][D] when batched)
   bf16* v_cache;
   int* err;
   int Q, Hq, Hkv, cap;
+  int batched;            // 1: row q is sequence q, at position pos[q], in cache slice q
 };
 
 __device__ __forceinline__ void norm_rope_global(const bf16* src, const bf16* gain, const bf16* cos_row,
@@ -526,13 +528,27 @@ __global__ void __launch_bounds__(128) rope_rows_kernel(const RopeRowsArgs a) {
   const int heads = a.Hq + 2 * a.Hkv;
   if (gw >= a.Q * heads) return;
   const int q = gw / heads, h = gw - q * heads;
-  const long long p0 = a.pos ? *a.pos : (long long)a.p0;
-  const long long pos = p0 + q;
-  if (p0 < 0 || p0 + a.Q > a.cap) {
-    if (gw == 0 && lane == 0) report_error(a.err, DEV_BAD_POSITION);
-    return;
+  long long pos;
+  bf16* k_cache = a.k_cache;
+  bf16* v_cache = a.v_cache;
+  if (a.batched) {
+    pos = a.pos[q];
+    if (pos < 0 || pos >= a.cap) {
+      if (h == 0 && lane == 0) report_error(a.err, DEV_BAD_POSITION);
+      return;
+    }
+    const size_t slice = (size_t)q * a.Hkv * a.cap * kAttnD;
+    k_cache += slice;
+    v_cache += slice;
+  } else {
+    const long long p0 = a.pos ? *a.pos : (long long)a.p0;
+    pos = p0 + q;
+    if (p0 < 0 || p0 + a.Q > a.cap) {
+      if (gw == 0 && lane == 0) report_error(a.err, DEV_BAD_POSITION);
+      return;
+    }
+    if (a.positions != nullptr && gw == 0 && lane < a.Q) a.positions[lane] = p0 + lane;
   }
-  if (a.positions != nullptr && gw == 0 && lane < a.Q) a.positions[lane] = p0 + lane;
   const bf16* src = a.qkv + (size_t)q * heads * kAttnD + (size_t)h * kAttnD;
   const bf16* cos_row = a.cos + (size_t)pos * kAttnD;
   const bf16* sin_row = a.sin + (size_t)pos * kAttnD;
@@ -540,10 +556,10 @@ __global__ void __launch_bounds__(128) rope_rows_kernel(const RopeRowsArgs a) {
     norm_rope_global(src, a.q_norm, cos_row, sin_row, a.eps, lane, a.q_out + ((size_t)q * a.Hq + h) * kAttnD);
   } else if (h < a.Hq + a.Hkv) {
     const int kvh = h - a.Hq;
-    norm_rope_global(src, a.k_norm, cos_row, sin_row, a.eps, lane, a.k_cache + ((size_t)kvh * a.cap + pos) * kAttnD);
+    norm_rope_global(src, a.k_norm, cos_row, sin_row, a.eps, lane, k_cache + ((size_t)kvh * a.cap + pos) * kAttnD);
   } else {
     const int kvh = h - a.Hq - a.Hkv;
-    *reinterpret_cast<uint2*>(a.v_cache + ((size_t)kvh * a.cap + pos) * kAttnD + 4 * lane) =
+    *reinterpret_cast<uint2*>(v_cache + ((size_t)kvh * a.cap + pos) * kAttnD + 4 * lane) =
         *reinterpret_cast<const uint2*>(src + 4 * lane);
   }
 }
@@ -588,6 +604,19 @@ __global__ void tp_pick_rows_kernel(const float* __restrict__ pairs, int tp, int
     if (v > best || (v == best && i < best_i)) { best = v; best_i = i; }
   }
   preds[q] = (best_i == 0x7fffffff) ? 0 : (int64_t)best_i;
+}
+
+// Batched decode: pos[b] += delta for the n sequences (after their pass).
+__global__ void add_rows_i64_kernel(int64_t* pos, int n, long long delta) {
+  pdl_wait();
+  if ((int)threadIdx.x < n) pos[threadIdx.x] += delta;
+}
+
+// Batched prefill: out[b] = ids[b][col] for the n prompts of length len
+// (ids row-major [n][len]), the token rows of one teacher-forced pass.
+__global__ void gather_column_i64_kernel(const int64_t* ids, int len, int col, int n, int64_t* out) {
+  pdl_wait();
+  if ((int)threadIdx.x < n) out[threadIdx.x] = ids[(size_t)threadIdx.x * len + col];
 }
 
 }  // namespace qb

@@ -420,6 +420,30 @@ int rows_cluster_size(int hkv) {
   return cached;
 }
 
+// Cluster size for the rows attention kernel over `vheads` KV heads of several
+// sequences (batched decode): the largest power of two <= 16 with every
+// cluster resident at once when possible (vheads * cs <= SMs); clusters do not
+// wait on each other, so more than fit at once is still correct. 0 when the
+// kernel's attributes cannot be set.
+int batch_attn_cluster(int vheads, int sm_count) {
+  static int attrs = -1;
+  if (attrs < 0) {
+    attrs = 1;
+    void (*kernels[3])(const CUtensorMap, const CUtensorMap, const AttnArgs) = {
+        attn_rows_kernel<1>, attn_rows_kernel<2>, attn_rows_kernel<3>};
+    for (auto k : kernels)
+      if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)va_smem_bytes()) != cudaSuccess ||
+          cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+        cudaGetLastError();
+        attrs = 0;
+      }
+  }
+  if (!attrs) return 0;
+  int cs = 16;
+  while (cs > 1 && vheads * cs > sm_count) cs >>= 1;
+  return cs;
+}
+
 cudaError_t launch_attn_rows(const CUtensorMap& tk, const CUtensorMap& tv, AttnArgs a, int cs, cudaStream_t st) {
   a.splits = cs;
   const int rows = (a.Hq / a.Hkv) * a.Q;
@@ -466,6 +490,7 @@ struct qb_ctx {
   qb_config lc;   // this rank's shard: Hq/n, Hkv/n, F/n, V/n (equal to cfg without tensor parallelism)
   int device = 0;
   int tp_rank = 0, tp_size = 1;
+  int batch = 1;                    // sequences decoded together (qb_set_batch; cache [L][B][Hkv][cap][D])
   ncclComm_t comm = nullptr;
   bool p2p = false;                 // peer-memory reduction (else NCCL all-reduce)
   void* tp_base = nullptr;          // this rank's [tagged receive words | epoch] allocation
@@ -776,6 +801,7 @@ void prepare_step(qb_ctx* c) {
   if (!c->weights_bound || !c->state_bound) return;
   if (!c->step_allowed) return off("not requested (QB_STEP_KERNEL=1)");
   if (c->tp_size != 1) return off("tensor parallel");
+  if (c->batch != 1) return off("batched decode");
   const qb_config& g = c->lc;
   const int G = c->sm_count, D = g.head_dim;
   if (g.n_heads / g.n_kv_heads > kDecRows || g.n_kv_heads > 64 || G > 1024) return off("head layout");
@@ -1119,6 +1145,99 @@ int run_verify(qb_ctx* c, const int64_t* ids, int n, const int64_t* pos, int64_t
   return QB_OK;
 }
 
+// Batched decode (the B = c->batch sequences of a batched context, one row
+// each; dryft's DecodeState at B > 1, dryft/engine/decode.py:102-138):
+// ids[b] at position pos[b] (device), sequence b's K/V in slice b of every
+// layer's [B][Hkv][cap][D]. The rows kernels stream every weight once for the
+// B rows; the rows attention runs B * Hkv KV heads, each reading its
+// sequence's position. head: the greedy next token of each sequence to
+// tok_out[b] (logits [B][V] optional); pos[b] += 1 either way.
+int run_batch_pass(qb_ctx* c, const int64_t* ids, int64_t* pos, int64_t* tok_out, void* logits, bool head,
+                   cudaStream_t st) {
+  const qb_config& g = c->lc;
+  const int B = c->batch, H = g.hidden, D = g.head_dim;
+  const int nqkv = (g.n_heads + 2 * g.n_kv_heads) * D;
+  const int vheads = B * g.n_kv_heads;
+  const int acs = batch_attn_cluster(vheads, c->sm_count);
+  if (acs <= 0) return set_err(&c->msg, QB_ERR_UNSUPPORTED, "rows attention kernel unavailable");
+  cudaError_t e;
+  for (int l = 0; l < g.n_layers; ++l) {
+    const qb_layer_weights& w = c->layers[l];
+    RowsArgs a = rows_args(w.qkv, H, nqkv, B, l == 0 ? nullptr : c->r_xa, c->r_qkv, c->err);
+    a.gain = static_cast<const bf16*>(w.input_norm);
+    a.eps = g.rms_eps;
+    if (l == 0) {
+      a.embed = c->embed;
+      a.tokens = ids;
+      a.vocab = c->cfg.vocab;
+      a.x_copy = c->r_xa;
+    }
+    if ((e = launch_rows<EPI_STORE>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "batch qkv");
+    const size_t layer_off = (size_t)l * vheads * c->cap * D;
+    RopeRowsArgs ra;
+    std::memset(&ra, 0, sizeof(ra));
+    ra.qkv = c->r_qkv;
+    ra.q_norm = static_cast<const bf16*>(w.q_norm);
+    ra.k_norm = static_cast<const bf16*>(w.k_norm);
+    ra.cos = c->cos;
+    ra.sin = c->sin;
+    ra.eps = g.rms_eps;
+    ra.pos = pos;
+    ra.q_out = c->r_q;
+    ra.k_cache = c->kc + layer_off;
+    ra.v_cache = c->vc + layer_off;
+    ra.err = c->err;
+    ra.Q = B;
+    ra.Hq = g.n_heads;
+    ra.Hkv = g.n_kv_heads;
+    ra.cap = c->cap;
+    ra.batched = 1;
+    const int warps = B * (g.n_heads + 2 * g.n_kv_heads);
+    if ((e = launch_ex(rope_rows_kernel, dim3((warps + 3) / 4), dim3(128), 0, st, ra)) != cudaSuccess)
+      return cuda_fail(&c->msg, e, "batch rope");
+    AttnArgs at;
+    std::memset(&at, 0, sizeof(at));
+    at.q = c->r_q;
+    at.pos = pos;
+    at.k_cache = ra.k_cache;
+    at.v_cache = ra.v_cache;
+    at.out = c->r_attn;
+    at.counters = c->counters;
+    at.err = c->err;
+    at.Hq = B * g.n_heads;
+    at.Hkv = vheads;
+    at.Q = 1;
+    at.cap = c->cap;
+    at.batch_hkv = g.n_kv_heads;
+    if ((e = launch_attn_rows(c->dmk[l], c->dmv[l], at, acs, st)) != cudaSuccess)
+      return cuda_fail(&c->msg, e, "batch attention");
+    a = rows_args(w.o, g.n_heads * D, H, B, c->r_attn, c->r_xb, c->err);
+    a.residual = c->r_xa;
+    if ((e = launch_rows<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "batch o");
+    a = rows_args(w.gate_up, H, 2 * g.ffn, B, c->r_xb, c->r_act, c->err);
+    a.gain = static_cast<const bf16*>(w.post_norm);
+    a.eps = g.rms_eps;
+    if ((e = launch_rows<EPI_SWIGLU>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "batch gu");
+    a = rows_args(w.down, g.ffn, H, B, c->r_act, c->r_xa, c->err);
+    a.residual = c->r_xb;
+    if ((e = launch_rows<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "batch down");
+  }
+  if (head) {
+    RowsArgs a = rows_args(c->lm_head, H, g.vocab, B, c->r_xa, nullptr, c->err);
+    a.gain = c->final_norm;
+    a.eps = g.rms_eps;
+    a.logits = static_cast<bf16*>(logits);
+    a.part_val = c->r_val;
+    a.part_idx = c->r_idx;
+    a.counter = c->counters + 66;
+    a.tokens_out = tok_out;
+    if ((e = launch_rows<EPI_ARGMAX>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "batch head");
+  }
+  if ((e = launch_ex(add_rows_i64_kernel, dim3(1), dim3(32), 0, st, pos, B, 1ll)) != cudaSuccess)
+    return cuda_fail(&c->msg, e, "batch positions");
+  return QB_OK;
+}
+
 // Batched prefill scratch: per prompt row xa, xb, xn [H]; qkv; q, attn [Hq*D];
 // act [F] (bf16).
 struct PrefillLayout {
@@ -1256,6 +1375,7 @@ int check_verify_args(qb_ctx* c, const int64_t* ids, int n, const int64_t* pos, 
   if ((c->lc.n_heads / c->lc.n_kv_heads) * n > 32)
     return set_err(&c->msg, QB_ERR_UNSUPPORTED, "GQA group x verify rows above 32");
   if (c->tp_size != 1 && c->comm == nullptr) return set_err(&c->msg, QB_ERR_STATE, "tensor parallel communicator not initialised");
+  if (c->batch != 1) return set_err(&c->msg, QB_ERR_UNSUPPORTED, "verify takes one sequence");
   if (c->sm_count > 1024) return set_err(&c->msg, QB_ERR_UNSUPPORTED, "more than 1024 SMs");
   return QB_OK;
 }
@@ -1417,12 +1537,15 @@ int qb_bind_state(qb_ctx* c, void* k_cache, void* v_cache, int capacity, const v
   c->tmv.assign(g.n_layers, CUtensorMap());
   c->dmk.assign(g.n_layers, CUtensorMap());
   c->dmv.assign(g.n_layers, CUtensorMap());
+  // batched: layer l holds the B sequences' [Hkv][cap][D] slices one after
+  // another, so one map per layer covers B * Hkv heads
+  const int mh = g.n_kv_heads * c->batch;
   for (int l = 0; l < g.n_layers; ++l) {
-    const size_t off = (size_t)l * g.n_kv_heads * capacity * g.head_dim;
-    if (!make_kv_map(&c->tmk[l], c->kc + off, g.n_kv_heads, capacity) ||
-        !make_kv_map(&c->tmv[l], c->vc + off, g.n_kv_heads, capacity) ||
-        !make_kv_map(&c->dmk[l], c->kc + off, g.n_kv_heads, capacity, kDecKeys) ||
-        !make_kv_map(&c->dmv[l], c->vc + off, g.n_kv_heads, capacity, kDecKeys))
+    const size_t off = (size_t)l * mh * capacity * g.head_dim;
+    if (!make_kv_map(&c->tmk[l], c->kc + off, mh, capacity) ||
+        !make_kv_map(&c->tmv[l], c->vc + off, mh, capacity) ||
+        !make_kv_map(&c->dmk[l], c->kc + off, mh, capacity, kDecKeys) ||
+        !make_kv_map(&c->dmv[l], c->vc + off, mh, capacity, kDecKeys))
       return set_err(&c->msg, QB_ERR_CUDA, "cuTensorMapEncodeTiled failed for the KV cache");
   }
   if (c->exec) {
@@ -1516,7 +1639,20 @@ int qb_decode_step(qb_ctx* c, int64_t* token, int64_t* position, void* logits_ou
   int rc = require_ready(c);
   if (rc) return rc;
   if (!token || !position) return set_err(&c->msg, QB_ERR_ARG, "token/position are NULL");
+  if (c->batch > 1)
+    return run_batch_pass(c, token, position, token, logits_out, true, static_cast<cudaStream_t>(stream));
   return run_rows_decode(c, token, token, position, logits_out, true, static_cast<cudaStream_t>(stream));
+}
+
+int qb_set_batch(qb_ctx* c, int batch) {
+  if (!c) return set_err(nullptr, QB_ERR_ARG, "ctx is NULL");
+  if (batch < 1 || batch > kRowsMaxQ) return set_err(&c->msg, QB_ERR_UNSUPPORTED, "batch must lie in 1..8");
+  if (batch > 1 && c->tp_size != 1) return set_err(&c->msg, QB_ERR_UNSUPPORTED, "batched decode runs on one GPU");
+  if (batch != c->batch) {
+    c->batch = batch;
+    c->state_bound = false;  // the cache layout changed: bind the state again
+  }
+  return QB_OK;
 }
 
 int qb_prefill(qb_ctx* c, const int64_t* ids, int n, int64_t* token, int64_t* position, void* logits_out,
@@ -1526,8 +1662,21 @@ int qb_prefill(qb_ctx* c, const int64_t* ids, int n, int64_t* token, int64_t* po
   if (!ids || !token || !position || n <= 0) return set_err(&c->msg, QB_ERR_ARG, "bad prefill arguments");
   if (n > c->cap) return set_err(&c->msg, QB_ERR_CAPACITY, "prompt longer than the KV capacity");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaMemsetAsync(position, 0, sizeof(int64_t), st);
+  cudaError_t e = cudaMemsetAsync(position, 0, sizeof(int64_t) * c->batch, st);
   if (e != cudaSuccess) return cuda_fail(&c->msg, e, "position reset");
+  if (c->batch > 1) {
+    // ids [B][n]: one batched pass per prompt column (teacher forced), the
+    // column's ids gathered into the rows' token buffer
+    for (int i = 0; i < n; ++i) {
+      const bool last = (i == n - 1);
+      if ((e = launch_ex(gather_column_i64_kernel, dim3(1), dim3(32), 0, st, ids, n, i, c->batch, c->r_pos)) !=
+          cudaSuccess)
+        return cuda_fail(&c->msg, e, "prompt column");
+      rc = run_batch_pass(c, c->r_pos, position, token, last ? logits_out : nullptr, last, st);
+      if (rc) return rc;
+    }
+    return QB_OK;
+  }
   for (int i = 0; i < n; ++i) {
     const bool last = (i == n - 1);
     rc = run_rows_decode(c, ids + i, token, position, last ? logits_out : nullptr, last, st);
@@ -1550,6 +1699,7 @@ int qb_prefill_batched(qb_ctx* c, const int64_t* ids, int n, void* scratch, size
   if (!ids || !token || !position || n <= 0) return set_err(&c->msg, QB_ERR_ARG, "bad prefill arguments");
   if (n > c->cap) return set_err(&c->msg, QB_ERR_CAPACITY, "prompt longer than the KV capacity");
   if (c->tp_size != 1) return set_err(&c->msg, QB_ERR_UNSUPPORTED, "batched prefill runs on one GPU");
+  if (c->batch != 1) return set_err(&c->msg, QB_ERR_UNSUPPORTED, "block prefill takes one sequence (qb_prefill: batched contexts)");
   if (!ptr_ok(scratch) || scratch_bytes < prefill_layout(c, n).total)
     return set_err(&c->msg, QB_ERR_ARG, "scratch smaller than qb_prefill_scratch_bytes(n) or unaligned");
   return run_prefill_batched(c, ids, n, static_cast<uint8_t*>(scratch), token, position, logits_out,
@@ -1574,7 +1724,8 @@ int qb_capture_decode(qb_ctx* c, int64_t* token, int64_t* position, void* logits
     const bool with_step = c->step_ready;
     cudaError_t e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
     if (e != cudaSuccess) return cuda_fail(&c->msg, e, "begin capture");
-    rc = run_rows_decode(c, token, token, position, logits_out, true, st);
+    rc = c->batch > 1 ? run_batch_pass(c, token, position, token, logits_out, true, st)
+                      : run_rows_decode(c, token, token, position, logits_out, true, st);
     cudaGraph_t graph = nullptr;
     e = cudaStreamEndCapture(st, &graph);
     if (rc == QB_OK && e == cudaSuccess) {

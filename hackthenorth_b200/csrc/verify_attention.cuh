@@ -80,7 +80,9 @@ __global__ void __launch_bounds__(kVaThreads, 1)
   // positions are written by the previous kernel: read after the wait.
   pdl_wait();
   pdl_trigger();
-  long long last = a.pos[Qn - 1];
+  // batched decode: this KV head's sequence has its own position
+  const int64_t* posv = a.batch_hkv > 0 ? a.pos + kvh / a.batch_hkv : a.pos;
+  long long last = posv[Qn - 1];
   if (last < 0 || last >= a.cap) {
     if (tid == 0 && blockIdx.x == 0) report_error(a.err, DEV_BAD_POSITION);
     last = -1;
@@ -134,7 +136,7 @@ __global__ void __launch_bounds__(kVaThreads, 1)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int r = nt * 8 + 2 * t4 + e;
-        lim[nt][e] = r < R ? (int)a.pos[r % Qn] : -1;
+        lim[nt][e] = r < R ? (int)posv[r % Qn] : -1;
       }
     float o[8][NT][4];
     float m[NT][2], l[NT][2];

@@ -46,17 +46,29 @@ class DecodeState:
     captured decode graph (``dryft/engine/decode.py:102-206``).
 
     Capacity = prompt_length + output_length - 1 + draft slots. The caches are
-    zero-filled (finite), laid out ``[L, Hkv, capacity, D]``.
+    zero-filled (finite), laid out ``[L, Hkv, capacity, D]``; with ``batch`` B > 1
+    sequences (one GPU, B <= 8) ``[L, B, Hkv, capacity, D]``, and ``token`` /
+    ``position`` hold one entry per sequence.
     """
 
+    MAX_BATCH = 8
+
     def __init__(self, engine: "Engine", prompt_length: int, output_length: int,
-                 draft_tokens: int = 0, keep_logits: bool = False, capacity: Optional[int] = None):
+                 draft_tokens: int = 0, keep_logits: bool = False, capacity: Optional[int] = None,
+                 batch: int = 1):
         cfg = engine.cfg
         dev = engine.device
+        if not 1 <= batch <= self.MAX_BATCH:
+            raise ValueError(f"batch must lie in 1..{self.MAX_BATCH}")
+        if batch > 1 and engine.tp_size > 1:
+            raise ValueError("batched decode runs on one GPU")
         self.engine = engine
-        self.shape = (1, prompt_length, output_length)
+        self.batch = batch
+        self.shape = (batch, prompt_length, output_length)
         self.capacity = capacity or (prompt_length + max(output_length, 1) - 1 + draft_tokens)
-        shape = (cfg.n_layers, cfg.n_kv_heads // engine.tp_size, self.capacity, cfg.head_dim)
+        hkv = cfg.n_kv_heads // engine.tp_size
+        shape = ((cfg.n_layers, hkv, self.capacity, cfg.head_dim) if batch == 1
+                 else (cfg.n_layers, batch, hkv, self.capacity, cfg.head_dim))
         self.keys = torch.zeros(shape, dtype=BF16, device=dev)
         self.values = torch.zeros(shape, dtype=BF16, device=dev)
         cos, sin = rotary_table(cfg, self.capacity)
@@ -65,11 +77,13 @@ class DecodeState:
         nbytes = _lib.c_size_t()
         _lib.check(L.qb_workspace_bytes(engine.ctx, _lib.ctypes.byref(nbytes)), engine.ctx)
         self.workspace = torch.empty(nbytes.value, dtype=torch.uint8, device=dev)
-        self.token = torch.zeros(1, dtype=torch.int64, device=dev)
-        self.position = torch.zeros(1, dtype=torch.int64, device=dev)
-        self.prompt = torch.zeros(max(prompt_length, 1), dtype=torch.int64, device=dev)
-        # this rank's vocabulary shard under tensor parallelism
-        self.logits = torch.zeros(cfg.vocab // engine.tp_size, dtype=BF16, device=dev) if keep_logits else None
+        self.token = torch.zeros(batch, dtype=torch.int64, device=dev)
+        self.position = torch.zeros(batch, dtype=torch.int64, device=dev)
+        self.prompt = torch.zeros(batch * max(prompt_length, 1), dtype=torch.int64, device=dev)
+        # this rank's vocabulary shard under tensor parallelism; [B, V] batched
+        vshape = (cfg.vocab // engine.tp_size,) if batch == 1 else (batch, cfg.vocab)
+        self.logits = torch.zeros(vshape, dtype=BF16, device=dev) if keep_logits else None
+        _lib.check(L.qb_set_batch(engine.ctx, batch), engine.ctx)
         _lib.check(L.qb_bind_state(engine.ctx, self.keys.data_ptr(), self.values.data_ptr(), self.capacity,
                                    self.cos.data_ptr(), self.sin.data_ptr(), self.workspace.data_ptr(),
                                    self.workspace.numel()), engine.ctx)
@@ -85,13 +99,21 @@ class DecodeState:
         """Write K/V for the prompt, emit the first token into ``self.token``
         and set ``position = len(prompt)``. ``batched`` forces (True) or
         forbids (False) the dense-block path; by default it is used for
-        prompts of ``BATCHED_PREFILL_MIN`` rows or more on one GPU."""
-        n = ids.numel()
+        prompts of ``BATCHED_PREFILL_MIN`` rows or more on one GPU. With
+        ``batch`` B > 1, ``ids`` is ``[B, P]`` (equal prompt lengths) and the
+        prompts run as P teacher-forced batched passes."""
+        if self.batch > 1:
+            if ids.dim() != 2 or ids.shape[0] != self.batch:
+                raise ValueError(f"batched prefill takes ids of shape [{self.batch}, P]")
+            if batched:
+                raise ValueError("the dense-block prefill takes one sequence")
+            batched = False
+        n = ids.shape[-1] if self.batch > 1 else ids.numel()
         if n > self.capacity:
             raise ValueError("prompt longer than the KV capacity")
-        if n > self.prompt.numel():
-            self.prompt = torch.zeros(n, dtype=torch.int64, device=self.token.device)
-        self.prompt[:n].copy_(ids.reshape(-1), non_blocking=True)
+        if self.batch * n > self.prompt.numel():
+            self.prompt = torch.zeros(self.batch * n, dtype=torch.int64, device=self.token.device)
+        self.prompt[:self.batch * n].copy_(ids.reshape(-1), non_blocking=True)
         self._ensure_bound()
         L = _lib.load()
         if batched is None:
@@ -153,6 +175,8 @@ class DecodeState:
         from .speculate import verified_tokens
 
         self._ensure_bound()
+        if self.batch > 1:
+            raise ValueError("verify takes one sequence")
         n = len(proposal) + 1
         if n > 8:
             raise ValueError("verify takes at most 7 draft tokens")
@@ -260,8 +284,11 @@ class Engine:
 
     def generate(self, input_ids: List[List[int]], max_new_tokens: int, draft_tokens: int = 0,
                  drafter=None):
-        """Greedy continuation; yields ``[token]`` exactly ``max_new_tokens``
-        times (``dryft/engine/engine.py:202-249``).
+        """Greedy continuation; yields one token per sequence exactly
+        ``max_new_tokens`` times (``dryft/engine/engine.py:202-249``). One
+        sequence runs the batch-one decode path; 2..8 sequences of equal prompt
+        length run as one batched decode (every weight streamed once per step
+        for all of them).
 
         With ``draft_tokens`` k > 0 the loop speculates as the reference does:
         a drafter (default: ``PromptLookup`` over the prompt and the emitted
@@ -276,17 +303,21 @@ class Engine:
         if draft_tokens > 0:
             yield from self._generate_speculative(input_ids, max_new_tokens, draft_tokens, drafter)
             return
-        if len(input_ids) != 1:
-            raise ValueError("this engine implements the batch-one decode path")
-        prompt = list(input_ids[0])
-        if not prompt:
+        B = len(input_ids)
+        if not 1 <= B <= DecodeState.MAX_BATCH:
+            raise ValueError(f"this engine decodes 1..{DecodeState.MAX_BATCH} sequences")
+        prompts = [list(p) for p in input_ids]
+        if any(len(p) != len(prompts[0]) for p in prompts):
+            raise ValueError("the sequences of a batch must have equal prompt lengths")
+        if not prompts[0]:
             raise ValueError("the prompt must hold at least one token")
+        P = len(prompts[0])
         with torch.inference_mode():
-            shape = (1, len(prompt), max_new_tokens)
+            shape = (B, P, max_new_tokens)
             if self.state is None or self.state.shape != shape or self._bound_state is not self.state:
-                self.new_state(len(prompt), max_new_tokens)
+                self.new_state(P, max_new_tokens, batch=B)
             state = self.state
-            ids = torch.tensor(prompt, dtype=torch.int64).pin_memory()
+            ids = torch.tensor(prompts if B > 1 else prompts[0], dtype=torch.int64).pin_memory()
             state.prefill(ids.to(self.device, non_blocking=True))
             first = state.read_token()
             yield from stream_decode(state, first, max_new_tokens)

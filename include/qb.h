@@ -108,6 +108,18 @@ int qb_bind_state(qb_ctx* ctx, void* k_cache, void* v_cache, int capacity,
                   const void* rope_cos, const void* rope_sin,
                   void* workspace, size_t workspace_bytes);
 
+/* Batched decode: decode `batch` (1..8) sequences together on one GPU
+ * (DecodeState at B > 1, dryft/engine/decode.py:102-138). Call before
+ * qb_bind_state (a change of batch unbinds the state): the caches bound next
+ * are [L][batch][Hkv][capacity][D] (sequence b of layer l in slice b), and
+ * qb_decode_step / qb_capture_decode / qb_prefill then take token[batch] and
+ * position[batch] (one entry per sequence, positions may differ), logits
+ * [batch][V], and qb_prefill takes ids [batch][n]. Every weight is streamed
+ * once per step for all sequences (the rows kernels of the verify pass).
+ * qb_verify and qb_prefill_batched take one sequence. QB_ERR_UNSUPPORTED for
+ * batch > 1 under tensor parallelism. */
+int qb_set_batch(qb_ctx* ctx, int batch);
+
 /* One batch-one decode step: DecodeState.step (dryft/engine/decode.py:126-138).
  * Reads *token (int64, device) at *position (int64, device), appends its K/V,
  * writes the greedy next token to *token and increments *position.
