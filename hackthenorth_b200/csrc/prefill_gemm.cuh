@@ -7,19 +7,23 @@
 // (dryft/engine/attention.py:92-98 uses torch linear for prompt rows; the
 // roundings are those of kernels/projection.py:13-83 and down.py:8-35).
 //
-// Per CTA one 128 x 256 output tile (128 prompt rows x 256 weight rows):
+// Output tiles of 128 x 256 (128 prompt rows x 256 weight rows); one
+// persistent CTA per SM walks tiles b, b + G, ...:
 //  * warp 0, one lane: TMA producer. X tile [128 rows][64 cols] and W tile
 //    [256 rows][64 cols] per K block (128-byte swizzle, no multicast) into a
-//    4-stage ring of 48 KB;
-//  * warp 1: allocates 256 TMEM columns (128 lanes x 256 fp32 accumulators);
-//    one lane issues 4 tcgen05.mma.cta_group::1.kind::f16 (M 128, N 256, K 16)
-//    per K block with shared-memory descriptors of both operands (K-major,
-//    128-byte swizzle), and tcgen05.commit frees each stage once its MMAs
-//    have read it; a last commit signals the accumulators complete;
+//    4-stage ring of 48 KB, continuously across the CTA's tiles;
+//  * warp 1: allocates 512 TMEM columns (two 128-lane x 256-column fp32
+//    accumulators); one lane issues 4 tcgen05.mma.cta_group::1.kind::f16
+//    (M 128, N 256, K 16) per K block with shared-memory descriptors of both
+//    operands (K-major, 128-byte swizzle); tcgen05.commit frees each stage once
+//    its MMAs have read it and signals a tile's accumulator complete; tile i
+//    uses accumulator i & 1 once the epilogue has drained tile i - 2;
 //  * warps 2-5: each reads its 32 TMEM lanes (32 prompt rows) with
-//    tcgen05.ld.32x32b and runs the epilogue on 8 columns at a time.
+//    tcgen05.ld.32x32b and runs the epilogue on 8 columns at a time, under
+//    the MMAs of the next tile.
 // Every wait is bounded (the kernel records an error and returns), and TMEM is
-// released by warp 1 after all readers are done, on every path.
+// released by warp 1 after its MMAs have completed and all readers are done,
+// on every path.
 #pragma once
 #include "common.cuh"
 
@@ -44,7 +48,7 @@ struct PgArgs {
   int* err;
 };
 
-__host__ inline size_t pg_smem_bytes() { return 1024 + (size_t)kPgStages * kPgStageBytes + 256; }
+__host__ inline size_t pg_smem_bytes() { return 1024 + (size_t)kPgStages * kPgStageBytes + 256; }  // + barriers, TMEM slot
 
 // Shared-memory matrix descriptor, K-major operand with 128-byte swizzle:
 // start address >> 4 at [0,14), leading byte offset (unused for swizzled
@@ -88,6 +92,43 @@ __device__ __forceinline__ void tc_ld8(uint32_t taddr, float (&v)[8]) {
 }
 
 template <int EPI>
+__device__ __forceinline__ void pg_epilogue_store(const PgArgs& a, int row, int n, const float (&v)[8]) {
+  if constexpr (EPI == PG_STORE) {
+    uint4 o;
+    o.x = pack_bf16(v[0], v[1]);
+    o.y = pack_bf16(v[2], v[3]);
+    o.z = pack_bf16(v[4], v[5]);
+    o.w = pack_bf16(v[6], v[7]);
+    *reinterpret_cast<uint4*>(a.out + (size_t)row * a.N + n) = o;
+  } else if constexpr (EPI == PG_RESIDUAL) {
+    const uint4 r = *reinterpret_cast<const uint4*>(a.residual + (size_t)row * a.N + n);
+    const uint32_t* pr = reinterpret_cast<const uint32_t*>(&r);
+    uint4 o;
+    uint32_t* po = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      po[j] = pack_bf16(round_bf16(v[2 * j]) + bf_lo(pr[j]), round_bf16(v[2 * j + 1]) + bf_hi(pr[j]));
+    *reinterpret_cast<uint4*>(a.out + (size_t)row * a.N + n) = o;
+  } else {  // PG_SWIGLU: columns (2j, 2j+1) = (gate j, up j)
+    float h[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float act = round_bf16(silu_f32(round_bf16(v[2 * j])));
+      h[j] = act * round_bf16(v[2 * j + 1]);
+    }
+    uint2 o;
+    o.x = pack_bf16(h[0], h[1]);
+    o.y = pack_bf16(h[2], h[3]);
+    *reinterpret_cast<uint2*>(a.out + (size_t)row * (a.N / 2) + n / 2) = o;
+  }
+}
+
+// Persistent: CTA b takes tiles b, b + G, b + 2G, ... (m tile fastest, so
+// consecutive CTAs share a weight tile in L2). The producer and the MMA lane
+// run through the k blocks of all their tiles without stopping; the MMA lane
+// alternates between two 256-column accumulators in TMEM, so the epilogue of
+// tile i (acc_full -> read -> acc_empty) overlaps the MMAs of tile i + 1.
+template <int EPI>
 __global__ void __launch_bounds__(kPgThreads, 1)
     prefill_gemm_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmw,
                         const PgArgs a) {
@@ -95,20 +136,27 @@ __global__ void __launch_bounds__(kPgThreads, 1)
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(ring + kPgStages * kPgStageBytes);
   uint64_t* empty = full + kPgStages;
-  uint64_t* done = empty + kPgStages;
+  uint64_t* acc_full = empty + kPgStages;  // [2] MMAs of the buffer's tile complete
+  uint64_t* acc_empty = acc_full + 2;      // [2] the 4 epilogue warps have read the buffer
+  uint64_t* done = acc_empty + 2;          // every MMA this CTA issued has completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* flags = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * kPgBM;
-  const int n0 = blockIdx.y * kPgBN;
   const int nkb = (a.K + kPgBK - 1) / kPgBK;
+  const int mt = (a.T + kPgBM - 1) / kPgBM;
+  const int tiles = mt * ((a.N + kPgBN - 1) / kPgBN);
+  const int my_tiles = blockIdx.x < tiles ? (tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kPgStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
     }
     mbar_init(done, 1);
     fence_mbar_init();
@@ -116,7 +164,7 @@ __global__ void __launch_bounds__(kPgThreads, 1)
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                 "r"(kPgTmemCols)
+                 "r"(2 * kPgTmemCols)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -133,94 +181,92 @@ __global__ void __launch_bounds__(kPgThreads, 1)
     if (lane == 0) {
       prefetch_tensormap(&tmx);
       prefetch_tensormap(&tmw);
-      int issued = 0;
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % kPgStages;
-        if (kb >= kPgStages &&
-            !mbar_wait(&empty[s], ((kb / kPgStages) - 1) & 1, a.err, DEV_TIMEOUT_GEMV_EMPTY)) {
-          flags[0] = 1;
-          break;
+      int g = 0;  // k blocks issued over all tiles
+      for (int i = 0; i < my_tiles && flags[0] == 0; ++i) {
+        const int t = blockIdx.x + i * gridDim.x;
+        const int m0 = (t % mt) * kPgBM, n0 = (t / mt) * kPgBN;
+        for (int kb = 0; kb < nkb; ++kb, ++g) {
+          const int s = g % kPgStages;
+          if (g >= kPgStages && !mbar_wait(&empty[s], ((g / kPgStages) - 1) & 1, a.err, DEV_TIMEOUT_GEMV_EMPTY)) {
+            flags[0] = 1;
+            break;
+          }
+          uint8_t* st = ring + s * kPgStageBytes;
+          mbar_arrive_expect_tx(&full[s], kPgStageBytes);
+          tma_load_2d(st, &tmx, kb * kPgBK, m0, &full[s]);
+          tma_load_2d(st + kPgABytes, &tmw, kb * kPgBK, n0, &full[s]);
         }
-        uint8_t* st = ring + s * kPgStageBytes;
-        mbar_arrive_expect_tx(&full[s], kPgStageBytes);
-        tma_load_2d(st, &tmx, kb * kPgBK, m0, &full[s]);
-        tma_load_2d(st + kPgABytes, &tmw, kb * kPgBK, n0, &full[s]);
-        issued = kb + 1;
       }
       // keep shared memory alive until every issued copy has landed
-      for (int kb = (issued > kPgStages ? issued - kPgStages : 0); kb < issued; ++kb)
-        mbar_wait(&full[kb % kPgStages], (kb / kPgStages) & 1, nullptr, 0);
+      for (int c = (g > kPgStages ? g - kPgStages : 0); c < g; ++c)
+        mbar_wait(&full[c % kPgStages], (c / kPgStages) & 1, nullptr, 0);
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = pg_idesc(kPgBM, kPgBN);
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % kPgStages;
-        if (!mbar_wait(&full[s], (kb / kPgStages) & 1, a.err, DEV_TIMEOUT_GEMV_FULL)) {
-          flags[0] = 1;
-          break;
-        }
-        tc_fence_after();
-        const uint8_t* st = ring + s * kPgStageBytes;
-        const uint64_t ad = pg_desc(st), bd = pg_desc(st + kPgABytes);
+      int g = 0;  // k blocks consumed over all tiles
+      for (int i = 0; i < my_tiles; ++i) {
+        const int ab = i & 1;
+        const uint32_t acc = tmem + (uint32_t)(ab * kPgTmemCols);
+        // the epilogue of tile i - 2 has read this buffer
+        bool ok = flags[0] == 0;
+        if (ok && i >= 2 && !mbar_wait(&acc_empty[ab], ((i >> 1) - 1) & 1, a.err, DEV_TIMEOUT_ATTN_FULL)) ok = false;
+        if (ok) tc_fence_after();
+        for (int kb = 0; kb < nkb && ok; ++kb, ++g) {
+          const int s = g % kPgStages;
+          if (!mbar_wait(&full[s], (g / kPgStages) & 1, a.err, DEV_TIMEOUT_GEMV_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* st = ring + s * kPgStageBytes;
+          const uint64_t ad = pg_desc(st), bd = pg_desc(st + kPgABytes);
 #pragma unroll
-        for (int k = 0; k < kPgBK / 16; ++k)  // K 16 per MMA = 32 bytes along the swizzled row
-          tc_mma(tmem, ad + (uint64_t)(k * 2), bd + (uint64_t)(k * 2), idesc, (kb | k) != 0 ? 1u : 0u);
-        tc_commit(&empty[s]);  // the stage is free once these MMAs have read it
+          for (int k = 0; k < kPgBK / 16; ++k)  // K 16 per MMA = 32 bytes along the swizzled row
+            tc_mma(acc, ad + (uint64_t)(k * 2), bd + (uint64_t)(k * 2), idesc, (kb | k) != 0 ? 1u : 0u);
+          tc_commit(&empty[s]);  // the stage is free once these MMAs have read it
+        }
+        if (!ok) flags[0] = 1;
+        tc_commit(&acc_full[ab]);  // this tile's MMAs complete (also after a stop: wakes the epilogue)
+        if (!ok) break;
       }
-      tc_commit(done);  // all issued MMAs complete (also after an early stop)
+      // TMEM is released below only after every MMA issued here has completed
+      // (on the normal path the epilogue has already seen them all)
+      tc_commit(done);
+      mbar_wait(done, 0, nullptr, 0);
     }
     __syncwarp();
   } else {
     // --------------------------------------------------------------- epilogue
     const int q = warp & 3;  // TMEM lanes 32q .. 32q+31
-    const int row = m0 + 32 * q + lane;
-    const bool ok = mbar_wait(done, 0, a.err, DEV_TIMEOUT_ATTN_FULL) && flags[0] == 0;
-    tc_fence_after();
-    if (ok) {
+    for (int i = 0; i < my_tiles; ++i) {
+      const int ab = i & 1;
+      const int t = blockIdx.x + i * gridDim.x;
+      const int m0 = (t % mt) * kPgBM, n0 = (t / mt) * kPgBN;
+      const int row = m0 + 32 * q + lane;
+      const bool ok = mbar_wait(&acc_full[ab], (i >> 1) & 1, a.err, DEV_TIMEOUT_ATTN_FULL) && flags[0] == 0;
+      tc_fence_after();
+      if (!ok) break;
+      const uint32_t base = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(ab * kPgTmemCols);
       for (int c = 0; c < kPgBN; c += 8) {
         float v[8];
-        tc_ld8(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c, v);
+        tc_ld8(base + (uint32_t)c, v);
         const int n = n0 + c;
-        if (row >= a.T || n >= a.N) continue;
-        if constexpr (EPI == PG_STORE) {
-          uint4 o;
-          o.x = pack_bf16(v[0], v[1]);
-          o.y = pack_bf16(v[2], v[3]);
-          o.z = pack_bf16(v[4], v[5]);
-          o.w = pack_bf16(v[6], v[7]);
-          *reinterpret_cast<uint4*>(a.out + (size_t)row * a.N + n) = o;
-        } else if constexpr (EPI == PG_RESIDUAL) {
-          const uint4 r = *reinterpret_cast<const uint4*>(a.residual + (size_t)row * a.N + n);
-          const uint32_t* pr = reinterpret_cast<const uint32_t*>(&r);
-          uint4 o;
-          uint32_t* po = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            po[j] = pack_bf16(round_bf16(v[2 * j]) + bf_lo(pr[j]), round_bf16(v[2 * j + 1]) + bf_hi(pr[j]));
-          *reinterpret_cast<uint4*>(a.out + (size_t)row * a.N + n) = o;
-        } else {  // PG_SWIGLU: columns (2j, 2j+1) = (gate j, up j)
-          float h[4];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const float act = round_bf16(silu_f32(round_bf16(v[2 * j])));
-            h[j] = act * round_bf16(v[2 * j + 1]);
-          }
-          uint2 o;
-          o.x = pack_bf16(h[0], h[1]);
-          o.y = pack_bf16(h[2], h[3]);
-          *reinterpret_cast<uint2*>(a.out + (size_t)row * (a.N / 2) + n / 2) = o;
-        }
+        if (row < a.T && n < a.N) pg_epilogue_store<EPI>(a, row, n, v);
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[ab]);
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPgTmemCols) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kPgTmemCols)
+                 : "memory");
   }
 }
 

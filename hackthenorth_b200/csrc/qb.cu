@@ -265,8 +265,10 @@ cudaError_t launch_prefill_gemm(int epi, const bf16* x, const bf16* w, bf16* out
     if (e != cudaSuccess) return e;
     attr[epi] = true;
   }
-  const dim3 grid((T + kPgBM - 1) / kPgBM, (N + kPgBN - 1) / kPgBN);
-  return launch_ex(k, grid, dim3(kPgThreads), smem, st, tx, tw, a);
+  // persistent: one CTA per SM (at most one per tile)
+  const long long tiles = (long long)((T + kPgBM - 1) / kPgBM) * ((N + kPgBN - 1) / kPgBN);
+  const int grid = (int)std::min<long long>(tiles, current_sm_count());
+  return launch_ex(k, dim3(grid), dim3(kPgThreads), smem, st, tx, tw, a);
 }
 
 int attn_splits_for(int hkv, int sm_count) {
