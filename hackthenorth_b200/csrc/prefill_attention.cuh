@@ -36,7 +36,7 @@ struct FpArgs {
 
 __host__ inline size_t fp_smem_bytes() { return 1024 + (size_t)kFpStages * kAttnStageBytes + 2 * kFpStages * 8 + 64; }
 
-__global__ void __launch_bounds__(kFpThreads, 1)
+__global__ void __launch_bounds__(kFpThreads, 2)
     flash_prefill_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                          const FpArgs a) {
   extern __shared__ uint8_t smem_raw[];
