@@ -427,7 +427,9 @@ def run_attention_sweep(args):
     """Decode-attention op sweep (GQA 32/8, D 128, bf16 N(0,1), batch 1):
     KV lengths 512..131072, 1 query row and the 5-row causal verify variant.
     Each timed launch reads a different KV buffer (>= 256 MB cycled), so the
-    K/V bytes come from HBM. One JSON line with a per-case list."""
+    K/V bytes come from HBM. "us" is device time per call (the timed calls
+    replayed as one CUDA graph); "us_host" the same calls issued one by one
+    from Python. One JSON line with a per-case list."""
     from hackthenorth_b200 import build as qbuild
     from hackthenorth_b200 import ops
 
@@ -449,6 +451,7 @@ def run_attention_sweep(args):
             torch.cuda.synchronize()
             reps = max(args.warmup + 3, 40 if L <= 4096 else 10)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            # host-driven: one op call per launch from Python (tensor maps encoded per call)
             e0.record()
             for i in range(reps):
                 k, v = kv[i % nbuf]
@@ -456,10 +459,28 @@ def run_attention_sweep(args):
             e1.record()
             torch.cuda.synchronize()
             ops.check_device_errors()
-            sec = e0.elapsed_time(e1) / 1000.0 / reps
+            host_sec = e0.elapsed_time(e1) / 1000.0 / reps
+            # device time: the same calls captured once as a CUDA graph and replayed
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for i in range(reps):
+                    k, v = kv[i % nbuf]
+                    ops.grouped_attention(q, k, v, pos)
+            graph.replay()
+            torch.cuda.synchronize()
+            replays = 3
+            e0.record()
+            for _ in range(replays):
+                graph.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            ops.check_device_errors()
+            sec = e0.elapsed_time(e1) / 1000.0 / (replays * reps)
+            del graph
             nbytes = per_call + 2 * q.numel() * 2 + queries * 8
             cases.append({"kv_len": L, "queries": queries, "us": round(sec * 1e6, 2),
-                          "GBps": round(nbytes / sec / 1e9, 1), "frac": round(nbytes / sec / 1e9 / peak_gbs, 4)})
+                          "GBps": round(nbytes / sec / 1e9, 1), "frac": round(nbytes / sec / 1e9 / peak_gbs, 4),
+                          "us_host": round(host_sec * 1e6, 2)})
             del kv
             torch.cuda.empty_cache()
     print(json.dumps({"op": "grouped_attention", "metric": "decode attention us and GB/s of K/V reads",

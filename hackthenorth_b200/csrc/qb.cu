@@ -47,6 +47,7 @@ constexpr int kMaxGemvStages = 12;
 constexpr size_t kOpScratchBytes = 16u << 20;
 
 // Op-level scratch layout (bytes).
+constexpr int kOpRowsMaxCap = 16384;     // op attention: cluster rows kernel below this capacity
 constexpr size_t kScrErr = 0;
 constexpr size_t kScrCounters = 256;       // unsigned[192]
 constexpr size_t kScrHeadVal = 1024;       // float[1024]
@@ -1961,7 +1962,15 @@ static int op_attention(const void* qkv, const void* q, const void* q_norm, cons
   a.Q = queries;
   a.cap = cap;
   a.splits = splits;
-  cudaError_t e = launch_attn(tk, tv, &dk, &dv, a, pro, static_cast<cudaStream_t>(stream));
+  cudaError_t e;
+  // Short caches without the prologue: the cluster kernel of the verify pass
+  // (DSMEM merge, no global round trip); long caches keep the split kernel,
+  // whose grid covers every SM.
+  const int rcs = (!pro && rows <= kVaMaxRows && cap < kOpRowsMaxCap) ? rows_cluster_size(hkv) : 0;
+  if (rcs > 0)
+    e = launch_attn_rows(dk, dv, a, rcs, static_cast<cudaStream_t>(stream));
+  else
+    e = launch_attn(tk, tv, &dk, &dv, a, pro, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(nullptr, e, "attention launch");
   return QB_OK;
 }
