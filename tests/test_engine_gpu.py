@@ -84,8 +84,12 @@ def test_generate_contract_and_repeated_prompts(small_engine):
             assert len(out) == n_new and all(len(s) == 1 for s in out)
             o = OracleQwen3(QWEN3_SMALL, oracle_state, 12 + n_new)
             assert [s[0] for s in out] == o.greedy(prompt, n_new)
+    # 2..8 equal-length prompts decode as one batch (test_batch_gpu.py); unequal
+    # prompt lengths and more than 8 sequences are contract violations
     with pytest.raises(ValueError):
-        list(small_engine.generate([[1, 2], [3, 4]], 2))
+        list(small_engine.generate([[1, 2], [3]], 2))
+    with pytest.raises(ValueError):
+        list(small_engine.generate([[1, 2]] * 9, 2))
 
 
 def test_stale_cache_slots_are_never_read(small_engine):
