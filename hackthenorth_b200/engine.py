@@ -27,18 +27,63 @@ from .weights import PackedWeights, load_checkpoint, random_state_dict, rotary_t
 BF16 = torch.bfloat16
 
 
-def stream_decode(state, first_tokens: List[int], output_length: int) -> Iterator[List[int]]:
-    """Overlap the next graph replay with delivery of an already-read token
+class _TokenHandle:
+    """A decode step's tokens on their way to the host: a pinned ring slot
+    filled by an asynchronous device-to-host copy, and the event after it."""
+
+    __slots__ = ("host", "event")
+
+    def __init__(self, host, event):
+        self.host, self.event = host, event
+
+    def result(self) -> List[int]:
+        self.event.synchronize()
+        return self.host.tolist()
+
+
+def stream_decode(state, first_tokens: List[int], output_length: int, depth: int = 1) -> Iterator[List[int]]:
+    """Overlap graph replays with the delivery of tokens already read
     (``dryft/engine/decode.py:8-22``): the final yield has no outstanding replay
-    and ``output_length == 1`` launches none."""
-    tokens = first_tokens
-    for step in range(output_length):
-        has_next = step + 1 < output_length
-        if has_next:
-            state.step()
-        yield tokens
-        if has_next:
-            tokens = state.read_token()
+    and ``output_length == 1`` launches none.
+
+    ``depth`` 1 is the reference's order (the next replay is launched, the
+    current token yielded, then the new token read synchronously). With
+    ``depth`` d > 1 and a state offering ``read_token_async`` (a device-to-host
+    token ring), up to d replays run ahead of the consumer: each replay's
+    tokens are copied asynchronously into a pinned slot, and a yield waits
+    only for its own step, so the GPU never idles between steps while the
+    host converts and yields."""
+    if depth <= 1 or not hasattr(state, "read_token_async"):
+        tokens = first_tokens
+        for step in range(output_length):
+            has_next = step + 1 < output_length
+            if has_next:
+                state.step()
+            yield tokens
+            if has_next:
+                tokens = state.read_token()
+        return
+    from collections import deque
+
+    pending = deque()
+    issued = 0
+    total = output_length - 1  # replays needed
+
+    def launch():
+        nonlocal issued
+        state.step()
+        pending.append(state.read_token_async(depth + 1))
+        issued += 1
+
+    while issued < min(depth, total):
+        launch()
+    if output_length >= 1:
+        yield first_tokens
+    for _ in range(total):
+        handle = pending.popleft()
+        if issued < total:
+            launch()
+        yield handle.result()
 
 
 class DecodeState:
@@ -159,6 +204,21 @@ class DecodeState:
     def read_token(self) -> List[int]:
         return self.token.tolist()
 
+    def read_token_async(self, slots: int = 3) -> _TokenHandle:
+        """Queue a device-to-host copy of ``token`` (after the work queued so
+        far on the current stream) into the next of ``slots`` pinned host
+        slots; ``.result()`` waits for that copy only."""
+        ring = getattr(self, "_token_ring", None)
+        if ring is None or len(ring) != slots:
+            ring = [(torch.empty(self.batch, dtype=torch.int64).pin_memory(), torch.cuda.Event())
+                    for _ in range(slots)]
+            self._token_ring, self._ring_next = ring, 0
+        host, event = ring[self._ring_next % slots]
+        self._ring_next += 1
+        host.copy_(self.token, non_blocking=True)
+        event.record()
+        return _TokenHandle(host, event)
+
     def check(self) -> None:
         """Synchronise and raise on a device-side error (bounded wait gave up,
         token or position out of range)."""
@@ -219,6 +279,9 @@ class DecodeState:
 class Engine:
     """``Engine(model_path)``: load an HF Qwen3 checkpoint to ``cuda:0`` in the
     engine layout; ``generate`` streams greedy tokens."""
+
+    # decode replays in flight ahead of the consumer in ``generate``
+    STREAM_DEPTH = 2
 
     def __init__(self, model_path: Optional[str] = None, device: str = "cuda:0", *,
                  cfg: Optional[ModelConfig] = None, state: Optional[Dict[str, torch.Tensor]] = None,
@@ -320,7 +383,7 @@ class Engine:
             ids = torch.tensor(prompts if B > 1 else prompts[0], dtype=torch.int64).pin_memory()
             state.prefill(ids.to(self.device, non_blocking=True))
             first = state.read_token()
-            yield from stream_decode(state, first, max_new_tokens)
+            yield from stream_decode(state, first, max_new_tokens, depth=self.STREAM_DEPTH)
 
     def _generate_speculative(self, input_ids, max_new_tokens: int, k: int, drafter):
         from .speculate import PromptLookup

@@ -96,11 +96,20 @@ def test_gate_up_interleave_and_checkpoint_roundtrip(tmp_path):
     assert all(torch.equal(state[k], loaded[k]) for k in state)
 
 
-def test_stream_decode_launches_before_yield_without_extra_steps():
-    # dryft/tests/test_decode.py:20-38
+@pytest.mark.parametrize("depth", [1, 2, 3])
+def test_stream_decode_launches_before_yield_without_extra_steps(depth):
+    # dryft/tests/test_decode.py:20-38; depth > 1: a token ring keeps that many
+    # replays ahead of the consumer, tokens still in order, no extra replays
     from hackthenorth_b200.engine import stream_decode
 
-    for length in (1, 2, 5):
+    class Handle:
+        def __init__(self, value):
+            self.value = value
+
+        def result(self):
+            return [self.value]
+
+    for length in (1, 2, 5, 9):
         token = [0]
         launches = []
 
@@ -109,9 +118,11 @@ def test_stream_decode_launches_before_yield_without_extra_steps():
             launches.append(1)
 
         state = SimpleNamespace(step=step, read_token=lambda: list(token))
+        if depth > 1:
+            state.read_token_async = lambda slots: Handle(token[0])
         saved = []
-        for i, out in enumerate(stream_decode(state, [0], length)):
+        for i, out in enumerate(stream_decode(state, [0], length, depth=depth)):
             assert out == [i]
-            assert len(launches) == min(i + 1, length - 1)
+            assert len(launches) == min(i + depth, length - 1)
             saved.append(out)
-        assert len(launches) == length - 1
+        assert len(launches) == length - 1 and len(saved) == length
