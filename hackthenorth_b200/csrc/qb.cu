@@ -1383,6 +1383,27 @@ int check_verify_args(qb_ctx* c, const int64_t* ids, int n, const int64_t* pos, 
   return QB_OK;
 }
 
+// Captured graphs hold the bound state's pointers: drop them whenever the
+// state (or its layout) changes.
+void drop_graphs(qb_ctx* c) {
+  if (c->exec) {
+    cudaGraphExecDestroy(c->exec);
+    c->exec = nullptr;
+  }
+  if (c->graph) {
+    cudaGraphDestroy(c->graph);
+    c->graph = nullptr;
+  }
+  if (c->vexec) {
+    cudaGraphExecDestroy(c->vexec);
+    c->vexec = nullptr;
+  }
+  if (c->vgraph) {
+    cudaGraphDestroy(c->vgraph);
+    c->vgraph = nullptr;
+  }
+}
+
 int require_ready(qb_ctx* c) {
   if (!c) return set_err(nullptr, QB_ERR_ARG, "ctx is NULL");
   if (!c->weights_bound) return set_err(&c->msg, QB_ERR_STATE, "weights not bound");
@@ -1551,22 +1572,7 @@ int qb_bind_state(qb_ctx* c, void* k_cache, void* v_cache, int capacity, const v
         !make_kv_map(&c->dmv[l], c->vc + off, mh, capacity, kDecKeys))
       return set_err(&c->msg, QB_ERR_CUDA, "cuTensorMapEncodeTiled failed for the KV cache");
   }
-  if (c->exec) {
-    cudaGraphExecDestroy(c->exec);
-    c->exec = nullptr;
-  }
-  if (c->graph) {
-    cudaGraphDestroy(c->graph);
-    c->graph = nullptr;
-  }
-  if (c->vexec) {
-    cudaGraphExecDestroy(c->vexec);
-    c->vexec = nullptr;
-  }
-  if (c->vgraph) {
-    cudaGraphDestroy(c->vgraph);
-    c->vgraph = nullptr;
-  }
+  drop_graphs(c);
   c->state_bound = true;
   prepare_step(c);
   return QB_OK;
@@ -1654,6 +1660,8 @@ int qb_set_batch(qb_ctx* c, int batch) {
   if (batch != c->batch) {
     c->batch = batch;
     c->state_bound = false;  // the cache layout changed: bind the state again
+    drop_graphs(c);
+    release_step(c);
   }
   return QB_OK;
 }
@@ -1751,7 +1759,7 @@ int qb_capture_decode(qb_ctx* c, int64_t* token, int64_t* position, void* logits
 
 int qb_replay_decode(qb_ctx* c, void* stream) {
   if (!c) return set_err(nullptr, QB_ERR_ARG, "ctx is NULL");
-  if (!c->exec) return set_err(&c->msg, QB_ERR_STATE, "no captured decode graph");
+  if (!c->exec || !c->state_bound) return set_err(&c->msg, QB_ERR_STATE, "no captured decode graph");
   cudaError_t e = cudaGraphLaunch(c->exec, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(&c->msg, e, "graph launch");
   return QB_OK;
@@ -1799,7 +1807,7 @@ int qb_capture_verify(qb_ctx* c, const int64_t* ids, int n, const int64_t* posit
 
 int qb_replay_verify(qb_ctx* c, void* stream) {
   if (!c) return set_err(nullptr, QB_ERR_ARG, "ctx is NULL");
-  if (!c->vexec) return set_err(&c->msg, QB_ERR_STATE, "no captured verify graph");
+  if (!c->vexec || !c->state_bound) return set_err(&c->msg, QB_ERR_STATE, "no captured verify graph");
   cudaError_t e = cudaGraphLaunch(c->vexec, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(&c->msg, e, "graph launch");
   return QB_OK;
