@@ -1,4 +1,5 @@
-"""Drop-in ``Engine`` for the dryft batch-one Qwen3 decode path, on sm_100a kernels.
+"""Drop-in ``Engine`` for the dryft Qwen3 decode path (batch one, plus batched
+decode of up to 8 equal-length prompts), on sm_100a kernels.
 
 Public API (``dryft/QWEN_ENGINE_CONTRACT.md:25-36``, ``dryft/engine/engine.py:175-249``):
 
@@ -6,8 +7,8 @@ Public API (``dryft/QWEN_ENGINE_CONTRACT.md:25-36``, ``dryft/engine/engine.py:17
     for step in engine.generate(input_ids, max_new_tokens):
         ...                                           # step == [token_id]
 
-``generate`` yields a one-element list exactly ``max_new_tokens`` times and
-never stops at an end-of-sequence token. The internal entry points the north
+``generate`` yields one token id per sequence exactly ``max_new_tokens``
+times and never stops at an end-of-sequence token. The internal entry points the north
 star names map as follows: load = ``Engine.__init__``; prefill =
 ``DecodeState.prefill``; decode_step = ``DecodeState.step`` (a replay of the
 captured graph); generate = ``Engine.generate``.
