@@ -47,6 +47,16 @@ constexpr int kAttnBarrierId = 2;
 constexpr int kAttnMinSplitKeys = 256;
 constexpr float kLog2e = 1.4426950408889634f;
 
+// Split length for n live keys over at most `want` splits (16-aligned), and
+// the number of splits that receive keys: rounding the length up can leave the
+// last of `want` splits empty, and those are dropped, so every split below the
+// returned count has k0 = split * per < n (merges never see an empty split).
+__device__ __forceinline__ int2 attn_split_len(int n, int want) {
+  int per = (n + max(1, want) - 1) / max(1, want);
+  per = (per + kAttnSub - 1) & ~(kAttnSub - 1);
+  return make_int2(per, per > 0 ? max(1, (n + per - 1) / per) : 1);
+}
+
 struct AttnArgs {
   const bf16* qkv;       // PRO: packed row [Hq*D + 2*Hkv*D]
   const bf16* q;         // plain: [Q][Hq][D]
@@ -505,9 +515,9 @@ __device__ __forceinline__ AttnRange attn_setup(const AttnArgs& a, const AttnSme
   R.n = (int)last + 1;
   // Splits actually used: about kAttnMinSplitKeys keys each, at most the
   // grid's split count. Short contexts then need no merge at all.
-  R.Se = max(1, min(a.splits, (R.n + kAttnMinSplitKeys - 1) / kAttnMinSplitKeys));
-  int per = (R.n + R.Se - 1) / R.Se;
-  per = (per + kAttnSub - 1) & ~(kAttnSub - 1);
+  const int2 sl = attn_split_len(R.n, min(a.splits, (R.n + kAttnMinSplitKeys - 1) / kAttnMinSplitKeys));
+  const int per = sl.x;
+  R.Se = sl.y;
   R.k0 = min(R.n, split * per);
   R.k1 = min(R.n, R.k0 + per);
   R.nst = (R.k1 - R.k0 + kAttnKeys - 1) / kAttnKeys;

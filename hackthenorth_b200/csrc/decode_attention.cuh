@@ -140,11 +140,10 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   // kDecShortSplits (at least one cluster's worth) below kDecMultiClusterKeys
   // live keys, up to C clusters' worth above. Cluster cl takes global splits [cl*S, cl*S+S).
   const int cmax = n >= kDecMultiClusterKeys ? C : min(C, max(1, kDecShortSplits / S));
-  const int SeT = max(1, min(cmax * S, (n + kAttnMinSplitKeys - 1) / kAttnMinSplitKeys));
+  const int2 sl = attn_split_len(n, min(cmax * S, (n + kAttnMinSplitKeys - 1) / kAttnMinSplitKeys));
+  const int per = sl.x, SeT = sl.y;            // every split below SeT has keys
   const int Cact = (SeT + S - 1) / S;           // clusters with work (uniform over the grid)
   const int Se = max(0, min(S, SeT - cl * S));  // active splits of this cluster
-  int per = (n + SeT - 1) / SeT;
-  per = (per + kAttnSub - 1) & ~(kAttnSub - 1);
   const int k0 = min(n, (cl * S + split) * per);
   const int k1 = min(n, k0 + per);
   const int nst = (k1 - k0 + kDecKeys - 1) / kDecKeys;

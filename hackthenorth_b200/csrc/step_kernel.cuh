@@ -130,9 +130,9 @@ struct StepAttnItem {
 __device__ __forceinline__ StepAttnItem step_attn_item(int b, int hkv, int max_splits, long long last) {
   StepAttnItem it;
   const int n = (int)last + 1;
-  it.Se = max(1, min(max_splits, (n + kAttnMinSplitKeys - 1) / kAttnMinSplitKeys));
-  int per = (n + it.Se - 1) / it.Se;
-  per = (per + kAttnSub - 1) & ~(kAttnSub - 1);
+  const int2 sl = attn_split_len(n, min(max_splits, (n + kAttnMinSplitKeys - 1) / kAttnMinSplitKeys));
+  const int per = sl.x;
+  it.Se = sl.y;  // every split below Se has keys
   if (b < hkv * it.Se && n > 0) {
     it.kvh = b / it.Se;
     it.split = b % it.Se;

@@ -88,9 +88,8 @@ __global__ void __launch_bounds__(kVaThreads, 1)
     last = -1;
   }
   const int n = (int)last + 1;
-  const int Se = max(1, min(S, (n + kAttnMinSplitKeys - 1) / kAttnMinSplitKeys));
-  int per = (n + Se - 1) / Se;
-  per = (per + kAttnSub - 1) & ~(kAttnSub - 1);
+  const int2 sl = attn_split_len(n, min(S, (n + kAttnMinSplitKeys - 1) / kAttnMinSplitKeys));
+  const int per = sl.x, Se = sl.y;  // every split below Se has keys
   const int k0 = min(n, split * per);
   const int k1 = min(n, k0 + per);
   const int nst = (k1 - k0 + kDecKeys - 1) / kDecKeys;

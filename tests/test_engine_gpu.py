@@ -217,3 +217,45 @@ def test_step_kernel_and_per_sublayer_launches_match_oracle(built_lib, cpu_threa
     for a, b in ((got["step-kernel"], ref), (got["per-sublayer"], ref), (got["step-kernel"], got["per-sublayer"])):
         d = (a - b).abs()
         assert d.max() <= LOGIT_ATOL and d.mean() <= 0.01, (float(d.max()), float(d.mean()))
+
+
+@pytest.mark.parametrize("hkv,context", [(4, 8200), (2, 15000), (1, 30000)])
+def test_long_context_few_kv_heads_matches_oracle(built_lib, cpu_threads, hkv, context):
+    """Few KV heads at long contexts run the decode attention as many clusters
+    per head (4 heads: 8 clusters of 4 CTAs; 2 heads: 7 of 8; 1 head: 7 of 16 on
+    a B200). At these lengths rounding the split length up used to leave the
+    last splits without keys; every split must get keys and the merged
+    attention must match the oracle: one decode step over a seeded N(0, 1)
+    cache prefix, logits within LOGIT_ATOL, appended K/V within bf16 rounding."""
+    from hackthenorth_b200.config import ModelConfig
+    from hackthenorth_b200.engine import Engine
+    from hackthenorth_b200.weights import random_state_dict
+    from oracle.qwen3_oracle import OracleQwen3
+
+    cfg = ModelConfig(f"kv{hkv}", hidden=1024, n_heads=4 * hkv, n_kv_heads=hkv, head_dim=128, ffn=2048,
+                      n_layers=1, vocab=4096, rope_theta=1e6)
+    state = random_state_dict(cfg, 8)
+    g = torch.Generator().manual_seed(13)
+    kp = torch.randn(1, hkv, context, 128, generator=g).to(BF16)
+    vp = torch.randn(1, hkv, context, 128, generator=g).to(BF16)
+    o = OracleQwen3(cfg, state, context + 4)
+    o.keys[:, :, :context] = kp
+    o.values[:, :, :context] = vp
+    ref, ref_tok = o.forward_rows([29], context)
+    ref = ref[0].float()
+    engine = Engine(None, "cuda:0", cfg=cfg, state=state)
+    st = engine.new_state(context, 4, keep_logits=True)
+    st.keys[:, :, :context] = kp.to(engine.device)
+    st.values[:, :, :context] = vp.to(engine.device)
+    st.token.fill_(29)
+    st.position.fill_(context)
+    st.step()
+    st.check()
+    got = st.logits.float().cpu()
+    d = (got - ref).abs()
+    assert d.max() <= LOGIT_ATOL and d.mean() <= 0.01, (float(d.max()), float(d.mean()))
+    if st.read_token()[0] != int(ref_tok[0]):
+        top2 = ref.topk(2).values
+        assert float(top2[0] - top2[1]) <= LOGIT_ATOL
+    torch.testing.assert_close(st.keys[0, :, context].float().cpu(), o.keys[0, :, context].float(), atol=0.0625,
+                               rtol=0.02)
