@@ -383,6 +383,8 @@ cudaError_t launch_attn_decode(const CUtensorMap& tk, const CUtensorMap& tv, Att
 
 // Verify-pass attention (attn_rows_kernel, R = G * Q <= 24 rows) as one
 // cluster per KV head: the cluster size (16 or 8) or 0 when it does not fit.
+int g_rows_active[3] = {0, 0, 0};  // clusters of 16, 8, 4 rows-kernel CTAs the GPU holds at once
+
 int rows_cluster_size(int hkv) {
   static int cached_hkv = -1, cached = 0;
   if (hkv == cached_hkv) return cached;
@@ -400,8 +402,8 @@ int rows_cluster_size(int hkv) {
       return 0;
     }
   }
-  const int sizes[2] = {16, 8};
-  for (int cs : sizes) {
+  for (int i = 0; i < 3; ++i) {
+    const int cs = kDecSizes[i];
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(hkv * cs);
     cfg.blockDim = dim3(kVaThreads);
@@ -414,13 +416,35 @@ int rows_cluster_size(int hkv) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, attn_rows_kernel<3>, &cfg) == cudaSuccess && n >= hkv) {
-      cached = cs;
-      break;
+    if (cudaOccupancyMaxActiveClusters(&n, attn_rows_kernel<3>, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      n = 0;
     }
-    cudaGetLastError();
+    g_rows_active[i] = n;
+    if (cached == 0 && cs >= 8 && n >= hkv) cached = cs;
   }
   return cached;
+}
+
+// Cluster size and clusters per KV head for the rows attention of a verify
+// pass: one cluster of rows_cluster_size(hkv) CTAs below kDecMultiClusterKeys
+// of capacity; above it the size and count that put the most CTAs to work at
+// once (the clusters merge through tickets and partial rows).
+void rows_attn_shape(AttnArgs& a, int cs) {
+  a.splits = cs;
+  a.clusters = 1;
+  if (a.tickets == nullptr || a.cap < kDecMultiClusterKeys) return;
+  const int cmax = std::min(kDecMaxClusters, a.part_splits * 32 / kVaMaxRows);
+  int best = a.Hkv * cs;
+  for (int i = 0; i < 3; ++i) {
+    const int s = kDecSizes[i];
+    const int c = std::min({cmax, g_rows_active[i] / a.Hkv, current_sm_count() / (a.Hkv * s)});
+    if (c >= 2 && a.Hkv * c * s > best) {
+      best = a.Hkv * c * s;
+      a.splits = s;
+      a.clusters = c;
+    }
+  }
 }
 
 // Cluster size for the rows attention kernel over `vheads` KV heads of several
@@ -448,16 +472,19 @@ int batch_attn_cluster(int vheads, int sm_count) {
 }
 
 cudaError_t launch_attn_rows(const CUtensorMap& tk, const CUtensorMap& tv, AttnArgs a, int cs, cudaStream_t st) {
-  a.splits = cs;
+  if (a.clusters <= 1) {  // one cluster of cs CTAs per KV head
+    a.splits = cs;
+    a.clusters = 1;
+  }
   const int rows = (a.Hq / a.Hkv) * a.Q;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.Hkv * cs);
+  cfg.gridDim = dim3(a.Hkv * a.clusters * a.splits);
   cfg.blockDim = dim3(kVaThreads);
   cfg.dynamicSmemBytes = va_smem_bytes();
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = cs;
+  attr[0].val.clusterDim.x = a.splits;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1079,6 +1106,11 @@ int run_verify(qb_ctx* c, const int64_t* ids, int n, const int64_t* pos, int64_t
     at.cap = c->cap;
     at.splits = c->splits;
     const int vcs = (g.n_heads / g.n_kv_heads) * n <= kVaMaxRows ? rows_cluster_size(g.n_kv_heads) : 0;
+    if (vcs > 0) {
+      at.part_splits = c->splits;
+      at.tickets = c->counters + 512;
+      rows_attn_shape(at, vcs);
+    }
     e = vcs > 0 ? launch_attn_rows(c->dmk[l], c->dmv[l], at, vcs, st)
                 : launch_attn(c->tmk[l], c->tmv[l], nullptr, nullptr, at, false, st);
     if (e != cudaSuccess) return cuda_fail(&c->msg, e, "verify attention");

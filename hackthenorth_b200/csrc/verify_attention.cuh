@@ -1,7 +1,9 @@
 // Multi-query decode attention for the verify pass: Q consecutive query
 // positions of one sequence (the current token and the draft tokens), GQA
-// group G, R = G * Q <= 24 query rows per KV head, as one thread-block cluster
-// of S CTAs per KV head.
+// group G, R = G * Q <= 24 query rows per KV head, as C thread-block clusters
+// of S CTAs per KV head (C > 1 from kDecMultiClusterKeys live keys when the
+// launch provides merge tickets; the clusters then merge through global
+// partial rows as in the decode kernel).
 //
 // Same arithmetic as the decode kernel (decode_attention.cuh) and the
 // reference's partial attention + LSE merge (dryft/engine/kernels/
@@ -61,9 +63,11 @@ __global__ void __launch_bounds__(kVaThreads, 1)
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const int S = a.splits;  // cluster size
-  const int kvh = blockIdx.x / S;
-  const int split = blockIdx.x % S;
+  const int S = a.splits;            // cluster size
+  const int C = max(1, a.clusters);  // clusters per KV head
+  const int kvh = blockIdx.x / (C * S);
+  const int cl = (blockIdx.x / S) % C;
+  const int split = blockIdx.x % S;  // == cluster rank
   const int G = a.Hq / a.Hkv;
   const int Qn = a.Q;
   const int R = G * Qn;  // <= ROWS
@@ -88,9 +92,19 @@ __global__ void __launch_bounds__(kVaThreads, 1)
     last = -1;
   }
   const int n = (int)last + 1;
-  const int2 sl = attn_split_len(n, min(S, (n + kAttnMinSplitKeys - 1) / kAttnMinSplitKeys));
-  const int per = sl.x, Se = sl.y;  // every split below Se has keys
-  const int k0 = min(n, split * per);
+  // Splits over the whole head as in the decode kernel: up to C clusters'
+  // worth from kDecMultiClusterKeys live keys; cluster cl takes splits
+  // [cl*S, cl*S+S) of SeT, every one of which has keys.
+  const int cmax = n >= kDecMultiClusterKeys ? C : min(C, max(1, kDecShortSplits / S));
+  const int2 sl = attn_split_len(n, min(cmax * S, (n + kAttnMinSplitKeys - 1) / kAttnMinSplitKeys));
+  const int per = sl.x, SeT = sl.y;
+  const int Cact = (SeT + S - 1) / S;           // clusters with work (uniform over the grid)
+  const int Se = max(0, min(S, SeT - cl * S));  // splits of this cluster
+  if (Se == 0) {  // a cluster without work leaves at once
+    cluster_wait();
+    return;
+  }
+  const int k0 = min(n, (cl * S + split) * per);
   const int k1 = min(n, k0 + per);
   const int nst = (k1 - k0 + kDecKeys - 1) / kDecKeys;
   const bool active = split < Se && nst > 0;
@@ -322,7 +336,7 @@ __global__ void __launch_bounds__(kVaThreads, 1)
 
   // ------------------------------------------------------------ cluster merge
   cluster_wait();
-  if (Se == 1) {  // uniform across the cluster
+  if (Se == 1 && Cact == 1) {  // uniform across the grid
     if (split == 0 && active && ok) {
 #pragma unroll
       for (int j = 0; j < (ROWS + 1) / 2; ++j) {
@@ -348,18 +362,55 @@ __global__ void __launch_bounds__(kVaThreads, 1)
     }
   }
   cluster_sync_all();
+  // Several clusters per head: each CTA publishes its dim slice of the
+  // cluster's result (normalised rows + log-sum-exp) to global partial rows;
+  // the CTA of the same slice index that draws the last ticket merges the
+  // clusters in cluster order. A row may see no key of a later cluster
+  // (causal limits): that cluster contributes 0 with weight 0.
+  float* po = a.part_o + (size_t)kvh * a.part_splits * kVaMaxRows * kAttnD;
+  float* pl = a.part_lse + (size_t)kvh * a.part_splits * kVaMaxRows;
   for (int idx = tid; idx < R * W; idx += kVaThreads) {
     const int r = idx / W, off = idx % W;
     float mx = -INFINITY;
     for (int sp = 0; sp < Se; ++sp) mx = fmaxf(mx, rlse[sp * R + r]);
     float den = 0.f, acc = 0.f;
-    for (int sp = 0; sp < Se; ++sp) {
-      const float w = exp2f(rlse[sp * R + r] - mx);
-      den += w;
-      acc = fmaf(rbuf[(sp * R + r) * W + off], w, acc);
+    if (mx != -INFINITY) {
+      for (int sp = 0; sp < Se; ++sp) {
+        const float w = exp2f(rlse[sp * R + r] - mx);
+        den += w;
+        acc = fmaf(rbuf[(sp * R + r) * W + off], w, acc);
+      }
     }
-    attn_store_out(a, kvh, r, split * W + off, acc / den);
+    const float cval = den > 0.f ? acc / den : 0.f;
+    if (Cact == 1) {
+      attn_store_out(a, kvh, r, split * W + off, cval);
+    } else {
+      po[((size_t)cl * R + r) * kAttnD + split * W + off] = cval;
+      if (off == 0) pl[cl * R + r] = den > 0.f ? mx + log2f(den) : -INFINITY;
+    }
   }
+  if (Cact == 1) return;
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned t = atomic_add_acq_rel_gpu(a.tickets + kvh * S + split, 1u);
+    flags[1] = (t == (unsigned)(Cact - 1)) ? 1 : 0;
+  }
+  __syncthreads();
+  if (flags[1] == 0) return;
+  for (int idx = tid; idx < R * W; idx += kVaThreads) {
+    const int r = idx / W, off = idx % W;
+    float mx = -INFINITY;
+    for (int c = 0; c < Cact; ++c) mx = fmaxf(mx, __ldcg(pl + c * R + r));
+    float den = 0.f, acc = 0.f;
+    for (int c = 0; c < Cact; ++c) {
+      const float l = __ldcg(pl + c * R + r);
+      const float w = l == -INFINITY ? 0.f : exp2f(l - mx);
+      den += w;
+      acc = fmaf(__ldcg(po + ((size_t)c * R + r) * kAttnD + split * W + off), w, acc);
+    }
+    attn_store_out(a, kvh, r, split * W + off, den > 0.f ? acc / den : 0.f);
+  }
+  if (tid == 0) a.tickets[kvh * S + split] = 0u;
 }
 
 }  // namespace qb

@@ -139,3 +139,45 @@ def test_verify_rejects_bad_arguments(built_lib):
                        _lib.stream_handle()) == 0
     with pytest.raises(ValueError, match="capacity"):
         st.check()
+
+
+@pytest.mark.parametrize("hkv,context", [(8, 9000), (2, 15000), (1, 30000)])
+def test_verify_long_context_matches_oracle(built_lib, cpu_threads, hkv, context):
+    """From a capacity of 8192 keys the verify attention runs several clusters
+    per KV head, merged through global partial rows (8 KV heads: 4 clusters of
+    4 CTAs on a B200; 2 heads: 7 of 8; 1 head: 7 of 16). Five rows over a seeded
+    N(0, 1) cache prefix: every row's logits within LOGIT_ATOL of the oracle
+    (mean below 0.01), predictions equal up to near ties, K/V rows appended."""
+    from hackthenorth_b200.config import ModelConfig
+    from hackthenorth_b200.engine import Engine
+    from hackthenorth_b200.weights import random_state_dict
+    from oracle.qwen3_oracle import OracleQwen3
+
+    cfg = ModelConfig(f"kv{hkv}", hidden=1024, n_heads=4 * hkv, n_kv_heads=hkv, head_dim=128, ffn=2048,
+                      n_layers=1, vocab=4096, rope_theta=1e6)
+    state = random_state_dict(cfg, 8)
+    g = torch.Generator().manual_seed(14)
+    kp = torch.randn(1, hkv, context, 128, generator=g).to(BF16)
+    vp = torch.randn(1, hkv, context, 128, generator=g).to(BF16)
+    current, drafts = 29, [3, 77, 1000, 5]
+    o = OracleQwen3(cfg, state, context + 16)
+    o.keys[:, :, :context] = kp
+    o.values[:, :, :context] = vp
+    ref, ref_tok = o.forward_rows([current, *drafts], context)
+    ref = ref.float()
+    engine = Engine(None, "cuda:0", cfg=cfg, state=state)
+    st = engine.new_state(context, 4, draft_tokens=8)
+    assert st.capacity >= 8192
+    st.keys[:, :, :context] = kp.to(engine.device)
+    st.values[:, :, :context] = vp.to(engine.device)
+    st.position.fill_(context)
+    preds, logits = _verify_rows(engine, st, current, drafts)
+    d = (logits - ref).abs()
+    assert d.max() <= LOGIT_ATOL and d.mean() <= 0.01, (float(d.max()), float(d.mean()))
+    for i in range(len(drafts) + 1):
+        if preds[i] != int(ref_tok[i]):
+            top2 = ref[i].topk(2).values
+            assert float(top2[0] - top2[1]) <= LOGIT_ATOL, f"row {i}"
+    n = len(drafts) + 1
+    torch.testing.assert_close(st.keys[0, :, context:context + n].float().cpu(),
+                               o.keys[0, :, context:context + n].float(), atol=0.0625, rtol=0.02)
