@@ -59,6 +59,9 @@ SIGNATURES = {
     "qb_replay_verify": (c_int, [c_void_p, c_void_p]),
     "qb_norm_projection": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_int, c_void_p]),
     "qb_projection_residual": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "qb_projection_residual_peer": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int,
+                                            ctypes.POINTER(c_void_p), c_int, c_int, c_int, c_int, c_void_p,
+                                            c_void_p, c_void_p]),
     "qb_op_scratch_bytes": (c_size_t, []),
     "qb_norm_greedy_head": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_float, c_void_p, c_void_p,
                                     c_void_p, c_size_t, c_void_p]),

@@ -80,6 +80,37 @@ int current_sm_count() {
   return sm_count_of(dev);
 }
 
+// Function attributes (cudaFuncSetAttribute) and occupancy results belong to
+// one device, so everything this file caches about them is kept per device and
+// looked up with the caller's device current. A device index beyond the table
+// gets a fresh entry on every call (attributes set again, occupancy queried
+// again): correct, only slower.
+constexpr int kMaxDevices = 64;
+struct DeviceCache {
+  bool gemv_attr[5] = {};
+  bool pg_attr[3] = {};
+  bool attn_attr[2][2] = {};  // [MT - 1][PRO]
+  bool rows_attr[5] = {};
+  bool fp_attr = false;
+  // attn_decode_kernel: cluster size for (hkv, rows) and clusters of 16/8/4 CTAs held at once
+  int dec_hkv = -1, dec_rows = -1, dec_cs = 0;
+  int dec_active[3] = {0, 0, 0};
+  // attn_rows_kernel: cluster size for hkv and clusters of 16/8/4 CTAs held at once
+  int rows_hkv = -1, rows_cs = 0;
+  int rows_active[3] = {0, 0, 0};
+  int batch_attrs = -1;
+};
+DeviceCache g_dev_cache[kMaxDevices];
+std::mutex g_dev_cache_mu;  // guards the occupancy entries while they are computed
+
+DeviceCache& dev_cache() {
+  int d = 0;
+  if (cudaGetDevice(&d) == cudaSuccess && d >= 0 && d < kMaxDevices) return g_dev_cache[d];
+  static thread_local DeviceCache overflow;
+  overflow = DeviceCache();
+  return overflow;
+}
+
 bool pdl_enabled() {
   static int v = -1;
   if (v < 0) {
@@ -153,7 +184,7 @@ bool plan_gemv(int epi, int K, int rows, int sm_count, GemvPlan* p) {
 
 template <int EPI>
 cudaError_t launch_gemv(GemvArgs a, int sm_count, cudaStream_t st) {
-  static bool attr_done = false;
+  bool& attr_done = dev_cache().gemv_attr[EPI];
   if (!attr_done) {
     cudaError_t e = cudaFuncSetAttribute(gemv_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return e;
@@ -257,7 +288,7 @@ cudaError_t launch_prefill_gemm(int epi, const bf16* x, const bf16* w, bf16* out
   a.residual = residual;
   a.err = err;
   const size_t smem = pg_smem_bytes();
-  static bool attr[3] = {false, false, false};
+  bool* attr = dev_cache().pg_attr;
   void (*k)(const CUtensorMap, const CUtensorMap, const PgArgs) =
       epi == PG_STORE ? prefill_gemm_kernel<PG_STORE> : epi == PG_RESIDUAL ? prefill_gemm_kernel<PG_RESIDUAL>
                                                                            : prefill_gemm_kernel<PG_SWIGLU>;
@@ -280,7 +311,7 @@ int attn_splits_for(int hkv, int sm_count) {
 
 template <int MT, bool PRO>
 cudaError_t launch_attn_t(const CUtensorMap& tk, const CUtensorMap& tv, const AttnArgs& a, cudaStream_t st) {
-  static bool attr_done = false;
+  bool& attr_done = dev_cache().attn_attr[MT - 1][PRO ? 1 : 0];
   const size_t smem = attn_smem_bytes(MT);
   if (!attr_done) {
     cudaError_t e = cudaFuncSetAttribute(attn_kernel<MT, PRO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -295,17 +326,17 @@ cudaError_t launch_attn_t(const CUtensorMap& tk, const CUtensorMap& tv, const At
 // query rows (16 when 16-CTA clusters of this kernel fit `hkv` at once, else
 // 8), or 0 when the kernel does not apply (then attn_kernel is used).
 // QB_ATTN_CLUSTER=0 disables it. Also records how many clusters of 16, 8 and 4
-// CTAs the GPU holds at once (g_dec_active), for launch_attn_decode's
+// CTAs the GPU holds at once (DeviceCache::dec_active), for launch_attn_decode's
 // long-context choice.
 constexpr int kDecSizes[3] = {16, 8, 4};
-int g_dec_active[3] = {0, 0, 0};
 
 int decode_cluster_size(int hkv, int rows) {
-  static int cached_hkv = -1, cached_rows = -1, cached = 0;
-  if (hkv == cached_hkv && rows == cached_rows) return cached;
-  cached_hkv = hkv;
-  cached_rows = rows;
-  cached = 0;
+  DeviceCache& dc = dev_cache();
+  std::lock_guard<std::mutex> lock(g_dev_cache_mu);
+  if (hkv == dc.dec_hkv && rows == dc.dec_rows) return dc.dec_cs;
+  dc.dec_hkv = hkv;
+  dc.dec_rows = rows;
+  dc.dec_cs = 0;
   const char* e = std::getenv("QB_ATTN_CLUSTER");
   if (e && e[0] == '0') return 0;
   if (rows > kDecRows) return 0;
@@ -332,10 +363,10 @@ int decode_cluster_size(int hkv, int rows) {
       cudaGetLastError();
       n = 0;
     }
-    g_dec_active[i] = n;
-    if (cached == 0 && cs >= 8 && n >= hkv) cached = cs;
+    dc.dec_active[i] = n;
+    if (dc.dec_cs == 0 && cs >= 8 && n >= hkv) dc.dec_cs = cs;
   }
-  return cached;
+  return dc.dec_cs;
 }
 
 cudaError_t launch_attn_decode(const CUtensorMap& tk, const CUtensorMap& tv, AttnArgs a, int cs, cudaStream_t st) {
@@ -348,7 +379,7 @@ cudaError_t launch_attn_decode(const CUtensorMap& tk, const CUtensorMap& tv, Att
     int best = a.Hkv * cs;
     for (int i = 0; i < 3; ++i) {
       const int s = kDecSizes[i];
-      const int c = std::min({kDecMaxClusters, a.part_splits, g_dec_active[i] / a.Hkv,
+      const int c = std::min({kDecMaxClusters, a.part_splits, dev_cache().dec_active[i] / a.Hkv,
                               current_sm_count() / (a.Hkv * s)});
       if (c >= 1 && a.Hkv * c * s > best) {
         best = a.Hkv * c * s;
@@ -361,7 +392,8 @@ cudaError_t launch_attn_decode(const CUtensorMap& tk, const CUtensorMap& tv, Att
   if (!reported && std::getenv("QB_VERBOSE")) {
     reported = true;
     std::fprintf(stderr, "qb: decode attention: %d KV heads x %d clusters x %d CTAs (GPU holds %d/%d/%d clusters of 16/8/4)\n",
-                 a.Hkv, a.clusters, a.splits, g_dec_active[0], g_dec_active[1], g_dec_active[2]);
+                 a.Hkv, a.clusters, a.splits, dev_cache().dec_active[0], dev_cache().dec_active[1],
+                 dev_cache().dec_active[2]);
   }
   cs = a.splits;
   cudaLaunchConfig_t cfg = {};
@@ -383,13 +415,14 @@ cudaError_t launch_attn_decode(const CUtensorMap& tk, const CUtensorMap& tv, Att
 
 // Verify-pass attention (attn_rows_kernel, R = G * Q <= 24 rows) as one
 // cluster per KV head: the cluster size (16 or 8) or 0 when it does not fit.
-int g_rows_active[3] = {0, 0, 0};  // clusters of 16, 8, 4 rows-kernel CTAs the GPU holds at once
-
+// Also records how many clusters of 16, 8 and 4 CTAs the GPU holds at once
+// (DeviceCache::rows_active), for rows_attn_shape.
 int rows_cluster_size(int hkv) {
-  static int cached_hkv = -1, cached = 0;
-  if (hkv == cached_hkv) return cached;
-  cached_hkv = hkv;
-  cached = 0;
+  DeviceCache& dc = dev_cache();
+  std::lock_guard<std::mutex> lock(g_dev_cache_mu);
+  if (hkv == dc.rows_hkv) return dc.rows_cs;
+  dc.rows_hkv = hkv;
+  dc.rows_cs = 0;
   const char* e = std::getenv("QB_ATTN_CLUSTER");
   if (e && e[0] == '0') return 0;
   const size_t smem = va_smem_bytes();
@@ -420,10 +453,10 @@ int rows_cluster_size(int hkv) {
       cudaGetLastError();
       n = 0;
     }
-    g_rows_active[i] = n;
-    if (cached == 0 && cs >= 8 && n >= hkv) cached = cs;
+    dc.rows_active[i] = n;
+    if (dc.rows_cs == 0 && cs >= 8 && n >= hkv) dc.rows_cs = cs;
   }
-  return cached;
+  return dc.rows_cs;
 }
 
 // Cluster size and clusters per KV head for the rows attention of a verify
@@ -434,11 +467,14 @@ void rows_attn_shape(AttnArgs& a, int cs) {
   a.splits = cs;
   a.clusters = 1;
   if (a.tickets == nullptr || a.cap < kDecMultiClusterKeys) return;
-  const int cmax = std::min(kDecMaxClusters, a.part_splits * 32 / kVaMaxRows);
+  // The kernel keeps part_splits * kVaMaxRows partial rows per KV head and
+  // cluster cl writes rows cl * R + r (R <= kVaMaxRows), so at most
+  // part_splits clusters stay inside their head's rows.
+  const int cmax = std::min(kDecMaxClusters, a.part_splits);
   int best = a.Hkv * cs;
   for (int i = 0; i < 3; ++i) {
     const int s = kDecSizes[i];
-    const int c = std::min({cmax, g_rows_active[i] / a.Hkv, current_sm_count() / (a.Hkv * s)});
+    const int c = std::min({cmax, dev_cache().rows_active[i] / a.Hkv, current_sm_count() / (a.Hkv * s)});
     if (c >= 2 && a.Hkv * c * s > best) {
       best = a.Hkv * c * s;
       a.splits = s;
@@ -453,7 +489,7 @@ void rows_attn_shape(AttnArgs& a, int cs) {
 // wait on each other, so more than fit at once is still correct. 0 when the
 // kernel's attributes cannot be set.
 int batch_attn_cluster(int vheads, int sm_count) {
-  static int attrs = -1;
+  int& attrs = dev_cache().batch_attrs;
   if (attrs < 0) {
     attrs = 1;
     void (*kernels[3])(const CUtensorMap, const CUtensorMap, const AttnArgs) = {
@@ -1003,7 +1039,7 @@ cudaError_t launch_step(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int6
 
 template <int EPI>
 cudaError_t launch_rows(const RowsArgs& a, int sm_count, cudaStream_t st) {
-  static bool attr_done = false;
+  bool& attr_done = dev_cache().rows_attr[EPI];
   const size_t smem = rows_smem_bytes();
   if (!attr_done) {
     cudaError_t e = cudaFuncSetAttribute(gemv_rows_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -1367,7 +1403,7 @@ int run_prefill_batched(qb_ctx* c, const int64_t* ids, int n, uint8_t* scratch, 
     fa.Hkv = g.n_kv_heads;
     fa.cap = c->cap;
     fa.err = c->err;
-    static bool fp_attr = false;
+    bool& fp_attr = dev_cache().fp_attr;
     if (!fp_attr) {
       if ((e = cudaFuncSetAttribute(flash_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                     (int)fp_smem_bytes())) != cudaSuccess)
@@ -1934,6 +1970,38 @@ int qb_projection_residual(const void* x, const void* w, const void* residual, v
   a.residual = static_cast<const bf16*>(residual);
   cudaError_t e = launch_gemv<EPI_RESIDUAL>(a, current_sm_count(), static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(nullptr, e, "projection_residual launch");
+  return QB_OK;
+}
+
+int qb_projection_residual_peer(const void* x, const void* w, const void* residual, void* out, int K, int N,
+                                void* const* recv_words, int rank, int size, int sublayer, int parity,
+                                const uint64_t* epoch, void* scratch, void* stream) {
+  if (!ptr_ok(x) || !ptr_ok(w) || !ptr_ok(out) || !residual || !ptr_ok(scratch) || !epoch)
+    return set_err(nullptr, QB_ERR_ARG, "x, w, residual, out, scratch, epoch must be device pointers (16-byte aligned)");
+  if (K <= 0 || K % 128 != 0) return set_err(nullptr, QB_ERR_UNSUPPORTED, "K must be a positive multiple of 128");
+  if (N <= 0) return set_err(nullptr, QB_ERR_ARG, "N must be positive");
+  if (size < 1 || size > kMaxTp) return set_err(nullptr, QB_ERR_UNSUPPORTED, "size must be 1..8 ranks");
+  if (rank < 0 || rank >= size) return set_err(nullptr, QB_ERR_ARG, "rank must lie in 0..size-1");
+  if (sublayer < 0 || sublayer > 254 || (parity != 0 && parity != 1))
+    return set_err(nullptr, QB_ERR_ARG, "sublayer must be 0..254 and parity 0 or 1");
+  if (size > 1 && !recv_words) return set_err(nullptr, QB_ERR_ARG, "recv_words is NULL");
+  GemvArgs a = gemv_args(w, K, N, x, out, reinterpret_cast<int*>(static_cast<uint8_t*>(scratch) + kScrErr));
+  a.residual = static_cast<const bf16*>(residual);
+  if (size > 1) {
+    for (int p = 0; p < size; ++p) {
+      if (!recv_words[p] || (reinterpret_cast<uintptr_t>(recv_words[p]) & 7) != 0)
+        return set_err(nullptr, QB_ERR_ARG, "every receive buffer must be an 8-byte aligned device pointer");
+      a.tp.recv[p] = static_cast<unsigned long long*>(recv_words[p]);
+    }
+    a.tp.epoch = reinterpret_cast<const unsigned long long*>(epoch);
+    a.tp.rank = rank;
+    a.tp.size = size;
+    a.tp_sub = sublayer;
+    a.tp_parity = parity;
+    a.hidden = N;
+  }
+  cudaError_t e = launch_gemv<EPI_RESIDUAL>(a, current_sm_count(), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(nullptr, e, "projection_residual_peer launch");
   return QB_OK;
 }
 

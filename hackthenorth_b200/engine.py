@@ -1,5 +1,6 @@
-"""Drop-in ``Engine`` for the dryft Qwen3 decode path (batch one, plus batched
-decode of up to 8 equal-length prompts), on sm_100a kernels.
+"""Drop-in ``Engine`` for the dryft Qwen3 decode path on sm_100a kernels: batch
+one (speculative with prompt lookup by default, as the reference), and batched
+decode of any number of equal-length prompts (8 per context per step).
 
 Public API (``dryft/QWEN_ENGINE_CONTRACT.md:25-36``, ``dryft/engine/engine.py:175-249``):
 
@@ -110,6 +111,7 @@ class DecodeState:
             raise ValueError("batched decode runs on one GPU")
         self.engine = engine
         self.batch = batch
+        self.draft_tokens = draft_tokens
         self.shape = (batch, prompt_length, output_length)
         self.capacity = capacity or (prompt_length + max(output_length, 1) - 1 + draft_tokens)
         hkv = cfg.n_kv_heads // engine.tp_size
@@ -321,8 +323,10 @@ class Engine:
         w = self.weights
         _lib.check(L.qb_bind_weights(ctx, table, cfg.n_layers, w.embed.data_ptr(), w.final_norm.data_ptr(),
                                      w.lm_head.data_ptr()), ctx)
+        self._weight_table = table
         self.state: Optional[DecodeState] = None
         self._bound_state = None
+        self._lanes: List["_Lane"] = []
 
     @classmethod
     def from_random(cls, cfg: ModelConfig, seed: int = 0, device: str = "cuda:0", init_device: str = "cpu",
@@ -346,35 +350,44 @@ class Engine:
         self.state = DecodeState(self, prompt_length, output_length, **kw)
         return self.state
 
-    def generate(self, input_ids: List[List[int]], max_new_tokens: int, draft_tokens: int = 0,
+    def generate(self, input_ids: List[List[int]], max_new_tokens: int, draft_tokens: Optional[int] = None,
                  drafter=None):
         """Greedy continuation; yields one token per sequence exactly
-        ``max_new_tokens`` times (``dryft/engine/engine.py:202-249``). One
-        sequence runs the batch-one decode path; 2..8 sequences of equal prompt
-        length run as one batched decode (every weight streamed once per step
-        for all of them).
+        ``max_new_tokens`` times (``dryft/engine/engine.py:202-249``).
 
-        With ``draft_tokens`` k > 0 the loop speculates as the reference does:
-        a drafter (default: ``PromptLookup`` over the prompt and the emitted
-        tokens, the reference's draft source) proposes up to k tokens, one
-        verify pass checks them, and the accepted prefix plus one target token
-        is emitted; without a proposal it takes a plain decode step. The
-        emitted sequence is the plain greedy one (verification only accepts
-        tokens the target itself predicts). ``drafter`` may be any object with
-        ``propose() -> list | None`` and ``append(token)``."""
+        As in the reference, one sequence speculates by default: a
+        ``PromptLookup`` over the prompt and the emitted tokens proposes
+        ``draft_width(max_new_tokens)`` tokens (up to 7), one verify pass
+        checks them, and the accepted prefix plus one target token is emitted;
+        without a proposal it takes a plain decode step. The emitted sequence
+        is the plain greedy one (verification only accepts tokens the target
+        itself predicts). ``draft_tokens`` overrides the width (0: plain decode
+        with replays running ahead of the consumer); ``drafter`` may be any
+        object with ``propose() -> list | None`` and ``append(token)``.
+
+        Several sequences of equal prompt length decode together (every weight
+        streamed once per step for up to 8 of them); more than 8 run as chunks
+        of 8, each on its own context over the same weights."""
         if max_new_tokens <= 0:
             return
-        if draft_tokens > 0:
-            yield from self._generate_speculative(input_ids, max_new_tokens, draft_tokens, drafter)
-            return
         B = len(input_ids)
-        if not 1 <= B <= DecodeState.MAX_BATCH:
-            raise ValueError(f"this engine decodes 1..{DecodeState.MAX_BATCH} sequences")
+        if B < 1:
+            raise ValueError("generate needs at least one sequence")
         prompts = [list(p) for p in input_ids]
         if any(len(p) != len(prompts[0]) for p in prompts):
             raise ValueError("the sequences of a batch must have equal prompt lengths")
         if not prompts[0]:
             raise ValueError("the prompt must hold at least one token")
+        if draft_tokens is None:
+            from .speculate import draft_width
+
+            draft_tokens = draft_width(max_new_tokens) if B == 1 else 0
+        if draft_tokens > 0:
+            yield from self._generate_speculative(prompts, max_new_tokens, draft_tokens, drafter)
+            return
+        if B > DecodeState.MAX_BATCH:
+            yield from self._generate_chunked(prompts, max_new_tokens)
+            return
         P = len(prompts[0])
         with torch.inference_mode():
             shape = (B, P, max_new_tokens)
@@ -386,19 +399,60 @@ class Engine:
             first = state.read_token()
             yield from stream_decode(state, first, max_new_tokens, depth=self.STREAM_DEPTH)
 
+    def _lane(self, i: int) -> "_Lane":
+        """Context i (>= 1) for chunk i of a large batch: its own qb context and
+        decode state, borrowing this engine's weights."""
+        while len(self._lanes) < i:
+            self._lanes.append(_Lane(self))
+        return self._lanes[i - 1]
+
+    def _generate_chunked(self, prompts: List[List[int]], max_new_tokens: int):
+        """More than 8 sequences: chunks of 8 (the last may be smaller), chunk 0
+        on this engine and chunk i on lane i; every step replays each chunk's
+        graph, then yields all tokens in sequence order."""
+        if self.tp_size > 1:
+            raise ValueError("batched decode runs on one GPU")
+        M = DecodeState.MAX_BATCH
+        chunks = [prompts[i:i + M] for i in range(0, len(prompts), M)]
+        P = len(prompts[0])
+        with torch.inference_mode():
+            states = []
+            for i, chunk in enumerate(chunks):
+                owner = self if i == 0 else self._lane(i)
+                shape = (len(chunk), P, max_new_tokens)
+                st = owner.state
+                if st is None or st.shape != shape or owner._bound_state is not st:
+                    st = owner.new_state(P, max_new_tokens, batch=len(chunk))
+                ids = torch.tensor(chunk if len(chunk) > 1 else chunk[0], dtype=torch.int64).pin_memory()
+                st.prefill(ids.to(self.device, non_blocking=True))
+                states.append(st)
+            tokens = [t for st in states for t in st.read_token()]
+            for step in range(max_new_tokens):
+                if step + 1 < max_new_tokens:
+                    for st in states:
+                        st.step()
+                yield tokens
+                if step + 1 < max_new_tokens:
+                    tokens = [t for st in states for t in st.read_token()]
+
     def _generate_speculative(self, input_ids, max_new_tokens: int, k: int, drafter):
         from .speculate import PromptLookup
 
         if len(input_ids) != 1:
-            raise ValueError("this engine implements the batch-one decode path")
+            raise ValueError("speculative decoding takes one sequence")
         prompt = list(input_ids[0])
         if not prompt:
             raise ValueError("the prompt must hold at least one token")
         if not 1 <= k <= 7:
             raise ValueError("draft_tokens must lie in 1..7")
         with torch.inference_mode():
-            # capacity holds the draft scratch slots (dryft/engine/decode.py:102-118)
-            state = self.new_state(len(prompt), max_new_tokens, draft_tokens=k)
+            # capacity holds the draft scratch slots (dryft/engine/decode.py:102-118);
+            # the state is shape-keyed like the plain path's (engine.py:212-215)
+            shape = (1, len(prompt), max_new_tokens)
+            state = self.state
+            if (state is None or state.shape != shape or self._bound_state is not state
+                    or getattr(state, "draft_tokens", 0) != k):
+                state = self.new_state(len(prompt), max_new_tokens, draft_tokens=k)
             ids = torch.tensor(prompt, dtype=torch.int64).pin_memory()
             state.prefill(ids.to(self.device, non_blocking=True))
             tokens = state.read_token()
@@ -421,3 +475,39 @@ class Engine:
                     lookup.append(tokens[0])
                     emitted += 1
                     yield tokens
+
+
+class _Lane:
+    """A second qb context over an engine's weights (no copy), with its own
+    decode state: one chunk of a batch larger than 8 sequences. Offers the
+    attributes ``DecodeState`` uses from an engine."""
+
+    def __init__(self, engine: Engine):
+        self.cfg, self.device, self.tp_size, self.tp_rank = engine.cfg, engine.device, 1, 0
+        self.weights = engine.weights
+        L = _lib.load()
+        cfg = self.cfg
+        qc = _lib.QbConfig(cfg.hidden, cfg.n_heads, cfg.n_kv_heads, cfg.head_dim, cfg.ffn, cfg.n_layers,
+                           cfg.vocab, cfg.rms_eps)
+        ctx = _lib.c_void_p()
+        _lib.check(L.qb_create(_lib.ctypes.byref(qc), self.device.index or 0, 0, 1, _lib.ctypes.byref(ctx)))
+        self.ctx = ctx
+        w = engine.weights
+        _lib.check(L.qb_bind_weights(ctx, engine._weight_table, cfg.n_layers, w.embed.data_ptr(),
+                                     w.final_norm.data_ptr(), w.lm_head.data_ptr()), ctx)
+        self.state: Optional[DecodeState] = None
+        self._bound_state = None
+
+    def new_state(self, prompt_length: int, output_length: int, **kw) -> DecodeState:
+        self.state = None
+        self.state = DecodeState(self, prompt_length, output_length, **kw)
+        return self.state
+
+    def __del__(self):
+        ctx = getattr(self, "ctx", None)
+        if ctx is not None and ctx.value:
+            try:
+                _lib.load().qb_destroy(ctx)
+            except Exception:
+                pass
+            self.ctx = None

@@ -76,6 +76,36 @@ def output_projection_residual(x, weight, residual):
     return out
 
 
+def projection_residual_peer(x, weight, residual, recv_words, rank, epoch, sublayer=0, parity=0):
+    """One rank's share of a tensor-parallel o-proj / down projection with the
+    cross-rank reduction in its epilogue: bf16(bf16(sum_r W_r.x_r) + residual),
+    partials added in rank order (``dryft/engine/kernels/projection.py:70-83``
+    with the sum spread over ranks). ``recv_words``: one uint64-viewable CUDA
+    tensor (or raw device address) per rank, each ``[2, size, N]`` words;
+    ``epoch``: CUDA int64 [1] (token base). Device-side wait timeouts surface
+    through ``check_device_errors``."""
+    _bf16_cuda(x, weight, residual)
+    n, k = weight.shape
+    _require(x.numel() == k and residual.numel() == n, "projection requires one activation and residual row")
+    size = len(recv_words)
+    _require(1 <= size <= 8 and 0 <= rank < size, "1..8 ranks, rank in range")
+    _require(epoch.is_cuda and epoch.dtype == torch.int64 and epoch.numel() >= 1, "epoch must be CUDA int64")
+    ptrs = []
+    for t in recv_words:
+        if isinstance(t, int):
+            ptrs.append(t)
+        else:
+            _require(t.is_cuda and t.numel() * t.element_size() >= 2 * size * n * 8, "receive buffer too small")
+            ptrs.append(t.data_ptr())
+    arr = (_lib.c_void_p * size)(*ptrs)
+    out = torch.empty_like(residual)
+    scratch = _op_scratch(x.device)
+    _lib.check(_lib.load().qb_projection_residual_peer(x.data_ptr(), weight.data_ptr(), residual.data_ptr(),
+                                                       out.data_ptr(), k, n, arr, rank, size, sublayer, parity,
+                                                       epoch.data_ptr(), scratch.data_ptr(), _lib.stream_handle()))
+    return out
+
+
 def down_residual(x, weight, residual):
     """Down projection + residual with one rounding before the add:
     ``dryft/engine/kernels/down.py:288-296``."""

@@ -70,7 +70,8 @@ def verified_tokens(proposal: Sequence[int], predictions: Sequence[int]) -> List
     """predictions[i] is the target's greedy token after current + proposal[:i].
     Accept the matching prefix, then emit the target's token after it."""
     if len(predictions) != len(proposal) + 1:
-        raise ValueError("verification needs one prediction per draft token plus a bonus")
+        raise ValueError(f"{len(predictions)} predictions for {len(proposal)} draft tokens: "
+                         "each draft token and the bonus position need one")
     accepted = 0
     for d, t in zip(proposal, predictions):
         if d != t:

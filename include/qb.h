@@ -210,6 +210,28 @@ int qb_norm_projection(const void* x, const void* gain, const void* w, void* out
 int qb_projection_residual(const void* x, const void* w, const void* residual, void* out,
                            int K, int N, void* stream);
 
+/* One rank's share of a tensor-parallel output or down projection with the
+ * cross-rank reduction fused into the epilogue: the op-level form of the
+ * o-proj / down sublayer under tensor parallelism. The reference has one GPU
+ * only; this keeps the single rounding of output_projection_residual
+ * (dryft/engine/kernels/projection.py:70-83): out = bf16(bf16(sum over ranks
+ * of W_r . x_r) + residual), the partials added in rank order.
+ * x [K] (this rank's input columns), W [N, K] (this rank's column shard),
+ * residual/out [N]. recv_words: host array of `size` device pointers, entry p
+ * = rank p's receive words [2][size][N] (uint64; peers' buffers reachable by
+ * this GPU, e.g. IPC-mapped). Every rank's grid writes {token, fp32 partial}
+ * words of its rows into recv_words[p][parity][rank][row] of every rank p,
+ * then waits (bounded, 2 s) until its own buffer holds the words of every
+ * rank for the same token, token = (*epoch + 1) * 256 + sublayer + 1 (epoch:
+ * device uint64 the caller advances between uses of the same sublayer id).
+ * All ranks must use the same GPU model (same row partition). A wait that
+ * gives up records a timeout in the scratch error word (qb_op_check returns
+ * QB_ERR_TIMEOUT) and the kernel returns; the output of that call is not
+ * defined. size 1 is qb_projection_residual. scratch: qb_op_scratch_bytes(). */
+int qb_projection_residual_peer(const void* x, const void* w, const void* residual, void* out, int K, int N,
+                                void* const* recv_words, int rank, int size, int sublayer, int parity,
+                                const uint64_t* epoch, void* scratch, void* stream);
+
 /* Scratch bytes the op-level head and attention calls need (a multiple of
  * 256). The scratch must be zero-filled before its first use; the kernels
  * leave their counters at zero again. */

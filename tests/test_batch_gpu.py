@@ -66,11 +66,12 @@ def test_batched_step_distinct_positions_matches_oracle(built_lib, cpu_threads, 
                                    rtol=0.02)
 
 
-@pytest.mark.parametrize("B", [2, 5, 8])
+@pytest.mark.parametrize("B", [2, 5, 8, 12, 17])
 def test_batched_generate_matches_oracle_greedy(built_lib, cpu_threads, B):
     """Engine.generate over B prompts of 16 tokens (teacher-forced batched
-    prefill, then the captured batched step): every sequence's stream equals
-    the oracle's greedy continuation of that prompt up to the first step where
+    prefill, then the captured batched step; above 8 sequences, chunks of 8
+    on contexts sharing the weights): every sequence's stream equals the
+    oracle's greedy continuation of that prompt up to the first step where
     the oracle's top-2 logits lie within LOGIT_ATOL."""
     from hackthenorth_b200.config import QWEN3_SMALL
     from hackthenorth_b200.engine import Engine

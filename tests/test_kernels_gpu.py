@@ -157,6 +157,47 @@ def test_grouped_attention_matches_oracle_and_sdpa(hq, hkv, cap, queries, first)
         assert torch.equal(again, out)
 
 
+def _sdpa_fp32_cuda(q, keys, values, positions):
+    """fp32 attention in plain PyTorch on the GPU, per KV head: query row
+    (i, head) sees keys 0..positions[i]; the same arithmetic as the reference's
+    SDPA check (dryft/tests/test_fused_kernels.py:390-401) at sizes where the
+    CPU restatement takes too long. q [Q, Hq, D]; keys/values [Hkv, cap, D]."""
+    Qn, hq, d = q.shape
+    hkv = keys.shape[0]
+    G = hq // hkv
+    n = int(positions[-1]) + 1
+    out = torch.empty(Qn, hq, d, dtype=torch.float32, device=q.device)
+    cols = torch.arange(n, device=q.device)
+    mask = cols[None, :] <= positions[:, None]  # [Q, n]
+    for h in range(hkv):
+        qh = q[:, h * G:(h + 1) * G].float()                       # [Q, G, D]
+        s = torch.einsum("qgd,kd->qgk", qh, keys[h, :n].float()) / d ** 0.5
+        s = s.masked_fill(~mask[:, None, :], float("-inf"))
+        out[:, h * G:(h + 1) * G] = torch.einsum("qgk,kd->qgd", torch.softmax(s, -1), values[h, :n].float())
+    return out
+
+
+@pytest.mark.parametrize("cap,queries", [(131072, 1), (131072, 5), (32768, 5)])
+def test_grouped_attention_long_contexts_match_fp32(cap, queries):
+    """The op sweep's long caches (GQA 32/8, D 128, N(0, 1) bf16 Q/K/V, query
+    rows at the last positions): within 1e-2 relative of fp32 attention, and
+    slots past the last position (NaN here) never read."""
+    from hackthenorth_b200 import ops
+
+    g = torch.Generator(device=DEV).manual_seed(2)
+    q = torch.randn(queries, 32, 128, generator=g, device=DEV).to(BF16)
+    k = torch.randn(8, cap + 64, 128, generator=g, device=DEV).to(BF16)
+    v = torch.randn(8, cap + 64, 128, generator=g, device=DEV).to(BF16)
+    pos = torch.arange(cap - queries, cap, dtype=torch.int64, device=DEV)
+    k[:, cap:] = float("nan")
+    v[:, cap:] = float("nan")
+    out = ops.grouped_attention(q, k, v, pos).float()
+    ref = _sdpa_fp32_cuda(q, k, v, pos)
+    assert torch.isfinite(out).all()
+    rel = ((out - ref).abs().max() / ref.abs().max()).item()
+    assert rel <= 1e-2, rel
+
+
 def test_attention_matches_golden_sdpa():
     from hackthenorth_b200 import ops
     from tests.golden.make_golden import attention_inputs

@@ -111,9 +111,13 @@ def test_speculative_generate_equals_plain_greedy(built_lib):
         assert engine.state._verify_n == k + 1
     # prompt lookup on a repetitive prompt proposes continuations
     rep = (prompt[:6] * 5)[:30]
-    plain = [s[0] for s in engine.generate([rep], 24)]
+    plain = [s[0] for s in engine.generate([rep], 24, draft_tokens=0)]
     spec = [s[0] for s in engine.generate([rep], 24, draft_tokens=4, drafter=PromptLookup(rep, draft_length=4))]
     assert spec == plain
+    # the default, as the reference's generate (dryft/engine/engine.py:214-249):
+    # prompt lookup with draft_width(24) = 7 draft tokens, verified 8 rows at a time
+    default = [s[0] for s in engine.generate([rep], 24)]
+    assert default == plain and engine.state._verify_n == 8
     for n in (1, 2, 3):
         assert len(list(engine.generate([rep], n, draft_tokens=4))) == n
 
@@ -141,13 +145,20 @@ def test_verify_rejects_bad_arguments(built_lib):
         st.check()
 
 
-@pytest.mark.parametrize("hkv,context", [(8, 9000), (2, 15000), (1, 30000)])
+@pytest.mark.parametrize("hkv,context", [(8, 9000), (2, 15000), (1, 30000), (2, 8188), (1, 8188)])
 def test_verify_long_context_matches_oracle(built_lib, cpu_threads, hkv, context):
     """From a capacity of 8192 keys the verify attention runs several clusters
     per KV head, merged through global partial rows (8 KV heads: 4 clusters of
     4 CTAs on a B200; 2 heads: 7 of 8; 1 head: 7 of 16). Five rows over a seeded
     N(0, 1) cache prefix: every row's logits within LOGIT_ATOL of the oracle
-    (mean below 0.01), predictions equal up to near ties, K/V rows appended."""
+    (mean below 0.01), predictions equal up to near ties, K/V rows appended.
+
+    Context 8188 (rows at positions 8188..8192, 8193 live keys): 33 splits of
+    256 keys, the last holding key 8192 alone; at these cluster shapes
+    (16 CTAs x C >= 3, 8 CTAs x C >= 5) that split is the only one of the
+    last working cluster, and every row but the last cannot see it. Those
+    rows take the merge branch where a cluster has no visible key
+    (log-sum-exp -inf, weight 0)."""
     from hackthenorth_b200.config import ModelConfig
     from hackthenorth_b200.engine import Engine
     from hackthenorth_b200.weights import random_state_dict
