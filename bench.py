@@ -22,10 +22,25 @@ step streams them from HBM.
              bf16, DynamicCache) decoding at the same shape on the host cores
 * --impl reference  times only that CPU path (rank 0; other ranks exit 0)
 
+* repeats    further windows of the same K steps: every window's tok/s,
+             the median and the spread
+* parity     correctness gate before timing (every N): the 0.6B golden
+             prompts of the reference's eager path (tokens up to the
+             golden file's first exact tie, top-64 logits within 0.0625),
+             and at N > 1 one 8B-shaped layer tensor parallel vs one GPU;
+             the run exits 3 after printing its line if the gate fails
+* configs    the other BASELINE configurations (N = 1): 8B at 32k, 4B with
+             a real 4096-token prefill + 256 steps, 0.6B with a 32-token
+             prompt + 128 steps, the attention op sweep; and at every N the
+             speculative line (8B target tensor parallel over the N GPUs,
+             0.6B draft replica per rank, k = 4, synthetic p = 0.7 drafts,
+             context 8192)
+
 Multi-GPU (N>1, launched by torchrun): tensor parallelism over the N GPUs
-(KV heads, FFN columns and vocabulary sharded; an NCCL fp32 all-reduce after
-o-proj and after down). `value` is the one sequence's tok/s (strong scaling);
-`step_roofline` uses the bytes each GPU streams per step.
+(KV heads, FFN columns and vocabulary sharded; the o-proj and down partial
+sums reduced over NVLink peer memory inside their GEMV epilogues). `value`
+is the one sequence's tok/s (strong scaling); `step_roofline` uses the bytes
+each GPU streams per step.
 """
 from __future__ import annotations
 
@@ -221,8 +236,10 @@ def profiled_traffic(name):
 
 def time_dominant_kernel(engine, reps_per_layer=2):
     """Gate/up + SwiGLU GEMV (about half of a step's bytes) launched alone over
-    every layer's weights in turn, timed with CUDA events on the launching
-    stream. Returns (average seconds per launch, algorithmic bytes per launch)."""
+    every layer's weights in turn: the launches are captured once as a CUDA
+    graph and the replay is timed with CUDA events on its stream, so the
+    figure is device time, not Python launch rate. Returns (average seconds
+    per launch, algorithmic bytes per launch)."""
     from hackthenorth_b200 import ops
 
     cfg = engine.cfg
@@ -231,26 +248,249 @@ def time_dominant_kernel(engine, reps_per_layer=2):
     for lw in layers[:3]:
         ops.norm_projection(x, lw["post_norm"], lw["gu"], cfg.rms_eps, swiglu=True)
     torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    n = 0
+    with torch.cuda.graph(graph):
+        for _ in range(reps_per_layer):
+            for lw in layers:
+                ops.norm_projection(x, lw["post_norm"], lw["gu"], cfg.rms_eps, swiglu=True)
+                n += 1
+    graph.replay()
+    torch.cuda.synchronize()
     stream = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    n = 0
-    for _ in range(reps_per_layer):
-        for lw in layers:
-            ops.norm_projection(x, lw["post_norm"], lw["gu"], cfg.rms_eps, swiglu=True)
-            n += 1
+    graph.replay()
     e1.record(stream)
     torch.cuda.synchronize()
+    ops.check_device_errors(engine.device)
     sec = e0.elapsed_time(e1) / 1000.0 / n
+    del graph
     gu = layers[0]["gu"]
     nbytes = gu.numel() * gu.element_size() + cfg.hidden * 2 * 2 + (gu.shape[0] // 2) * 2
     return sec, nbytes
 
 
+def build_engine(cfg, world, dev, seed=0, cpu_weights=False):
+    """This rank's engine: tensor parallel under torchrun, else one GPU.
+    ``cpu_weights``: draw the weights with the CPU generator (the golden
+    vectors' weights), else on the GPU."""
+    from hackthenorth_b200.engine import Engine
+
+    if world > 1:
+        from hackthenorth_b200 import tp
+
+        return tp.engine_from_random(cfg, seed=seed, init_device="cpu" if cpu_weights else None)
+    return Engine.from_random(cfg, seed=seed, device=str(dev), init_device="cpu" if cpu_weights else str(dev))
+
+
+def timed_steps(state, steps, first_token, ctx, world):
+    """K graph replays from position ``ctx``, bracketed by a barrier and a
+    synchronize on both sides, CUDA events on the replay stream; the slowest
+    rank's seconds."""
+    state.token.fill_(first_token)
+    state.position.fill_(ctx)
+    stream = torch.cuda.current_stream()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        state.step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    sec = e0.elapsed_time(e1) / 1000.0
+    state.check()
+    return max_over_ranks(sec, world)
+
+
+def warm_state(state, warmup, first_token, ctx):
+    state.token.fill_(first_token)
+    state.position.fill_(ctx)
+    if not state.captured:
+        state.capture()
+    for _ in range(warmup):
+        state.step()
+    state.check()
+
+
+def prefill_decode_line(cfg, world, dev, ctx, n_decode, warmup, peak_gbs, note):
+    """A configuration line: a real batched prefill of a seeded random prompt
+    of ``ctx`` tokens (timed after one untimed prefill of the same prompt),
+    then ``n_decode`` greedy decode steps from position ``ctx`` timed as one
+    window (graph replays; warm-up steps first, whose K/V slots the timed
+    steps overwrite)."""
+    engine = build_engine(cfg, world, dev)
+    st = engine.new_state(ctx, n_decode + 1, capacity=ctx + n_decode + warmup + 8)
+    prompt = torch.randint(0, cfg.vocab, (ctx,), generator=torch.Generator().manual_seed(1)).to(dev)
+    st.prefill(prompt)
+    st.check()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record()
+    st.prefill(prompt)
+    p1.record()
+    torch.cuda.synchronize()
+    st.check()
+    prefill_ms = p0.elapsed_time(p1)
+    first = st.read_token()[0]
+    warm_state(st, warmup, first, ctx)
+    sec = timed_steps(st, n_decode, first, ctx, world)
+    mean_ctx = int(round(ctx + (n_decode - 1) / 2.0))
+    step_bytes = cfg.step_bytes(mean_ctx) // world
+    line = {"tok_s": round(n_decode / sec, 2), "ms_per_step": round(1000.0 * sec / n_decode, 4),
+            "steps": n_decode, "prefill_tokens": ctx, "prefill_ms": round(prefill_ms, 3),
+            "roofline": {"bytes_per_step": step_bytes, "achieved_GBps": round(step_bytes / (sec / n_decode) / 1e9, 1),
+                         "peak": peak_gbs, "frac": round(step_bytes / (sec / n_decode) / 1e9 / peak_gbs, 4),
+                         "roofline_tok_s": round(peak_gbs * 1e9 / step_bytes, 1)},
+            "workload": note}
+    import gc
+
+    del st, engine
+    gc.collect()  # engine and state refer to each other
+    torch.cuda.empty_cache()
+    return line
+
+
+def seeded_kv(state, cfg, ctx, dev, seed=2):
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    for t in (state.keys, state.values):
+        for l in range(cfg.n_layers):
+            t[l, ..., :ctx, :].normal_(generator=gen)  # [Hkv, cap, D] or [B, Hkv, cap, D]
+
+
+GOLDEN_FILES = ("qwen3_0p6b_greedy.json", "qwen3_0p6b_greedy_notie.json")
+LOGIT_ATOL = 0.0625
+
+
+def gather_logits(t, world):
+    """The full logit row from this rank's vocabulary shard (every rank)."""
+    if world == 1:
+        return t.float().cpu()
+    import torch.distributed as dist
+
+    parts = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(parts, t.contiguous())
+    return torch.cat(parts, dim=-1).float().cpu()
+
+
+def parity_check(world, rank, dev):
+    """Correctness gate run before timing (every N): the engine (tensor
+    parallel over the N GPUs) against the committed golden vectors of the
+    reference's eager path, and at N > 1 against this engine on one GPU.
+
+    * 0.6B shape, CPU-drawn seed-0 weights, each golden prompt: the plain
+      greedy stream equals the golden tokens up to the golden file's first
+      exact top-1/top-2 tie (all 128 for the tie-free prompt), and every
+      teacher-forced step's logits at the golden top-64 ids lie within
+      LOGIT_ATOL of the native values.
+    * N > 1: one Qwen3-8B-shaped layer (full vocabulary) over a seeded N(0, 1)
+      cache at context 4096: the tensor-parallel step's logits (gathered from
+      the vocabulary shards) against the same step on rank 0's GPU alone, max
+      abs within LOGIT_ATOL, mean within 0.01, same greedy token unless the
+      one-GPU logits hold a near tie.
+    Returns (report, ok); every rank takes the same collective steps."""
+    import dataclasses
+
+    from hackthenorth_b200.config import QWEN3_0P6B, QWEN3_8B
+
+    report = {"tolerance": {"logit_max_abs": LOGIT_ATOL, "tp_vs_one_gpu_mean_abs": 0.01}}
+    ok = True
+    threads = torch.get_num_threads()
+    torch.set_num_threads(max(1, (os.cpu_count() or 1) // world))
+    engine = build_engine(QWEN3_0P6B, world, dev, seed=0, cpu_weights=True)
+    torch.set_num_threads(threads)
+    for name in GOLDEN_FILES:
+        path = os.path.join(ROOT, "tests", "golden", name)
+        if not os.path.exists(path):
+            continue
+        with open(path) as f:
+            g = json.load(f)
+        prompt, gold = g["prompt"], g["tokens"]
+        st = engine.new_state(len(prompt), len(gold), keep_logits=True)
+        st.prefill(torch.tensor(prompt, dtype=torch.int64, device=dev))
+        rows = [gather_logits(st.logits, world)]
+        for t in gold[:-1]:
+            st.token.fill_(t)
+            st.step()
+            rows.append(gather_logits(st.logits, world))
+        st.check()
+        worst = 0.0
+        for row, s in zip(rows, g["steps"]):
+            ids = torch.tensor(s["top_ids"])
+            worst = max(worst, float((row[ids] - torch.tensor(s["top_vals"])).abs().max()))
+        free = [s[0] for s in engine.generate([prompt], len(gold), draft_tokens=0)]
+        engine.state.check()
+        upto = next((i for i, s in enumerate(g["steps"]) if s["margin"] == 0.0), len(gold))
+        same = free[:upto] == gold[:upto]
+        first_diff = next((i for i, (a, b) in enumerate(zip(free, gold)) if a != b), None)
+        report[name] = {"tokens_required_equal": upto, "tokens_equal": same, "first_difference": first_diff,
+                        "top64_logit_max_abs": round(worst, 5)}
+        ok = ok and same and worst <= LOGIT_ATOL
+        del st
+    import gc
+
+    del engine
+    gc.collect()
+    torch.cuda.empty_cache()
+    if world > 1:
+        from hackthenorth_b200.engine import Engine
+
+        cfg1 = dataclasses.replace(QWEN3_8B, n_layers=1)
+        ctx = 4096
+        gen = torch.Generator(device=dev).manual_seed(4)
+        kfull = torch.randn(1, cfg1.n_kv_heads, ctx, cfg1.head_dim, generator=gen, device=dev).to(torch.bfloat16)
+        vfull = torch.randn(1, cfg1.n_kv_heads, ctx, cfg1.head_dim, generator=gen, device=dev).to(torch.bfloat16)
+        hl = cfg1.n_kv_heads // world
+        tpe = build_engine(cfg1, world, dev, seed=3)
+        st = tpe.new_state(ctx, 4, keep_logits=True)
+        st.keys[:, :, :ctx] = kfull[:, rank * hl:(rank + 1) * hl]
+        st.values[:, :, :ctx] = vfull[:, rank * hl:(rank + 1) * hl]
+        st.token.fill_(17)
+        st.position.fill_(ctx)
+        st.step()
+        st.check()
+        tp_logits = gather_logits(st.logits, world)
+        tp_tok = st.read_token()[0]
+        del st, tpe
+        gc.collect()  # releases the TP graph (it holds NCCL calls) and the weights
+        torch.cuda.empty_cache()
+        flag = torch.ones(1, dtype=torch.int32, device=dev)
+        if rank == 0:
+            one = Engine.from_random(cfg1, seed=3, device=str(dev), init_device=str(dev))
+            s1 = one.new_state(ctx, 4, keep_logits=True)
+            s1.keys[:, :, :ctx] = kfull
+            s1.values[:, :, :ctx] = vfull
+            s1.token.fill_(17)
+            s1.position.fill_(ctx)
+            s1.step()
+            s1.check()
+            ref = s1.logits.float().cpu()
+            one_tok = s1.read_token()[0]
+            d = (tp_logits - ref).abs()
+            top2 = ref.topk(2).values
+            tok_ok = tp_tok == one_tok or float(top2[0] - top2[1]) <= LOGIT_ATOL
+            good = float(d.max()) <= LOGIT_ATOL and float(d.mean()) <= 0.01 and tok_ok
+            report["tp_vs_one_gpu"] = {"workload": f"qwen3-8b shape, 1 layer, context {ctx}, seeded N(0,1) K/V",
+                                       "logit_max_abs": round(float(d.max()), 5),
+                                       "logit_mean_abs": round(float(d.mean()), 6),
+                                       "token_tp": tp_tok, "token_one_gpu": one_tok, "ok": good}
+            flag.fill_(1 if good else 0)
+            del s1, one
+            gc.collect()
+            torch.cuda.empty_cache()
+        import torch.distributed as dist
+
+        dist.broadcast(flag, src=0)
+        ok = ok and bool(flag.item())
+    report["ok"] = ok
+    return report, ok
+
+
 def run_ours(args):
     from hackthenorth_b200 import build as qbuild
     from hackthenorth_b200.config import get_config
-    from hackthenorth_b200.engine import Engine
 
     world, rank, local = dist_setup(args.gpus)
     qbuild.build()
@@ -263,18 +503,19 @@ def run_ours(args):
         cfg = dataclasses.replace(cfg, n_layers=args.layers)
     dev = torch.device(f"cuda:{local}")
     peak_gbs, peak_kind = load_peaks()
-    if world > 1:
-        from hackthenorth_b200 import tp
-
-        engine = tp.engine_from_random(cfg, seed=0)  # tensor parallel: this rank's shard
-    else:
-        engine = Engine.from_random(cfg, seed=0, device=str(dev), init_device=str(dev))
-    torch.cuda.empty_cache()
-    ctx = args.context
-    total_steps = args.warmup + args.steps
     B = args.batch
     if B > 1 and (world > 1 or args.real_prefill):
         raise SystemExit("--batch > 1 runs on one GPU over seeded K/V (no --real-prefill)")
+    full = not args.layers and B == 1 and not args.real_prefill
+
+    parity, parity_ok = (None, True)
+    if full and not args.no_parity:
+        parity, parity_ok = parity_check(world, rank, dev)
+
+    engine = build_engine(cfg, world, dev)
+    torch.cuda.empty_cache()
+    ctx = args.context
+    total_steps = args.warmup + args.steps
     state = engine.new_state(ctx, total_steps + 2, capacity=ctx + 2 * total_steps + 8, batch=B)
     prefill_ms = None
     if args.real_prefill and world == 1:
@@ -292,36 +533,20 @@ def run_ours(args):
         prefill_ms = p0.elapsed_time(p1)
         first_token = state.read_token()[0]
     else:
-        gen = torch.Generator(device=dev).manual_seed(2)
-        for t in (state.keys, state.values):
-            for l in range(cfg.n_layers):
-                t[l, ..., :ctx, :].normal_(generator=gen)  # [Hkv, cap, D] or [B, Hkv, cap, D]
+        seeded_kv(state, cfg, ctx, dev)
         first_token = 1
-    state.token.fill_(first_token)
-    state.position.fill_(ctx)
-    state.capture()
+    warm_state(state, args.warmup, first_token, ctx)
     stream = torch.cuda.current_stream()
-    for _ in range(args.warmup):
-        state.step()
-    state.check()
-    state.token.fill_(first_token)
-    state.position.fill_(ctx)
-    torch.cuda.synchronize()
 
     clocks = ClockSampler(local)
     clocks.start()
-    barrier(world)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        state.step()
-    e1.record(stream)
-    torch.cuda.synchronize()
-    barrier(world)
-    dev_s = e0.elapsed_time(e1) / 1000.0
+    t_dev = timed_steps(state, args.steps, first_token, ctx, world)
     clk = clocks.stop()
-    state.check()
+    # Repeats: the same K steps timed again in further windows (the line's
+    # value is the first window, as the contract asks; the spread shows how
+    # stable it is).
+    windows = [t_dev] + [timed_steps(state, args.steps, first_token, ctx, world) for _ in range(args.repeats)]
+    rates = [B * args.steps / t for t in windows]
 
     # e2e: the same steps with host buffers (pinned H2D of the token, replay,
     # D2H of the result, sync) — the per-token loop of generate().
@@ -345,23 +570,29 @@ def run_ours(args):
     state.check()
 
     kern_s, kern_bytes = time_dominant_kernel(engine)
+    kern_s = max_over_ranks(kern_s, world)
 
     # The public API end to end (one GPU, batch one): Engine.generate on the
     # configuration's seeded random prompt of `ctx` tokens; decode rate from
     # the first yielded token to the last (prefill excluded), host ints out.
-    gen_rate = None
-    if world == 1 and B == 1 and not args.layers:
+    # Default generate speculates with prompt lookup (the reference's
+    # default); draft_tokens=0 is plain decode with replays running ahead.
+    gen_rates = {}
+    if world == 1 and full:
         prompt = torch.randint(0, cfg.vocab, (ctx,), generator=torch.Generator().manual_seed(1)).tolist()
         n_gen = args.steps + 1
-        for _ in engine.generate([prompt], 4):  # warm-up: shape-keyed state, graph capture
-            pass
-        t_first = None
-        for i, _tok in enumerate(engine.generate([prompt], n_gen)):
-            if i == 0:
-                t_first = time.perf_counter()
-        gen_rate = (n_gen - 1) / (time.perf_counter() - t_first)
+        for label, kw in (("default", {}), ("plain", {"draft_tokens": 0})):
+            for _ in engine.generate([prompt], 4, **kw):  # warm-up: shape-keyed state, graph capture
+                pass
+            for _ in engine.generate([prompt], n_gen, **kw):
+                pass
+            t_first = None
+            for i, _tok in enumerate(engine.generate([prompt], n_gen, **kw)):
+                if i == 0:
+                    t_first = time.perf_counter()
+            gen_rates[label] = (n_gen - 1) / (time.perf_counter() - t_first)
+            engine.state.check()
 
-    t_dev = max_over_ranks(dev_s, world)
     t_e2e = max_over_ranks(e2e_s, world)
     ms_step = 1000.0 * t_dev / args.steps
     value = B * args.steps / t_dev  # B sequences; with N GPUs one sequence sharded across them
@@ -395,10 +626,14 @@ def run_ours(args):
                    "decode_path": os.environ.get("QB_STEP_KERNEL") == "1" and world == 1 and "step-kernel"
                    or "per-sublayer",
                    "l2": "inputs larger than L2 (weights stream %.1f GB per step)" % (cfg.weight_bytes_per_token() / 1e9)},
+        "repeats": {"windows": len(windows), "steps_each": args.steps,
+                    "tok_s": [round(r, 2) for r in rates], "median_tok_s": round(statistics.median(rates), 2),
+                    "spread_pct": round(100.0 * (max(rates) - min(rates)) / statistics.median(rates), 2)},
         "roofline": {"bound": "hbm", "kernel": "gemv_kernel<EPI_SWIGLU> (post-norm + gate/up + SwiGLU)",
                      "achieved": round(achieved, 1), "peak": peak_gbs, "unit": "GB/s",
                      "frac": round(achieved / peak_gbs, 4), "peak_source": peak_kind,
                      "bytes_per_launch": kern_bytes, "us_per_launch": round(kern_s * 1e6, 2),
+                     "timing": "CUDA events around a replayed graph of the kernel over every layer's weights",
                      "traffic": profiled_traffic("gemv_swiglu_qwen3-8b") if (cfg.name == "qwen3-8b" and world == 1) else None,
                      "traffic_source": "ncu capture, profiles/gemv_swiglu_qwen3-8b.md"},
         "step_roofline": {"bytes_per_step": step_bytes, "achieved": round(step_bytes / (t_dev / args.steps) / 1e9, 1),
@@ -408,22 +643,71 @@ def run_ours(args):
         "e2e": {"value": round(args.steps / t_e2e, 3), "unit": "tok/s",
                 "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
                 "d2h_bytes_per_step": host_out.numel() * host_out.element_size()},
-        "e2e_generate": None if gen_rate is None else {
-            "value": round(gen_rate, 3), "unit": "tok/s",
-            "how": "Engine.generate(prompt of the context length) yielding host token ids; first to last yield; "
-                   "replays run %d ahead of the consumer through a pinned device-to-host token ring" % engine.STREAM_DEPTH},
+        "e2e_generate": None if not gen_rates else {
+            "value": round(gen_rates["default"], 3), "unit": "tok/s",
+            "plain_value": round(gen_rates["plain"], 3),
+            "how": "Engine.generate(prompt of the context length) yielding host token ids; first to last yield. "
+                   "value: the default generate (prompt-lookup speculation, as the reference's); plain_value: "
+                   "draft_tokens=0, replays %d ahead of the consumer through a pinned device-to-host token ring"
+                   % engine.STREAM_DEPTH},
         "gpu_launches": launches_per_step * args.steps,
         "prefill_ms": None if prefill_ms is None else round(prefill_ms, 3),
         "profile_only": bool(args.layers),
         "clocks": clk,
+        "parity": parity,
     }
     if B > 1:
         # the dominant kernels of a batched step are the rows GEMVs: the step's
         # own bytes over its time are the roofline figure
         out["roofline"] = dict(out["step_roofline"], bound="hbm", kernel="whole batched step (rows kernels)",
                                traffic=None, peak_source=peak_kind)
+
+    configs = {}
+    if full and world == 1 and cfg.name == "qwen3-8b" and not args.no_configs:
+        # BASELINE configurations beside the headline, each as its own line
+        long_ctx = 32768
+        del state
+        torch.cuda.empty_cache()
+        st = engine.new_state(long_ctx, total_steps + 2, capacity=long_ctx + 2 * total_steps + 8)
+        seeded_kv(st, cfg, long_ctx, dev)
+        warm_state(st, args.warmup, 1, long_ctx)
+        sec = timed_steps(st, args.steps, 1, long_ctx, world)
+        sb = cfg.step_bytes(int(round(long_ctx + (args.steps - 1) / 2.0)))
+        configs["qwen3-8b@32k"] = {
+            "tok_s": round(args.steps / sec, 2), "ms_per_step": round(1000.0 * sec / args.steps, 4),
+            "steps": args.steps,
+            "roofline": {"bytes_per_step": sb, "achieved_GBps": round(sb / (sec / args.steps) / 1e9, 1),
+                         "peak": peak_gbs, "frac": round(sb / (sec / args.steps) / 1e9 / peak_gbs, 4),
+                         "roofline_tok_s": round(peak_gbs * 1e9 / sb, 1)},
+            "workload": "qwen3-8b shape, batch 1, KV cache of 32768 seeded N(0,1) positions, greedy decode"}
+        del st
+    import gc
+
+    del engine
+    state = engine = None
+    gc.collect()  # engine and state refer to each other
+    torch.cuda.empty_cache()
+    if full and world == 1 and cfg.name == "qwen3-8b" and not args.no_configs:
+        from hackthenorth_b200.config import QWEN3_0P6B, QWEN3_4B
+
+        cs = ClockSampler(local)
+        cs.start()
+        configs["qwen3-4b"] = prefill_decode_line(
+            QWEN3_4B, world, dev, 4096, 256, args.warmup, peak_gbs,
+            "qwen3-4b shape, batched prefill of a seeded random 4096-token prompt, then 256 greedy decode steps "
+            "(KV cache 4096 -> 4352)")
+        configs["qwen3-0.6b"] = prefill_decode_line(
+            QWEN3_0P6B, world, dev, 32, 128, args.warmup, peak_gbs,
+            "qwen3-0.6b shape, 32-token seeded random prompt, then 128 greedy decode steps")
+        configs["attention"] = {"cases": attention_cases(args.warmup, peak_gbs),
+                                "workload": "decode attention op, GQA 32/8, D 128, bf16 N(0,1) Q/K/V, batch 1; "
+                                            "us = device time per call from a replayed graph of the calls"}
+        configs["clocks"] = cs.stop()
+    if full and not args.no_spec:
+        configs["speculative"] = speculative_line(args, world, rank, local)
+    if configs:
+        out["configs"] = configs
     if world == 1 and not args.no_cpu_baseline and B == 1:
-        del state, engine
         torch.cuda.empty_cache()
         out["cpu_baseline"] = cpu_reference_decode(cfg, ctx, budget_s=args.cpu_budget)
     if rank == 0:
@@ -440,21 +724,19 @@ def run_ours(args):
         torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
+    if not parity_ok:
+        raise SystemExit(3)
 
 
-def run_attention_sweep(args):
+def attention_cases(warmup, peak_gbs):
     """Decode-attention op sweep (GQA 32/8, D 128, bf16 N(0,1), batch 1):
     KV lengths 512..131072, 1 query row and the 5-row causal verify variant.
     Each timed launch reads a different KV buffer (>= 256 MB cycled), so the
     K/V bytes come from HBM. "us" is device time per call (the timed calls
     replayed as one CUDA graph); "us_host" the same calls issued one by one
-    from Python. One JSON line with a per-case list."""
-    from hackthenorth_b200 import build as qbuild
+    from Python. Returns the per-case list."""
     from hackthenorth_b200 import ops
 
-    qbuild.build()
-    torch.cuda.set_device(0)
-    peak_gbs, peak_kind = load_peaks()
     gen = torch.Generator(device="cuda").manual_seed(2)
     cases = []
     for L in (512, 4096, 32768, 131072):
@@ -468,7 +750,7 @@ def run_attention_sweep(args):
             for k, v in kv[:2]:
                 ops.grouped_attention(q, k, v, pos)
             torch.cuda.synchronize()
-            reps = max(args.warmup + 3, 40 if L <= 4096 else 10)
+            reps = max(warmup + 3, 40 if L <= 4096 else 10)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             # host-driven: one op call per launch from Python (tensor maps encoded per call)
             e0.record()
@@ -502,12 +784,23 @@ def run_attention_sweep(args):
                           "us_host": round(host_sec * 1e6, 2)})
             del kv
             torch.cuda.empty_cache()
+    return cases
+
+
+def run_attention_sweep(args):
+    """The attention op sweep alone: one JSON line with a per-case list."""
+    from hackthenorth_b200 import build as qbuild
+
+    qbuild.build()
+    torch.cuda.set_device(0)
+    peak_gbs, peak_kind = load_peaks()
+    cases = attention_cases(args.warmup, peak_gbs)
     print(json.dumps({"op": "grouped_attention", "metric": "decode attention us and GB/s of K/V reads",
                       "peak_gbs": peak_gbs, "peak_source": peak_kind, "dtype": "bf16",
                       "config": {"q_heads": 32, "kv_heads": 8, "head_dim": 128}, "cases": cases}), flush=True)
 
 
-def run_speculative(args):
+def speculative_line(args, world, rank, local, ctx=8192):
     """Speculative decoding line (not the headline): the 8B target verifies
     k = 4 draft tokens per cycle (tensor parallel over the ranks under
     torchrun), the 0.6B draft model runs its k decode steps every cycle on each
@@ -523,16 +816,13 @@ def run_speculative(args):
     that point with plain decode steps (untimed), recording the plain top-2
     margin there. Only the draft + verify cycles are timed (CUDA events on the
     stream, plus the host read of each cycle's predictions)."""
-    from hackthenorth_b200 import build as qbuild
     from hackthenorth_b200.config import QWEN3_0P6B, get_config
     from hackthenorth_b200.engine import Engine
     from hackthenorth_b200.speculate import SyntheticDraft
 
-    world, rank, local = dist_setup(args.gpus)
-    qbuild.build()
     dev = torch.device(f"cuda:{local}")
     cfg = get_config(args.config)
-    ctx, k, n_out = args.context, 4, 256
+    k, n_out = 4, 256
     if world > 1:
         from hackthenorth_b200 import tp
 
@@ -653,17 +943,29 @@ def run_speculative(args):
         "timing": "sum of per-cycle CUDA-event times (draft steps + verify + the host read of its predictions), "
                   "max over ranks; re-anchoring after a near-tie disagreement is untimed",
     }
+    # the verify and decode graphs hold NCCL calls under tensor parallelism:
+    # release them before the caller tears the process group down
+    import gc
+
+    ts = ds = target = draft = None
+    gc.collect()
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return line
+
+
+def run_speculative(args):
+    """The speculative line alone (target tensor parallel under torchrun)."""
+    from hackthenorth_b200 import build as qbuild
+
+    world, rank, local = dist_setup(args.gpus)
+    qbuild.build()
+    line = speculative_line(args, world, rank, local, ctx=args.context)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
-        import gc
-
         import torch.distributed as dist
 
-        # the verify and decode graphs hold NCCL calls: release them first
-        ts = ds = target = draft = None
-        gc.collect()
-        torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
 
@@ -711,6 +1013,12 @@ def main(argv=None):
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--repeats", type=int, default=4,
+                    help="further timed windows of K steps after the first (median and spread reported)")
+    ap.add_argument("--no-parity", action="store_true", help="skip the correctness gate run before timing")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the other BASELINE configurations (0.6B, 4B, 8B@32k, attention sweep)")
+    ap.add_argument("--no-spec", action="store_true", help="skip the speculative-decoding configuration")
     ap.add_argument("--op", choices=("decode", "attention", "speculative"), default="decode",
                     help="attention: the decode-attention op sweep; speculative: verify + draft cycles "
                          "(neither is the headline line)")

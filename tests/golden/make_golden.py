@@ -13,6 +13,12 @@ runs exactly that on seeded random-init weights and writes small fixtures:
   bf16 logits (values, ids), the top-1/top-2 margin and fp64 sum / sum of
   squares of the whole logit row. Also the noise floor of the reference
   itself: cached-decode vs full-prefix logits on the first 8 steps.
+* ``qwen3_0p6b_greedy_notie.json``: the same for a second 32-token prompt
+  (seed 81) chosen because no step of its 128 has a top-1/top-2 margin below
+  0.0625 (4 bf16 ulps at the logits' scale), so every token can be required
+  identical; the seed-1 prompt holds an exact tie at step 14. Prompt seeds
+  from 2 upward were scanned in order: 81 is the first whose stream changes
+  token and has no margin below 0.0625 (most seeds hold exact ties).
 * ``qwen3_small_greedy.npz``: the small test shape (seed 0 weights, seed 1
   prompt of 16), 24 greedy tokens with the full bf16 logit rows.
 * ``attention_sdpa.npz``: fp32 SDPA outputs (the reference's attention check,
@@ -57,13 +63,10 @@ def bf16_bits(t: torch.Tensor) -> np.ndarray:
     return t.to(torch.bfloat16).view(torch.int16).numpy().astype(np.uint16)
 
 
-def main():
-    torch.set_num_threads(max(1, os.cpu_count() or 1))
-    # --- 0.6B greedy, 128 steps -------------------------------------------------
-    cfg = QWEN3_0P6B
-    state = random_state_dict(cfg, seed=0)
-    model = hf_eager.build_hf_model(cfg, state)
-    prompt = prompt_ids(cfg.vocab, 32)
+def write_0p6b_greedy(model, cfg, prompt_seed: int, filename: str):
+    """128 native greedy tokens for a 32-token prompt, per-step top-64 logits,
+    margins, row sums, and the native cached vs full-prefix noise floor."""
+    prompt = prompt_ids(cfg.vocab, 32, seed=prompt_seed)
     logits = []
     tokens = hf_eager.greedy(model, prompt, 128, logits)
     steps = []
@@ -79,14 +82,27 @@ def main():
         })
     tf = hf_eager.teacher_forced_logits(model, prompt + tokens[:8], len(prompt) - 1)
     floor = [float((a.float() - b.float()).abs().max()) for a, b in zip(logits[:8], tf[:8])]
-    with open(os.path.join(HERE, "qwen3_0p6b_greedy.json"), "w") as f:
+    with open(os.path.join(HERE, filename), "w") as f:
         json.dump({
-            "config": cfg.name, "weights_seed": 0, "prompt_seed": 1,
+            "config": cfg.name, "weights_seed": 0, "prompt_seed": prompt_seed,
             "transformers": __import__("transformers").__version__,
             "prompt": prompt, "tokens": tokens, "steps": steps,
             "self_noise_cached_vs_full_prefix": floor,
         }, f)
+
+
+def main(only_notie: bool = False):
+    torch.set_num_threads(max(1, os.cpu_count() or 1))
+    # --- 0.6B greedy, 128 steps -------------------------------------------------
+    cfg = QWEN3_0P6B
+    state = random_state_dict(cfg, seed=0)
+    model = hf_eager.build_hf_model(cfg, state)
+    if not only_notie:
+        write_0p6b_greedy(model, cfg, 1, "qwen3_0p6b_greedy.json")
+    write_0p6b_greedy(model, cfg, 81, "qwen3_0p6b_greedy_notie.json")
     del model, state
+    if only_notie:
+        return
 
     # --- small shape, full logits ----------------------------------------------
     cfg = QWEN3_SMALL
@@ -109,4 +125,4 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    main(only_notie="--notie" in sys.argv)

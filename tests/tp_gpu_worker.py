@@ -49,9 +49,11 @@ def main():
         torch.cuda.synchronize()
         dist.destroy_process_group()
         return
-    toks = [s[0] for s in engine.generate([prompt], n_new)]
+    toks = [s[0] for s in engine.generate([prompt], n_new, draft_tokens=0)]  # plain decode
     engine.state.check()
-    toks2 = [s[0] for s in engine.generate([prompt], n_new)]  # graph replay with a fresh prompt state
+    # the default generate (prompt-lookup speculation, tensor-parallel verify)
+    # with a fresh prompt state
+    toks2 = [s[0] for s in engine.generate([prompt], n_new)]
     if dist.get_rank() == 0:
         with open(out_path, "w") as f:
             json.dump({"tokens": toks, "again": toks2}, f)
