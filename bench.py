@@ -495,18 +495,27 @@ def run_ours(args):
     world, rank, local = dist_setup(args.gpus)
     qbuild.build()
     cfg = get_config(args.config)
+    import dataclasses
+
     if args.layers:
         # Profiling only: fewer layers of the same shapes (keeps each kernel's
         # launch identical, and the device footprint small enough for ncu).
-        import dataclasses
-
         cfg = dataclasses.replace(cfg, n_layers=args.layers)
+    if args.shard_of > 1:
+        # Profiling only: one rank's shapes under N-way tensor parallelism (its
+        # query/KV heads, FFN columns and vocabulary rows) on one GPU without
+        # the cross-rank exchange, so a 1-GPU profiler sees the per-rank kernels.
+        n = args.shard_of
+        if world > 1 or cfg.n_kv_heads % n or cfg.ffn % n or cfg.vocab % n:
+            raise SystemExit("--shard-of N runs on one GPU and needs KV heads, FFN and vocabulary divisible by N")
+        cfg = dataclasses.replace(cfg, name=f"{cfg.name}-tp{n}-rank", n_heads=cfg.n_heads // n,
+                                  n_kv_heads=cfg.n_kv_heads // n, ffn=cfg.ffn // n, vocab=cfg.vocab // n)
     dev = torch.device(f"cuda:{local}")
     peak_gbs, peak_kind = load_peaks()
     B = args.batch
     if B > 1 and (world > 1 or args.real_prefill):
         raise SystemExit("--batch > 1 runs on one GPU over seeded K/V (no --real-prefill)")
-    full = not args.layers and B == 1 and not args.real_prefill
+    full = not args.layers and B == 1 and not args.real_prefill and args.shard_of <= 1
 
     parity, parity_ok = (None, True)
     if full and not args.no_parity:
@@ -571,6 +580,20 @@ def run_ours(args):
 
     kern_s, kern_bytes = time_dominant_kernel(engine)
     kern_s = max_over_ranks(kern_s, world)
+
+    if args.trace and B == 1:
+        # One more step with the kernels' own timestamps (after the timed
+        # windows; the trace drops and re-captures the step graph).
+        from hackthenorth_b200.trace import StepTrace
+
+        tr = StepTrace(state)
+        warm_state(state, 2, first_token, ctx)
+        timed_steps(state, 1, first_token, ctx, world)
+        summ = tr.summary()
+        tr.close()
+        path = args.trace if world == 1 else f"{args.trace}.rank{rank}"
+        with open(path, "w") as f:
+            json.dump({"config": cfg.name, "context": ctx, "n_gpus": world, "rank": rank, **summ}, f)
 
     # The public API end to end (one GPU, batch one): Engine.generate on the
     # configuration's seeded random prompt of `ctx` tokens; decode rate from
@@ -652,7 +675,7 @@ def run_ours(args):
                    % engine.STREAM_DEPTH},
         "gpu_launches": launches_per_step * args.steps,
         "prefill_ms": None if prefill_ms is None else round(prefill_ms, 3),
-        "profile_only": bool(args.layers),
+        "profile_only": bool(args.layers) or args.shard_of > 1,
         "clocks": clk,
         "parity": parity,
     }
@@ -1024,6 +1047,12 @@ def main(argv=None):
                          "(neither is the headline line)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: override the layer count (the line is marked profile_only)")
+    ap.add_argument("--trace", default="",
+                    help="write a per-launch timeline of one decode step (the kernels' %%globaltimer stamps) "
+                         "to this JSON path (per rank under torchrun: PATH.rankR)")
+    ap.add_argument("--shard-of", type=int, default=1,
+                    help="profiling only: one rank's shapes under N-way tensor parallelism, on one GPU "
+                         "without the exchange (the line is marked profile_only)")
     ap.add_argument("--real-prefill", action="store_true",
                     help="fill the context with a real prefill of a seeded random prompt (timed, reported as "
                          "prefill_ms) instead of seeded random K/V values")

@@ -80,6 +80,7 @@ struct AttnArgs {
   int batch_hkv;         // rows kernel, batched decode: KV heads per sequence (KV head h of the
                          // launch belongs to sequence h / batch_hkv, whose position is pos[h / batch_hkv]);
                          // 0: one sequence, pos[i] is query i's position
+  unsigned long long* trace;  // decode cluster kernel: this launch's trace records (common.cuh), or NULL
 };
 
 __host__ inline size_t attn_smem_bytes(int mt) {

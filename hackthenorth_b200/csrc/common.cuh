@@ -43,6 +43,25 @@ __device__ __forceinline__ void report_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
 
+// ---- tracing -------------------------------------------------------------------
+// Optional %globaltimer stamps (ns) of each CTA of a traced launch, written
+// only when the launch carries a trace pointer (qb_set_trace): record
+// trace[(launch * kTraceMaxCtas + cta) * kTraceStamps + k] with k =
+// TRACE_ENTRY (CTA start), TRACE_WAIT (griddepcontrol.wait returned),
+// TRACE_FIRST (first input stage landed), TRACE_LOOP (main loop done,
+// epilogue / merge starts), TRACE_EXIT (CTA done). CTAs beyond kTraceMaxCtas
+// are not recorded.
+constexpr int kTraceMaxCtas = 256;
+constexpr int kTraceStamps = 8;
+enum TraceStamp : int { TRACE_ENTRY = 0, TRACE_WAIT = 1, TRACE_FIRST = 2, TRACE_LOOP = 3, TRACE_EXIT = 4 };
+__device__ __forceinline__ unsigned long long* trace_slot(unsigned long long* launch_base) {
+  return (launch_base != nullptr && blockIdx.x < kTraceMaxCtas) ? launch_base + (size_t)blockIdx.x * kTraceStamps
+                                                                 : nullptr;
+}
+__device__ __forceinline__ void trace_stamp(unsigned long long* slot, int k) {
+  if (slot != nullptr) slot[k] = global_timer_ns();
+}
+
 // ---- programmatic dependent launch --------------------------------------------
 // Rule used by every kernel here: touch only immutable data (weights) or data
 // written at least two launches earlier before pdl_wait(); call

@@ -115,6 +115,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   const int cl = (blockIdx.x / S) % C;
   const int split = blockIdx.x % S;  // == cluster rank
   const int G = a.Hq / a.Hkv;        // query rows, <= kDecRows
+  unsigned long long* const trace = trace_slot(a.trace);
+  if (tid == 0) trace_stamp(trace, TRACE_ENTRY);
 
   // First cluster phase: arrived now, waited before the first remote store.
   cluster_arrive_relaxed();
@@ -203,6 +205,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     // --------------------------------------------------------------- consumers
     pdl_wait();
     pdl_trigger();
+    if (tid == 0) trace_stamp(trace, TRACE_WAIT);
     if (active) {
       if (tid < kDecRows * kAttnD / 8) reinterpret_cast<uint4*>(sm.qs)[tid] = make_uint4(0, 0, 0, 0);
       named_barrier(kDecBarrierId, kDecWarps * 32);
@@ -255,6 +258,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
           ok = false;
           break;
         }
+        if (c == 0 && lane == 0) trace_stamp(trace, TRACE_FIRST);
         const int kstage = k0 + c * kDecKeys;
         if (owns_new && kstage <= last && last < kstage + kDecKeys) {
           const int kr = (int)last - kstage;
@@ -359,6 +363,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       }
       if (!ok && lane == 0) sm.flags[0] = 1;
       named_barrier(kDecBarrierId, kDecWarps * 32);
+      if (tid == 0) trace_stamp(trace, TRACE_LOOP);
       ok = sm.flags[0] == 0;
       if (ok) {
         // Merge the 8 warps (fixed order) through the drained ring.
@@ -417,6 +422,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         if (r < G) attn_store_out(a, kvh, r, tid & 127, val[i]);
       }
     }
+    if (tid == 0) trace_stamp(trace, TRACE_EXIT);
     return;
   }
   const int W = kAttnD / S;
@@ -452,6 +458,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     clse = mx + log2f(den);
     if (Cact == 1) attn_store_out(a, kvh, r, split * W + off, cval);
   }
+  if (tid == 0 && Cact == 1) trace_stamp(trace, TRACE_EXIT);
   if (Cact == 1) return;
   // Several clusters per head: each CTA publishes its slice of the cluster's
   // result (normalised rows + log-sum-exp) and the CTA of the same slice
@@ -469,6 +476,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     sm.flags[1] = (t == (unsigned)(Cact - 1)) ? 1 : 0;
   }
   __syncthreads();
+  if (tid == 0) trace_stamp(trace, TRACE_EXIT);  // the merging CTA overwrites it below
   if (sm.flags[1] == 0) return;
   if (tid < G * W) {
     const int r = tid / W, off = tid % W;
@@ -483,6 +491,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     attn_store_out(a, kvh, r, split * W + off, acc / den);
   }
   if (tid == 0) a.tickets[kvh * S + split] = 0u;
+  if (tid == 0) trace_stamp(trace, TRACE_EXIT);
 }
 
 }  // namespace qb

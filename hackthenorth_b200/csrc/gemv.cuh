@@ -97,6 +97,7 @@ struct GemvArgs {
   // they come from L2 across the kernel boundary. NULL: nothing to prefetch.
   const bf16* nx_w;
   int nx_K, nx_rows, nx_rpu, nx_kc, nx_grid;
+  unsigned long long* trace;  // this launch's trace records (see common.cuh), or NULL
 };
 
 __host__ __device__ inline int gemv_rows_per_unit(int epi) { return epi == EPI_SWIGLU ? 2 : 1; }
@@ -156,6 +157,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
   uint64_t* full = reinterpret_cast<uint64_t*>(rowsum + ((a.max_rows + 3) & ~3));
   uint64_t* empty = full + stages;
   float* misc = reinterpret_cast<float*>(empty + stages);
+  unsigned long long* const trace = trace_slot(a.trace);
+  if (tid == 0) trace_stamp(trace, TRACE_ENTRY);
 
   if (tid == 0) {
     for (int s = 0; s < stages; ++s) {
@@ -237,6 +240,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
   const int ctid = tid;  // 0..kGemvConsumers-1
   pdl_wait();
   pdl_trigger();
+  if (ctid == 0) trace_stamp(trace, TRACE_WAIT);
 
   // 1. Input row (optionally the embedding gather) and its RMSNorm, to fp32 smem.
   const bf16* xsrc = a.x;
@@ -314,6 +318,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
         ok = false;
         break;
       }
+      if (c == 0 && ctid == 0) trace_stamp(trace, TRACE_FIRST);
       if (active) {
         const int c0 = kc * KC;
         const uint8_t* piece = ring + (size_t)s * stage_bytes + warp * (KC * 2) + lane * 16;
@@ -351,6 +356,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
   if (!ok && lane == 0) reinterpret_cast<volatile int*>(misc)[100] = 1;
   named_barrier(kGemvBarrierId, kGemvConsumers);
   if (reinterpret_cast<volatile int*>(misc)[100] != 0) return;  // uniform across the CTA
+  if (ctid == 0) trace_stamp(trace, TRACE_LOOP);
 
   // 3. Epilogue.
   if constexpr (EPI == EPI_STORE) {
@@ -462,6 +468,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
         *a.counter = 0u;
       }
     }
+    if (ctid == 0) trace_stamp(trace, TRACE_EXIT);
     return;
   }
   if (a.pos_inc != nullptr && b == 0 && ctid == 0) {
@@ -469,6 +476,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
     // grid are past pdl_wait, and the next reader runs after this grid ends.
     *a.pos_inc += 1;
   }
+  if (ctid == 0) trace_stamp(trace, TRACE_EXIT);
 }
 
 }  // namespace qb

@@ -609,6 +609,12 @@ struct qb_ctx {
   const StepPhase* step_phases = nullptr;
   int step_nphases = 0, step_xs = 0, step_rows = 0, step_splits = 1;
   size_t step_smem = 0;
+  // tracing (qb_set_trace): launch i of the decode step records its CTAs'
+  // stamps at trace + i * kTraceMaxCtas * kTraceStamps
+  unsigned long long* trace = nullptr;
+  size_t trace_launches = 0;  // capacity of the buffer in launches
+  int trace_next = 0;         // next launch index while a step is built
+  std::string trace_labels;   // one label per traced launch, '\n'-terminated
   std::string msg;
 };
 
@@ -683,6 +689,16 @@ int validate_config(const qb_config* g, std::string* msg) {
 cudaError_t launch_step(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t* pos, void* logits,
                         cudaStream_t st);
 
+// The trace records of the next launch of the step being built (NULL when
+// tracing is off or the buffer is full), and its label.
+unsigned long long* next_trace(qb_ctx* c, const char* label, int layer) {
+  if (c->trace == nullptr || (size_t)c->trace_next >= c->trace_launches) return nullptr;
+  char buf[64];
+  std::snprintf(buf, sizeof(buf), "%s %d\n", label, layer);
+  c->trace_labels += buf;
+  return c->trace + (size_t)(c->trace_next++) * kTraceMaxCtas * kTraceStamps;
+}
+
 // One decode row through every layer. tok_in: device id; pos: device position
 // (read, then incremented by the last kernel). head=false skips the LM head
 // and lets the last down-projection increment the position (prefill rows).
@@ -705,6 +721,10 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
   const bool p2p = tp && c->p2p;
   cudaError_t e;
   ncclResult_t nr;
+  if (head) {  // a decode step: its launches are traced from index 0
+    c->trace_next = 0;
+    c->trace_labels.clear();
+  }
   // NCCL fallback: the next GEMV finishes the all-reduced sum (round + residual).
   auto peer_reduce = [&](GemvArgs& a, int sub, int parity) {
     a.tp = c->peers;
@@ -734,6 +754,7 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
       consume(a, c->xb, c->xa);
     }
     set_next_gemv(a, EPI_RESIDUAL, w.o, g.n_heads * D, H, c->sm_count);  // across the attention launch
+    if (head) a.trace = next_trace(c, "qkv", l);
     if ((e = launch_gemv<EPI_STORE>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "qkv launch");
     // 2. attention with the norm/rope/append prologue
     AttnArgs at;
@@ -760,6 +781,7 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
     at.splits = c->splits;
     at.part_splits = c->splits;
     at.tickets = c->counters + 512;
+    if (head) at.trace = next_trace(c, "attn", l);
     if ((e = launch_attn(c->tmk[l], c->tmv[l], &c->dmk[l], &c->dmv[l], at, true, st)) != cudaSuccess)
       return cuda_fail(&c->msg, e, "attention launch");
     // 3. o-proj (+ residual): xb = xa + O . attn
@@ -767,6 +789,7 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
       a = gemv_args(w.o, g.n_heads * D, H, c->attn, nullptr, c->err);
       a.out32 = c->y32;
       set_next_gemv(a, EPI_SWIGLU, w.gate_up, H, 2 * g.ffn, c->sm_count);
+      if (head) a.trace = next_trace(c, "o", l);
       if ((e = launch_gemv<EPI_PARTIAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "o launch");
       if ((nr = ncclAllReduce(c->y32, c->y32, H, ncclFloat32, ncclSum, c->comm, st)) != ncclSuccess)
         return set_err(&c->msg, QB_ERR_CUDA, std::string("ncclAllReduce: ") + ncclGetErrorString(nr));
@@ -775,6 +798,7 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
       a.residual = c->xa;
       if (p2p) peer_reduce(a, 2 * l, 0);
       set_next_gemv(a, EPI_SWIGLU, w.gate_up, H, 2 * g.ffn, c->sm_count);
+      if (head) a.trace = next_trace(c, "o", l);
       if ((e = launch_gemv<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "o launch");
     }
     // 4. RMSNorm + gate/up + SwiGLU
@@ -783,6 +807,7 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
     a.eps = g.rms_eps;
     if (tp && !p2p) consume(a, c->xa, c->xb);
     set_next_gemv(a, EPI_RESIDUAL, w.down, g.ffn, H, c->sm_count);
+    if (head) a.trace = next_trace(c, "gateup", l);
     if ((e = launch_gemv<EPI_SWIGLU>(a, c->sm_count, st)) != cudaSuccess)
       return cuda_fail(&c->msg, e, "gate/up launch");
     // 5. down (+ residual): xa = xb + Down . act
@@ -794,6 +819,7 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
       a = gemv_args(w.down, g.ffn, H, c->act, nullptr, c->err);
       a.out32 = c->y32;
       next_of_down(a);
+      if (head) a.trace = next_trace(c, "down", l);
       if ((e = launch_gemv<EPI_PARTIAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "down launch");
       if ((nr = ncclAllReduce(c->y32, c->y32, H, ncclFloat32, ncclSum, c->comm, st)) != ncclSuccess)
         return set_err(&c->msg, QB_ERR_CUDA, std::string("ncclAllReduce: ") + ncclGetErrorString(nr));
@@ -803,6 +829,7 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
       if (p2p) peer_reduce(a, 2 * l + 1, 1);
       else if (!head && l == g.n_layers - 1) a.pos_inc = pos;
       next_of_down(a);
+      if (head) a.trace = next_trace(c, "down", l);
       if ((e = launch_gemv<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess)
         return cuda_fail(&c->msg, e, "down launch");
     }
@@ -819,6 +846,7 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
       a.counter = c->counters + 64;
       a.row_base = c->tp_rank * g.vocab;
       a.pair_out = c->pairs;
+      a.trace = next_trace(c, "head", g.n_layers);
       if ((e = launch_gemv<EPI_ARGMAX>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "head launch");
       if ((nr = ncclAllGather(c->pairs, c->pairs + 2, 2, ncclFloat32, c->comm, st)) != ncclSuccess)
         return set_err(&c->msg, QB_ERR_CUDA, std::string("ncclAllGather: ") + ncclGetErrorString(nr));
@@ -844,6 +872,7 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
     a.counter = c->counters + 64;
     a.token_out = tok_out;
     a.pos_inc = pos;
+    a.trace = next_trace(c, "head", g.n_layers);
     if ((e = launch_gemv<EPI_ARGMAX>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "head launch");
   }
   return QB_OK;
@@ -1934,6 +1963,23 @@ int qb_decode_mode(const qb_ctx* c) {
   if (!c) return -1;
   return c->step_ready ? 1 : 0;
 }
+
+int qb_set_trace(qb_ctx* c, void* buffer, size_t bytes) {
+  if (!c) return set_err(nullptr, QB_ERR_ARG, "ctx is NULL");
+  if (buffer != nullptr && (reinterpret_cast<uintptr_t>(buffer) & 7) != 0)
+    return set_err(&c->msg, QB_ERR_ARG, "trace buffer must be 8-byte aligned");
+  const size_t per_launch = (size_t)kTraceMaxCtas * kTraceStamps * sizeof(unsigned long long);
+  c->trace = static_cast<unsigned long long*>(buffer);
+  c->trace_launches = buffer ? bytes / per_launch : 0;
+  c->trace_next = 0;
+  c->trace_labels.clear();
+  // A captured step keeps the trace pointers it was built with: drop it.
+  if (c->exec) { cudaGraphExecDestroy(c->exec); c->exec = nullptr; }
+  if (c->graph) { cudaGraphDestroy(c->graph); c->graph = nullptr; }
+  return QB_OK;
+}
+
+const char* qb_trace_labels(const qb_ctx* c) { return c ? c->trace_labels.c_str() : ""; }
 
 // --------------------------------------------------------------- op level
 size_t qb_op_scratch_bytes(void) { return kOpScratchBytes; }

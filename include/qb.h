@@ -182,6 +182,22 @@ int qb_check(qb_ctx* ctx, void* stream);
  * 0. Returns -1 for NULL. */
 int qb_decode_mode(const qb_ctx* ctx);
 
+/* Tracing (diagnostics; the reference's profiling is external, e.g. the timing
+ * harness of dryft/experiments): give the context a device buffer (8-byte
+ * aligned, zero-filled by the caller) and every launch of the decode steps
+ * built afterwards records, per CTA, %globaltimer stamps in ns at its start,
+ * after griddepcontrol.wait, when its first input stage landed, when its main
+ * loop ended and at its exit: launch i, CTA b, stamp k at
+ * buffer[(i * 256 + b) * 8 + k] (uint64; CTAs past 256 are not recorded,
+ * stamps a kernel does not take stay 0). Launches beyond the buffer are not
+ * traced. A captured decode graph keeps the buffer it was built with, so this
+ * call drops the context's decode graph (capture again). NULL turns tracing
+ * off. Replays overwrite the same records: the buffer holds the latest step. */
+int qb_set_trace(qb_ctx* ctx, void* buffer, size_t bytes);
+/* One label per traced launch of the last decode step built ("qkv 0", "attn 0",
+ * "o 0", "gateup 0", "down 0", ..., "head 36"), each ended by '\n'. */
+const char* qb_trace_labels(const qb_ctx* ctx);
+
 /* ---- op-level entry points (the reference's kernel wrappers) ------------- */
 
 /* Prefill projection on tcgen05 tensor cores: out = epilogue(x . w^T) for
