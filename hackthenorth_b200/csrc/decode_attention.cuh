@@ -37,13 +37,17 @@
 
 namespace qb {
 
-constexpr int kDecWarps = 8;
-constexpr int kDecThreads = (kDecWarps + 1) * 32;
+// The kernel is built for NW = 8 or 12 consumer warps; warp w owns ring slot w,
+// so the ring has NW slots and a CTA has NW stages in flight.
+constexpr int kDecWarps = 8;                         // default consumer warps (= ring slots)
+constexpr int kDecMaxWarps = 12;
+__host__ __device__ constexpr int dec_threads(int nw) { return (nw + 1) * 32; }
+constexpr int kDecThreads = dec_threads(kDecWarps);
 constexpr int kDecKeys = 32;                         // keys per stage
 constexpr int kDecSubTile = kDecKeys * 128;          // [32 keys][64 dims] bf16 = 4 KB
 constexpr int kDecStageBytes = 4 * kDecSubTile;      // K lo, K hi, V lo, V hi = 16 KB
-constexpr int kDecStages = 8;
-static_assert(kDecStages == kDecWarps, "warp w owns ring slot w");
+constexpr int kDecStages = kDecWarps;
+constexpr int kDecMergeThreads = 256;                // the in-CTA merge: dim tid & 127, rows (tid >> 7) + 2i
 constexpr int kDecRows = 8;                          // query rows per KV head (N of the mma)
 constexpr int kDecMaxCluster = 16;
 constexpr int kDecObStride = kAttnD + 4;             // padded fp32 row of the in-CTA merge
@@ -52,16 +56,17 @@ constexpr int kDecMultiClusterKeys = 8192;  // live keys from which a KV head ma
 constexpr int kDecShortSplits = 8;          // splits per KV head below that (clusters of 4: two clusters)
 constexpr int kDecMaxClusters = 8;          // clusters per KV head
 
-__host__ inline size_t dec_smem_bytes() {
-  return 1024 + (size_t)kDecStages * kDecStageBytes     // ring
+__host__ __device__ inline size_t dec_smem_bytes(int nw = kDecWarps) {
+  return 1024 + (size_t)nw * kDecStageBytes             // ring
          + kDecRows * kAttnD * 2                        // query rows
          + 2 * kAttnD * 2                               // new k, v
-         + 2 * kDecStages * 8                           // full, empty
-         + kDecWarps * kDecRows * 2 * 4                 // per-warp m, l
+         + 2 * nw * 8                                   // full, empty
+         + nw * kDecRows * 2 * 4                        // per-warp m, l
          + kDecRows * kAttnD * 4                        // receive slices [split][row][128 / S]
          + kDecMaxCluster * kDecRows * 4                // receive lse
          + 64;
 }
+static_assert(kDecMaxWarps * kDecRows * kDecObStride * 4 <= kDecWarps * kDecStageBytes, "merge buffer fits the ring");
 
 struct DecSmem {
   uint8_t* ring;
@@ -75,16 +80,16 @@ struct DecSmem {
   volatile int* flags;
 };
 
-__device__ __forceinline__ DecSmem dec_carve(uint8_t* smem_raw) {
+__device__ __forceinline__ DecSmem dec_carve(uint8_t* smem_raw, int nw) {
   DecSmem m;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   m.ring = smem;
-  m.qs = reinterpret_cast<bf16*>(m.ring + kDecStages * kDecStageBytes);
+  m.qs = reinterpret_cast<bf16*>(m.ring + nw * kDecStageBytes);
   m.kvnew = m.qs + kDecRows * kAttnD;
   m.full = reinterpret_cast<uint64_t*>(m.kvnew + 2 * kAttnD);
-  m.empty = m.full + kDecStages;
-  m.ml = reinterpret_cast<float*>(m.empty + kDecStages);
-  m.rbuf = m.ml + kDecWarps * kDecRows * 2;
+  m.empty = m.full + nw;
+  m.ml = reinterpret_cast<float*>(m.empty + nw);
+  m.rbuf = m.ml + nw * kDecRows * 2;
   m.rlse = m.rbuf + kDecRows * kAttnD;
   m.flags = reinterpret_cast<volatile int*>(m.rlse + kDecMaxCluster * kDecRows);
   return m;
@@ -101,11 +106,13 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t v) {
   return r;
 }
 
-__global__ void __launch_bounds__(kDecThreads, 1)
+template <int NW>
+__global__ void __launch_bounds__((NW + 1) * 32, 1)
     attn_decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                        const AttnArgs a) {
+  static_assert(NW >= 8 && NW <= kDecMaxWarps, "8..12 consumer warps");
   extern __shared__ uint8_t smem_raw[];
-  const DecSmem sm = dec_carve(smem_raw);
+  const DecSmem sm = dec_carve(smem_raw, NW);
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
@@ -121,7 +128,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   // First cluster phase: arrived now, waited before the first remote store.
   cluster_arrive_relaxed();
   if (tid == 0) {
-    for (int s = 0; s < kDecStages; ++s) {
+    for (int s = 0; s < NW; ++s) {
       mbar_init(&sm.full[s], 1);
       mbar_init(&sm.empty[s], 1);
     }
@@ -158,7 +165,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     return;
   }
 
-  if (warp == kDecWarps) {
+  if (warp == NW) {
     // ---------------------------------------------------------------- producer
     if (active && lane == 0) {
       prefetch_tensormap(&tmk);
@@ -166,14 +173,14 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       bool waited = false;
       int issued = 0;
       for (int c = 0; c < nst; ++c) {
-        const int s = c % kDecStages;
-        if (c >= kDecStages) {
+        const int s = c % NW;
+        if (c >= NW) {
           if (!waited) {
             pdl_wait();
             pdl_trigger();
             waited = true;
           }
-          if (!mbar_wait(&sm.empty[s], ((c / kDecStages) - 1) & 1, a.err, DEV_TIMEOUT_ATTN_EMPTY)) {
+          if (!mbar_wait(&sm.empty[s], ((c / NW) - 1) & 1, a.err, DEV_TIMEOUT_ATTN_EMPTY)) {
             ok = false;
             break;
           }
@@ -193,8 +200,8 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       }
       if (!ok) {
         // Keep shared memory alive until the copies already in flight land.
-        for (int c = (issued > kDecStages ? issued - kDecStages : 0); c < issued; ++c)
-          mbar_wait(&sm.full[c % kDecStages], (c / kDecStages) & 1, nullptr, 0);
+        for (int c = (issued > NW ? issued - NW : 0); c < issued; ++c)
+          mbar_wait(&sm.full[c % NW], (c / NW) & 1, nullptr, 0);
       }
     } else {
       pdl_wait();
@@ -208,7 +215,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     if (tid == 0) trace_stamp(trace, TRACE_WAIT);
     if (active) {
       if (tid < kDecRows * kAttnD / 8) reinterpret_cast<uint4*>(sm.qs)[tid] = make_uint4(0, 0, 0, 0);
-      named_barrier(kDecBarrierId, kDecWarps * 32);
+      named_barrier(kDecBarrierId, NW * 32);
       const bool owns_new = (k0 <= last) && (last < k1);
       const bf16* cos_row = a.cos + (size_t)last * kAttnD;
       const bf16* sin_row = a.sin + (size_t)last * kAttnD;
@@ -217,17 +224,17 @@ __global__ void __launch_bounds__(kDecThreads, 1)
                        sm.qs + warp * kAttnD, nullptr);
       if (owns_new) {
         const size_t slot = ((size_t)kvh * a.cap + last) * kAttnD;
-        if (warp == kDecWarps - 1) {
+        if (warp == NW - 1) {
           norm_rope_head(a.qkv + (size_t)a.Hq * kAttnD + kvh * kAttnD, a.k_norm, cos_row, sin_row, a.eps, lane,
                          sm.kvnew, a.k_cache + slot);
-        } else if (warp == kDecWarps - 2) {
+        } else if (warp == NW - 2) {
           const uint2 v =
               *reinterpret_cast<const uint2*>(a.qkv + (size_t)(a.Hq + a.Hkv) * kAttnD + kvh * kAttnD + 4 * lane);
           *reinterpret_cast<uint2*>(sm.kvnew + kAttnD + 4 * lane) = v;
           *reinterpret_cast<uint2*>(a.v_cache + slot + 4 * lane) = v;
         }
       }
-      named_barrier(kDecBarrierId, kDecWarps * 32);
+      named_barrier(kDecBarrierId, NW * 32);
 
       // Q^T as the B operand of every k-step: qb[ks] = dims [16ks, 16ks+16) of rows 0..7.
       uint32_t qb[8][2];
@@ -252,9 +259,9 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       const int s = warp;
       uint8_t* stage = sm.ring + s * kDecStageBytes;
 
-      for (int c = warp; c < nst; c += kDecWarps) {
+      for (int c = warp; c < nst; c += NW) {
         // Every lane waits; the verdict is made warp-uniform before the shuffles below.
-        if (!__all_sync(0xffffffffu, mbar_wait(&sm.full[s], (c / kDecStages) & 1, a.err, DEV_TIMEOUT_ATTN_FULL))) {
+        if (!__all_sync(0xffffffffu, mbar_wait(&sm.full[s], (c / NW) & 1, a.err, DEV_TIMEOUT_ATTN_FULL))) {
           ok = false;
           break;
         }
@@ -362,7 +369,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
         l[e] += __shfl_xor_sync(0xffffffffu, l[e], 16);
       }
       if (!ok && lane == 0) sm.flags[0] = 1;
-      named_barrier(kDecBarrierId, kDecWarps * 32);
+      named_barrier(kDecBarrierId, NW * 32);
       if (tid == 0) trace_stamp(trace, TRACE_LOOP);
       ok = sm.flags[0] == 0;
       if (ok) {
@@ -385,20 +392,20 @@ __global__ void __launch_bounds__(kDecThreads, 1)
             sm.ml[(warp * kDecRows + 2 * t4 + e) * 2 + 1] = l[e];
           }
         }
-        named_barrier(kDecBarrierId, kDecWarps * 32);
+        named_barrier(kDecBarrierId, NW * 32);
         const int d = tid & 127;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           const int r = (tid >> 7) + 2 * i;
           val[i] = 0.f;
           lsev[i] = -INFINITY;
-          if (r < G) {
+          if (r < G && tid < kDecMergeThreads) {
             float M = -INFINITY;
 #pragma unroll
-            for (int w = 0; w < kDecWarps; ++w) M = fmaxf(M, sm.ml[(w * kDecRows + r) * 2]);
+            for (int w = 0; w < NW; ++w) M = fmaxf(M, sm.ml[(w * kDecRows + r) * 2]);
             float L = 0.f, acc = 0.f;
 #pragma unroll
-            for (int w = 0; w < kDecWarps; ++w) {
+            for (int w = 0; w < NW; ++w) {
               const float mw = sm.ml[(w * kDecRows + r) * 2];
               const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
               L += sm.ml[(w * kDecRows + r) * 2 + 1] * f;
@@ -415,7 +422,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
   // ------------------------------------------------------------ cluster merge
   cluster_wait();  // every CTA of the cluster is running
   if (Se == 1 && Cact == 1) {  // uniform: the single split is the answer
-    if (warp < kDecWarps && split == 0 && active && ok) {
+    if (tid < kDecMergeThreads && split == 0 && active && ok) {
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int r = (tid >> 7) + 2 * i;
@@ -426,7 +433,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     return;
   }
   const int W = kAttnD / S;
-  if (warp < kDecWarps && active && ok) {
+  if (tid < kDecMergeThreads && active && ok) {
     const int d = tid & 127;
     const int owner = d / W;
     const uint32_t rb = map_shared_rank(sm.rbuf, owner);

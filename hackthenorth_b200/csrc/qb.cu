@@ -330,6 +330,19 @@ cudaError_t launch_attn_t(const CUtensorMap& tk, const CUtensorMap& tv, const At
 // long-context choice.
 constexpr int kDecSizes[3] = {16, 8, 4};
 
+// Consumer warps of the decode attention kernel (= ring slots = stages in
+// flight per CTA): 8, or 12 with QB_DEC_WARPS=12.
+int dec_warps() {
+  static int v = 0;
+  if (v == 0) {
+    const char* e = std::getenv("QB_DEC_WARPS");
+    v = (e && std::strtol(e, nullptr, 10) == 12) ? 12 : 8;
+  }
+  return v;
+}
+typedef void (*DecKernelFn)(const CUtensorMap, const CUtensorMap, const AttnArgs);
+DecKernelFn dec_kernel() { return dec_warps() == 12 ? attn_decode_kernel<12> : attn_decode_kernel<8>; }
+
 int decode_cluster_size(int hkv, int rows) {
   DeviceCache& dc = dev_cache();
   std::lock_guard<std::mutex> lock(g_dev_cache_mu);
@@ -340,16 +353,15 @@ int decode_cluster_size(int hkv, int rows) {
   const char* e = std::getenv("QB_ATTN_CLUSTER");
   if (e && e[0] == '0') return 0;
   if (rows > kDecRows) return 0;
-  const size_t smem = dec_smem_bytes();
-  if (cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-      cudaSuccess)
+  const size_t smem = dec_smem_bytes(dec_warps());
+  if (cudaFuncSetAttribute(dec_kernel(), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
     return 0;
-  cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  cudaFuncSetAttribute(dec_kernel(), cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
   for (int i = 0; i < 3; ++i) {
     const int cs = kDecSizes[i];
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(hkv * cs);
-    cfg.blockDim = dim3(kDecThreads);
+    cfg.blockDim = dim3(dec_threads(dec_warps()));
     cfg.dynamicSmemBytes = smem;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -359,7 +371,7 @@ int decode_cluster_size(int hkv, int rows) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, attn_decode_kernel, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&n, dec_kernel(), &cfg) != cudaSuccess) {
       cudaGetLastError();
       n = 0;
     }
@@ -398,8 +410,8 @@ cudaError_t launch_attn_decode(const CUtensorMap& tk, const CUtensorMap& tv, Att
   cs = a.splits;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.Hkv * a.clusters * cs);
-  cfg.blockDim = dim3(kDecThreads);
-  cfg.dynamicSmemBytes = dec_smem_bytes();
+  cfg.blockDim = dim3(dec_threads(dec_warps()));
+  cfg.dynamicSmemBytes = dec_smem_bytes(dec_warps());
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -410,7 +422,7 @@ cudaError_t launch_attn_decode(const CUtensorMap& tk, const CUtensorMap& tv, Att
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, attn_decode_kernel, tk, tv, a);
+  return cudaLaunchKernelEx(&cfg, dec_kernel(), tk, tv, a);
 }
 
 // Verify-pass attention (attn_rows_kernel, R = G * Q <= 24 rows) as one

@@ -29,18 +29,19 @@ namespace qb {
 constexpr int kVaWarps = 8;
 constexpr int kVaThreads = kVaWarps * 32;
 constexpr int kVaMaxRows = 24;
+constexpr int kVaStages = 8;  // ring slots: warp w owns slot w
 constexpr int kVaBarrierId = 4;
 
 __host__ inline size_t va_smem_bytes() {
-  return 1024 + (size_t)kDecStages * kDecStageBytes          // ring (also the in-CTA merge buffer)
+  return 1024 + (size_t)kVaStages * kDecStageBytes          // ring (also the in-CTA merge buffer)
          + kVaMaxRows * kAttnD * 2                           // query rows
-         + kDecStages * 8                                    // full barriers
+         + kVaStages * 8                                    // full barriers
          + kVaWarps * kVaMaxRows * 2 * 4                     // per-warp m, l
          + kVaMaxRows * kAttnD * 4                           // receive slices [split][row][128 / S]
          + kDecMaxCluster * kVaMaxRows * 4                   // receive lse
          + 64;
 }
-static_assert(kVaWarps * kVaMaxRows * kDecObStride * 4 <= kDecStages * kDecStageBytes, "merge buffer fits the ring");
+static_assert(kVaWarps * kVaMaxRows * kDecObStride * 4 <= kVaStages * kDecStageBytes, "merge buffer fits the ring");
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -53,9 +54,9 @@ __global__ void __launch_bounds__(kVaThreads, 1)
   constexpr int ROWS = NT * 8;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  bf16* qs = reinterpret_cast<bf16*>(ring + kDecStages * kDecStageBytes);  // [ROWS][128]
+  bf16* qs = reinterpret_cast<bf16*>(ring + kVaStages * kDecStageBytes);  // [ROWS][128]
   uint64_t* full = reinterpret_cast<uint64_t*>(qs + kVaMaxRows * kAttnD);
-  float* ml = reinterpret_cast<float*>(full + kDecStages);  // [warp][row][2]
+  float* ml = reinterpret_cast<float*>(full + kVaStages);  // [warp][row][2]
   float* rbuf = ml + kVaWarps * kVaMaxRows * 2;             // [split][row][W]
   float* rlse = rbuf + kVaMaxRows * kAttnD;                 // [split][row]
   volatile int* flags = reinterpret_cast<volatile int*>(rlse + kDecMaxCluster * kVaMaxRows);
@@ -74,7 +75,7 @@ __global__ void __launch_bounds__(kVaThreads, 1)
 
   cluster_arrive_relaxed();  // first cluster phase, waited before the first remote store
   if (tid == 0) {
-    for (int s = 0; s < kDecStages; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < kVaStages; ++s) mbar_init(&full[s], 1);
     fence_mbar_init();
     flags[0] = 0;
   }
@@ -110,7 +111,7 @@ __global__ void __launch_bounds__(kVaThreads, 1)
   const bool active = split < Se && nst > 0;
 
   auto issue = [&](int c) {  // lane 0 of warp c % 8: stage c into slot c % 8
-    const int s = c % kDecStages;
+    const int s = c % kVaStages;
     uint8_t* st = ring + s * kDecStageBytes;
     const int y = kvh * a.cap + k0 + c * kDecKeys;
     mbar_arrive_expect_tx(&full[s], kDecStageBytes);
@@ -164,7 +165,7 @@ __global__ void __launch_bounds__(kVaThreads, 1)
     const int s = warp;
     uint8_t* stage = ring + s * kDecStageBytes;
     for (int c = warp; c < nst; c += kVaWarps) {
-      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (c / kDecStages) & 1, a.err, DEV_TIMEOUT_ATTN_FULL))) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], (c / kVaStages) & 1, a.err, DEV_TIMEOUT_ATTN_FULL))) {
         ok = false;
         break;
       }
@@ -264,15 +265,15 @@ __global__ void __launch_bounds__(kVaThreads, 1)
           }
       }
       __syncwarp();
-      if (lane == 0 && c + kDecStages < nst) {
+      if (lane == 0 && c + kVaStages < nst) {
         fence_proxy_async_smem();  // this warp's reads of the slot precede the refill
-        issue(c + kDecStages);
+        issue(c + kVaStages);
       }
     }
     if (!ok) {
       // Let the copies this warp issued land before shared memory goes away.
       if (lane == 0)
-        for (int c = warp; c < nst; c += kVaWarps) mbar_wait(&full[s], (c / kDecStages) & 1, nullptr, 0);
+        for (int c = warp; c < nst; c += kVaWarps) mbar_wait(&full[s], (c / kVaStages) & 1, nullptr, 0);
       flags[0] = 1;
     }
 #pragma unroll
