@@ -122,8 +122,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
   const int cl = (blockIdx.x / S) % C;
   const int split = blockIdx.x % S;  // == cluster rank
   const int G = a.Hq / a.Hkv;        // query rows, <= kDecRows
-  unsigned long long* const trace = trace_slot(a.trace);
-  if (tid == 0) trace_stamp(trace, TRACE_ENTRY);
+  if (tid == 0) trace_stamp(trace_slot(a.trace), TRACE_ENTRY);
 
   // First cluster phase: arrived now, waited before the first remote store.
   cluster_arrive_relaxed();
@@ -212,7 +211,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
     // --------------------------------------------------------------- consumers
     pdl_wait();
     pdl_trigger();
-    if (tid == 0) trace_stamp(trace, TRACE_WAIT);
+    if (tid == 0) trace_stamp(trace_slot(a.trace), TRACE_WAIT);
     if (active) {
       if (tid < kDecRows * kAttnD / 8) reinterpret_cast<uint4*>(sm.qs)[tid] = make_uint4(0, 0, 0, 0);
       named_barrier(kDecBarrierId, NW * 32);
@@ -265,7 +264,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
           ok = false;
           break;
         }
-        if (c == 0 && lane == 0) trace_stamp(trace, TRACE_FIRST);
+        if (c == 0 && lane == 0) trace_stamp(trace_slot(a.trace), TRACE_FIRST);
         const int kstage = k0 + c * kDecKeys;
         if (owns_new && kstage <= last && last < kstage + kDecKeys) {
           const int kr = (int)last - kstage;
@@ -370,7 +369,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
       }
       if (!ok && lane == 0) sm.flags[0] = 1;
       named_barrier(kDecBarrierId, NW * 32);
-      if (tid == 0) trace_stamp(trace, TRACE_LOOP);
+      if (tid == 0) trace_stamp(trace_slot(a.trace), TRACE_LOOP);
       ok = sm.flags[0] == 0;
       if (ok) {
         // Merge the 8 warps (fixed order) through the drained ring.
@@ -429,7 +428,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
         if (r < G) attn_store_out(a, kvh, r, tid & 127, val[i]);
       }
     }
-    if (tid == 0) trace_stamp(trace, TRACE_EXIT);
+    if (tid == 0) trace_stamp(trace_slot(a.trace), TRACE_EXIT);
     return;
   }
   const int W = kAttnD / S;
@@ -465,7 +464,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
     clse = mx + log2f(den);
     if (Cact == 1) attn_store_out(a, kvh, r, split * W + off, cval);
   }
-  if (tid == 0 && Cact == 1) trace_stamp(trace, TRACE_EXIT);
+  if (tid == 0 && Cact == 1) trace_stamp(trace_slot(a.trace), TRACE_EXIT);
   if (Cact == 1) return;
   // Several clusters per head: each CTA publishes its slice of the cluster's
   // result (normalised rows + log-sum-exp) and the CTA of the same slice
@@ -483,7 +482,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
     sm.flags[1] = (t == (unsigned)(Cact - 1)) ? 1 : 0;
   }
   __syncthreads();
-  if (tid == 0) trace_stamp(trace, TRACE_EXIT);  // the merging CTA overwrites it below
+  if (tid == 0) trace_stamp(trace_slot(a.trace), TRACE_EXIT);  // the merging CTA overwrites it below
   if (sm.flags[1] == 0) return;
   if (tid < G * W) {
     const int r = tid / W, off = tid % W;
@@ -498,7 +497,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
     attn_store_out(a, kvh, r, split * W + off, acc / den);
   }
   if (tid == 0) a.tickets[kvh * S + split] = 0u;
-  if (tid == 0) trace_stamp(trace, TRACE_EXIT);
+  if (tid == 0) trace_stamp(trace_slot(a.trace), TRACE_EXIT);
 }
 
 }  // namespace qb

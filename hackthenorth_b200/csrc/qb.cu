@@ -87,7 +87,7 @@ int current_sm_count() {
 // again): correct, only slower.
 constexpr int kMaxDevices = 64;
 struct DeviceCache {
-  bool gemv_attr[5] = {};
+  bool gemv_attr[5][1] = {};
   bool pg_attr[3] = {};
   bool attn_attr[2][2] = {};  // [MT - 1][PRO]
   bool rows_attr[5] = {};
@@ -138,9 +138,20 @@ cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sm
 
 // ---------------------------------------------------------------- GEMV launch
 struct GemvPlan {
-  int grid, stages, max_rows, kc;
+  int grid, stages, max_rows, kc, cw;
   size_t smem;
 };
+
+// Small GEMVs on kGemvSmallWarps consumer warps with the CTA's whole share in
+// flight (gemv.cuh); QB_GEMV_SMALL=0 keeps every GEMV on 16 warps.
+bool small_gemv_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("QB_GEMV_SMALL");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
 
 int gemv_kc_pref() {
   static int v = 0;
@@ -168,6 +179,21 @@ bool plan_gemv(int epi, int K, int rows, int sm_count, GemvPlan* p) {
   if (units <= 0) return false;
   p->grid = units < sm_count ? units : sm_count;
   p->max_rows = ((units + p->grid - 1) / p->grid) * rpu;
+  if (small_gemv_enabled()) {
+    // One row piece per stage up to K = 4096 columns, every stage of the CTA in flight.
+    const int cw = kGemvSmallWarps;
+    const int kc = K <= 4096 ? K : 2048;
+    const int stages = ((p->max_rows + cw - 1) / cw) * ((K + kc - 1) / kc);
+    const size_t smem = gemv_smem_bytes(K, stages, p->max_rows, kc, cw);
+    if ((size_t)stages * gemv_stage_bytes(kc, cw) <= kGemvSmallRingBytes && smem <= kGemvSmallSmemMax) {
+      p->cw = cw;
+      p->kc = kc;
+      p->stages = stages;
+      p->smem = smem;
+      return true;
+    }
+  }
+  p->cw = kGemvConsumerWarps;
   const size_t fixed = gemv_smem_bytes(K, 0, p->max_rows, 1024);
   // Wider pieces when K allows and the ring still holds >= 3 of them.
   int kc = (K >= 2048 && gemv_kc_pref() == 2048) ? 2048 : 1024;
@@ -184,18 +210,25 @@ bool plan_gemv(int epi, int K, int rows, int sm_count, GemvPlan* p) {
 
 template <int EPI>
 cudaError_t launch_gemv(GemvArgs a, int sm_count, cudaStream_t st) {
-  bool& attr_done = dev_cache().gemv_attr[EPI];
-  if (!attr_done) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  bool* attr_done = dev_cache().gemv_attr[EPI];
+  if (!attr_done[0]) {
+    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<EPI, kGemvConsumerWarps>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return e;
-    attr_done = true;
+    e = cudaFuncSetAttribute(gemv_kernel<EPI, kGemvSmallWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)kGemvSmallSmemMax);
+    if (e != cudaSuccess) return e;
+    attr_done[0] = true;
   }
   GemvPlan p;
   if (!plan_gemv(EPI, a.K, a.rows, sm_count, &p)) return cudaErrorInvalidValue;
   a.stages = p.stages;
   a.max_rows = p.max_rows;
   a.kc = p.kc;
-  return launch_ex(gemv_kernel<EPI>, dim3(p.grid), dim3(kGemvThreads), p.smem, st, a);
+  if (p.cw == kGemvSmallWarps)
+    return launch_ex(gemv_kernel<EPI, kGemvSmallWarps>, dim3(p.grid), dim3(gemv_threads(kGemvSmallWarps)), p.smem,
+                     st, a);
+  return launch_ex(gemv_kernel<EPI, kGemvConsumerWarps>, dim3(p.grid), dim3(kGemvThreads), p.smem, st, a);
 }
 
 // The GEMV launched after `a` in the step (its weights, shape and epilogue):
@@ -210,6 +243,7 @@ void set_next_gemv(GemvArgs& a, int epi, const void* w, int K, int rows, int sm_
   a.nx_rpu = gemv_rows_per_unit(epi);
   a.nx_kc = p.kc;
   a.nx_grid = p.grid;
+  a.nx_cw = p.cw;
 }
 
 GemvArgs gemv_args(const void* w, int K, int rows, const void* x, void* out, int* err) {
