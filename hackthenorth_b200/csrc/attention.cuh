@@ -81,6 +81,8 @@ struct AttnArgs {
                          // launch belongs to sequence h / batch_hkv, whose position is pos[h / batch_hkv]);
                          // 0: one sequence, pos[i] is query i's position
   unsigned long long* trace;  // decode cluster kernel: this launch's trace records (common.cuh), or NULL
+  int multi_keys;             // decode cluster kernel: live keys from which a KV head uses all its
+                              // clusters (0: kDecMultiClusterKeys)
 };
 
 __host__ inline size_t attn_smem_bytes(int mt) {

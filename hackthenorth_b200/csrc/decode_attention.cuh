@@ -37,12 +37,8 @@
 
 namespace qb {
 
-// The kernel is built for NW = 8 or 12 consumer warps; warp w owns ring slot w,
-// so the ring has NW slots and a CTA has NW stages in flight.
-constexpr int kDecWarps = 8;                         // default consumer warps (= ring slots)
-constexpr int kDecMaxWarps = 12;
-__host__ __device__ constexpr int dec_threads(int nw) { return (nw + 1) * 32; }
-constexpr int kDecThreads = dec_threads(kDecWarps);
+constexpr int kDecWarps = 8;                         // consumer warps; warp w owns ring slot w
+constexpr int kDecThreads = (kDecWarps + 1) * 32;
 constexpr int kDecKeys = 32;                         // keys per stage
 constexpr int kDecSubTile = kDecKeys * 128;          // [32 keys][64 dims] bf16 = 4 KB
 constexpr int kDecStageBytes = 4 * kDecSubTile;      // K lo, K hi, V lo, V hi = 16 KB
@@ -56,7 +52,7 @@ constexpr int kDecMultiClusterKeys = 8192;  // live keys from which a KV head ma
 constexpr int kDecShortSplits = 8;          // splits per KV head below that (clusters of 4: two clusters)
 constexpr int kDecMaxClusters = 8;          // clusters per KV head
 
-__host__ __device__ inline size_t dec_smem_bytes(int nw = kDecWarps) {
+__host__ __device__ inline size_t dec_smem_bytes(int nw = kDecStages) {
   return 1024 + (size_t)nw * kDecStageBytes             // ring
          + kDecRows * kAttnD * 2                        // query rows
          + 2 * kAttnD * 2                               // new k, v
@@ -66,7 +62,7 @@ __host__ __device__ inline size_t dec_smem_bytes(int nw = kDecWarps) {
          + kDecMaxCluster * kDecRows * 4                // receive lse
          + 64;
 }
-static_assert(kDecMaxWarps * kDecRows * kDecObStride * 4 <= kDecWarps * kDecStageBytes, "merge buffer fits the ring");
+static_assert(kDecWarps * kDecRows * kDecObStride * 4 <= kDecStages * kDecStageBytes, "merge buffer fits the ring");
 
 struct DecSmem {
   uint8_t* ring;
@@ -106,11 +102,11 @@ __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t v) {
   return r;
 }
 
-template <int NW>
-__global__ void __launch_bounds__((NW + 1) * 32, 1)
+template <bool TRACE = false>
+__global__ void __launch_bounds__(kDecThreads, 1)
     attn_decode_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
                        const AttnArgs a) {
-  static_assert(NW >= 8 && NW <= kDecMaxWarps, "8..12 consumer warps");
+  constexpr int NW = kDecWarps;  // consumer warps = ring slots
   extern __shared__ uint8_t smem_raw[];
   const DecSmem sm = dec_carve(smem_raw, NW);
   const int tid = threadIdx.x;
@@ -122,7 +118,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
   const int cl = (blockIdx.x / S) % C;
   const int split = blockIdx.x % S;  // == cluster rank
   const int G = a.Hq / a.Hkv;        // query rows, <= kDecRows
-  if (tid == 0) trace_stamp(trace_slot(a.trace), TRACE_ENTRY);
+  if (TRACE && tid == 0) trace_stamp(trace_slot(a.trace), TRACE_ENTRY);
 
   // First cluster phase: arrived now, waited before the first remote store.
   cluster_arrive_relaxed();
@@ -147,7 +143,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
   // Splits over the whole head: about kAttnMinSplitKeys keys each, at most
   // kDecShortSplits (at least one cluster's worth) below kDecMultiClusterKeys
   // live keys, up to C clusters' worth above. Cluster cl takes global splits [cl*S, cl*S+S).
-  const int cmax = n >= kDecMultiClusterKeys ? C : min(C, max(1, kDecShortSplits / S));
+  const int mk = a.multi_keys > 0 ? a.multi_keys : kDecMultiClusterKeys;
+  const int cmax = n >= mk ? C : min(C, max(1, kDecShortSplits / S));
   const int2 sl = attn_split_len(n, min(cmax * S, (n + kAttnMinSplitKeys - 1) / kAttnMinSplitKeys));
   const int per = sl.x, SeT = sl.y;            // every split below SeT has keys
   const int Cact = (SeT + S - 1) / S;           // clusters with work (uniform over the grid)
@@ -211,7 +208,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
     // --------------------------------------------------------------- consumers
     pdl_wait();
     pdl_trigger();
-    if (tid == 0) trace_stamp(trace_slot(a.trace), TRACE_WAIT);
+    if (TRACE && tid == 0) trace_stamp(trace_slot(a.trace), TRACE_WAIT);
     if (active) {
       if (tid < kDecRows * kAttnD / 8) reinterpret_cast<uint4*>(sm.qs)[tid] = make_uint4(0, 0, 0, 0);
       named_barrier(kDecBarrierId, NW * 32);
@@ -264,7 +261,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
           ok = false;
           break;
         }
-        if (c == 0 && lane == 0) trace_stamp(trace_slot(a.trace), TRACE_FIRST);
+        if (TRACE && c == 0 && lane == 0) trace_stamp(trace_slot(a.trace), TRACE_FIRST);
         const int kstage = k0 + c * kDecKeys;
         if (owns_new && kstage <= last && last < kstage + kDecKeys) {
           const int kr = (int)last - kstage;
@@ -369,7 +366,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
       }
       if (!ok && lane == 0) sm.flags[0] = 1;
       named_barrier(kDecBarrierId, NW * 32);
-      if (tid == 0) trace_stamp(trace_slot(a.trace), TRACE_LOOP);
+      if (TRACE && tid == 0) trace_stamp(trace_slot(a.trace), TRACE_LOOP);
       ok = sm.flags[0] == 0;
       if (ok) {
         // Merge the 8 warps (fixed order) through the drained ring.
@@ -428,7 +425,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
         if (r < G) attn_store_out(a, kvh, r, tid & 127, val[i]);
       }
     }
-    if (tid == 0) trace_stamp(trace_slot(a.trace), TRACE_EXIT);
+    if (TRACE && tid == 0) trace_stamp(trace_slot(a.trace), TRACE_EXIT);
     return;
   }
   const int W = kAttnD / S;
@@ -464,7 +461,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
     clse = mx + log2f(den);
     if (Cact == 1) attn_store_out(a, kvh, r, split * W + off, cval);
   }
-  if (tid == 0 && Cact == 1) trace_stamp(trace_slot(a.trace), TRACE_EXIT);
+  if (TRACE && tid == 0 && Cact == 1) trace_stamp(trace_slot(a.trace), TRACE_EXIT);
   if (Cact == 1) return;
   // Several clusters per head: each CTA publishes its slice of the cluster's
   // result (normalised rows + log-sum-exp) and the CTA of the same slice
@@ -482,7 +479,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
     sm.flags[1] = (t == (unsigned)(Cact - 1)) ? 1 : 0;
   }
   __syncthreads();
-  if (tid == 0) trace_stamp(trace_slot(a.trace), TRACE_EXIT);  // the merging CTA overwrites it below
+  if (TRACE && tid == 0) trace_stamp(trace_slot(a.trace), TRACE_EXIT);  // the merging CTA overwrites it below
   if (sm.flags[1] == 0) return;
   if (tid < G * W) {
     const int r = tid / W, off = tid % W;
@@ -497,7 +494,7 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1)
     attn_store_out(a, kvh, r, split * W + off, acc / den);
   }
   if (tid == 0) a.tickets[kvh * S + split] = 0u;
-  if (tid == 0) trace_stamp(trace_slot(a.trace), TRACE_EXIT);
+  if (TRACE && tid == 0) trace_stamp(trace_slot(a.trace), TRACE_EXIT);
 }
 
 }  // namespace qb

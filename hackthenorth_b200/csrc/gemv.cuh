@@ -27,19 +27,10 @@ namespace qb {
 constexpr int kGemvConsumerWarps = 16;
 constexpr int kGemvConsumers = kGemvConsumerWarps * 32;
 constexpr int kGemvThreads = kGemvConsumers + 32;
-// Small GEMVs (a CTA's whole share of the weights fits a ring of at most
-// kGemvSmallRingBytes) run with 8 consumer warps and a ring sized to that share:
-// two such CTAs, of consecutive kernels, fit one SM (registers and shared
-// memory), so under programmatic dependent launch the next kernel's CTAs are
-// resident early and bring in all their weights while this one finishes.
-constexpr int kGemvSmallWarps = 8;
-constexpr size_t kGemvSmallRingBytes = 96 * 1024;
-constexpr size_t kGemvSmallSmemMax = 112 * 1024;
-__host__ __device__ constexpr int gemv_threads(int cw) { return (cw + 1) * 32; }
-// A stage holds the same kc-column piece (kc = 1024 or 2048) of cw rows (16,
-// or 8 for small GEMVs): cw one-dimensional bulk copies of 2 or 4 KB, one per
-// row, issued by cw producer lanes in parallel.
-__host__ __device__ inline int gemv_stage_bytes(int kc, int cw = kGemvConsumerWarps) { return cw * kc * 2; }
+// A stage holds the same kc-column piece (kc = 1024 or 2048) of 16 rows:
+// 16 one-dimensional bulk copies of 2 or 4 KB, one per row, issued by 16
+// producer lanes in parallel.
+__host__ __device__ inline int gemv_stage_bytes(int kc) { return kGemvConsumerWarps * kc * 2; }
 constexpr int kGemvBarrierId = 1;  // named barrier of the consumer threads
 constexpr int kGemvL2Ahead = 2;    // stages of the next GEMV brought into L2 by each CTA
 
@@ -105,14 +96,14 @@ struct GemvArgs {
   // L2 for the first stages of the rows the same CTA index streams next, so
   // they come from L2 across the kernel boundary. NULL: nothing to prefetch.
   const bf16* nx_w;
-  int nx_K, nx_rows, nx_rpu, nx_kc, nx_grid, nx_cw;
+  int nx_K, nx_rows, nx_rpu, nx_kc, nx_grid;
   unsigned long long* trace;  // this launch's trace records (see common.cuh), or NULL
 };
 
 __host__ __device__ inline int gemv_rows_per_unit(int epi) { return epi == EPI_SWIGLU ? 2 : 1; }
 
-__host__ inline size_t gemv_smem_bytes(int K, int stages, int max_rows, int kc, int cw = kGemvConsumerWarps) {
-  return (size_t)stages * gemv_stage_bytes(kc, cw) + (size_t)K * 2 + (((size_t)max_rows * 4 + 15) & ~size_t(15)) +
+__host__ inline size_t gemv_smem_bytes(int K, int stages, int max_rows, int kc) {
+  return (size_t)stages * gemv_stage_bytes(kc) + (size_t)K * 2 + (((size_t)max_rows * 4 + 15) & ~size_t(15)) +
          (size_t)2 * stages * 8 + 128 * 4;
 }
 
@@ -137,9 +128,8 @@ __device__ __forceinline__ float dot8_bf16(const uint4 w, const uint4 x, float a
   return acc;
 }
 
-template <int EPI, int CW = kGemvConsumerWarps>
-__global__ void __launch_bounds__((CW + 1) * 32, CW == kGemvSmallWarps ? 2 : 1) gemv_kernel(const GemvArgs a) {
-  constexpr int kCons = CW * 32;  // consumer threads
+template <int EPI, bool TRACE = false>
+__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -156,9 +146,9 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW == kGemvSmallWarps ? 2 : 1) 
   const int r0 = u0 * rpu;
   const int nrows = (u1 - u0) * rpu;
   const int KC = a.kc;
-  const int stage_bytes = gemv_stage_bytes(KC, CW);
+  const int stage_bytes = gemv_stage_bytes(KC);
   const int nkc = (K + KC - 1) / KC;
-  const int nblk = (nrows + CW - 1) / CW;
+  const int nblk = (nrows + kGemvConsumerWarps - 1) / kGemvConsumerWarps;
   const int nstage = nblk * nkc;
 
   uint8_t* ring = smem;
@@ -167,19 +157,19 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW == kGemvSmallWarps ? 2 : 1) 
   uint64_t* full = reinterpret_cast<uint64_t*>(rowsum + ((a.max_rows + 3) & ~3));
   uint64_t* empty = full + stages;
   float* misc = reinterpret_cast<float*>(empty + stages);
-  if (tid == 0) trace_stamp(trace_slot(a.trace), TRACE_ENTRY);
+  if (TRACE && tid == 0) trace_stamp(trace_slot(a.trace), TRACE_ENTRY);
 
   if (tid == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], CW);
+      mbar_init(&empty[s], kGemvConsumerWarps);
     }
     fence_mbar_init();
     reinterpret_cast<int*>(misc)[100] = 0;  // CTA-wide abort flag
   }
   __syncthreads();
 
-  if (warp == CW) {
+  if (warp == kGemvConsumerWarps) {
     // ---------------- producer warp ----------------
     // Lane r copies row r of each 16-row block; lane 0 also drives the ring.
     const uint64_t policy = policy_evict_first();
@@ -203,14 +193,14 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW == kGemvSmallWarps ? 2 : 1) 
         }
       }
       const int blk = c / nkc, kc = c - blk * nkc;
-      const int nr = min(CW, nrows - blk * CW);
+      const int nr = min(kGemvConsumerWarps, nrows - blk * kGemvConsumerWarps);
       const int c0 = kc * KC;
       const uint32_t piece = (uint32_t)min(KC, K - c0) * 2;
       if (lane == 0) mbar_arrive_expect_tx(&full[s], piece * nr);
       __syncwarp();
       if (lane < nr)
         bulk_g2s(ring + (size_t)s * stage_bytes + lane * (KC * 2),
-                 a.w + (size_t)(r0 + blk * CW + lane) * K + c0, piece, &full[s], policy);
+                 a.w + (size_t)(r0 + blk * kGemvConsumerWarps + lane) * K + c0, piece, &full[s], policy);
       issued = c + 1;
     }
     if (ok && a.nx_w != nullptr && b < a.nx_grid) {
@@ -223,8 +213,8 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW == kGemvSmallWarps ? 2 : 1) 
       const int nkc_n = (a.nx_K + a.nx_kc - 1) / a.nx_kc;
       for (int c = 0; c < kGemvL2Ahead; ++c) {
         const int blk = c / nkc_n, kc = c - blk * nkc_n;
-        const int row = blk * a.nx_cw + lane;
-        if (lane < a.nx_cw && row < nrows_n) {
+        const int row = blk * kGemvConsumerWarps + lane;
+        if (lane < kGemvConsumerWarps && row < nrows_n) {
           const int c0 = kc * a.nx_kc;
           const uint32_t bytes = (uint32_t)min(a.nx_kc, a.nx_K - c0) * 2;
           asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a.nx_w + (size_t)(nr0 + row) * a.nx_K + c0),
@@ -246,10 +236,10 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW == kGemvSmallWarps ? 2 : 1) 
   }
 
   // ---------------- consumer warps ----------------
-  const int ctid = tid;  // 0..kCons-1
+  const int ctid = tid;  // 0..kGemvConsumers-1
   pdl_wait();
   pdl_trigger();
-  if (ctid == 0) trace_stamp(trace_slot(a.trace), TRACE_WAIT);
+  if (TRACE && ctid == 0) trace_stamp(trace_slot(a.trace), TRACE_WAIT);
 
   // 1. Input row (optionally the embedding gather) and its RMSNorm, to fp32 smem.
   const bf16* xsrc = a.x;
@@ -263,7 +253,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW == kGemvSmallWarps ? 2 : 1) 
   }
   const float* x32 = a.x32;
   float ss = 0.f;
-  for (int i = ctid * 8; i < K; i += kCons * 8) {
+  for (int i = ctid * 8; i < K; i += kGemvConsumers * 8) {
     uint4 v;
     if (x32 != nullptr) {
       // Residual add after the cross-rank reduction: the projection is
@@ -292,13 +282,13 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW == kGemvSmallWarps ? 2 : 1) 
   if (a.gain != nullptr) {
     ss = warp_sum(ss);
     if (lane == 0) misc[warp] = ss;
-    named_barrier(kGemvBarrierId, kCons);
+    named_barrier(kGemvBarrierId, kGemvConsumers);
     float tot = 0.f;
 #pragma unroll
-    for (int w = 0; w < CW; ++w) tot += misc[w];
+    for (int w = 0; w < kGemvConsumerWarps; ++w) tot += misc[w];
     // rsqrt(mean(x^2) + eps) as 1/sqrt: correctly rounded sqrt and division.
     const float inv = 1.0f / sqrtf(tot / (float)K + a.eps);
-    for (int i = ctid * 8; i < K; i += kCons * 8) {
+    for (int i = ctid * 8; i < K; i += kGemvConsumers * 8) {
       uint4 v = *reinterpret_cast<const uint4*>(xs + i);
       const uint4 g = ldg128_nc(a.gain + i);
       uint32_t* pv = reinterpret_cast<uint32_t*>(&v);
@@ -312,14 +302,14 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW == kGemvSmallWarps ? 2 : 1) 
       *reinterpret_cast<uint4*>(xs + i) = v;
     }
   }
-  named_barrier(kGemvBarrierId, kCons);
+  named_barrier(kGemvBarrierId, kGemvConsumers);
 
   // 2. Stream the weights: warp w owns row w of every 16-row block.
   float rowacc = 0.f;
   bool ok = true;
   int c = 0;
   for (int blk = 0; blk < nblk && ok; ++blk) {
-    const int row = blk * CW + warp;
+    const int row = blk * kGemvConsumerWarps + warp;
     const bool active = row < nrows;
     for (int kc = 0; kc < nkc; ++kc, ++c) {
       const int s = c % stages;
@@ -327,7 +317,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW == kGemvSmallWarps ? 2 : 1) 
         ok = false;
         break;
       }
-      if (c == 0 && ctid == 0) trace_stamp(trace_slot(a.trace), TRACE_FIRST);
+      if (TRACE && c == 0 && ctid == 0) trace_stamp(trace_slot(a.trace), TRACE_FIRST);
       if (active) {
         const int c0 = kc * KC;
         const uint8_t* piece = ring + (size_t)s * stage_bytes + warp * (KC * 2) + lane * 16;
@@ -363,15 +353,15 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW == kGemvSmallWarps ? 2 : 1) 
     }
   }
   if (!ok && lane == 0) reinterpret_cast<volatile int*>(misc)[100] = 1;
-  named_barrier(kGemvBarrierId, kCons);
+  named_barrier(kGemvBarrierId, kGemvConsumers);
   if (reinterpret_cast<volatile int*>(misc)[100] != 0) return;  // uniform across the CTA
-  if (ctid == 0) trace_stamp(trace_slot(a.trace), TRACE_LOOP);
+  if (TRACE && ctid == 0) trace_stamp(trace_slot(a.trace), TRACE_LOOP);
 
   // 3. Epilogue.
   if constexpr (EPI == EPI_STORE) {
-    for (int r = ctid; r < nrows; r += kCons) a.out[r0 + r] = __float2bfloat16_rn(rowsum[r]);
+    for (int r = ctid; r < nrows; r += kGemvConsumers) a.out[r0 + r] = __float2bfloat16_rn(rowsum[r]);
   } else if constexpr (EPI == EPI_PARTIAL) {
-    for (int r = ctid; r < nrows; r += kCons) a.out32[r0 + r] = rowsum[r];
+    for (int r = ctid; r < nrows; r += kGemvConsumers) a.out32[r0 + r] = rowsum[r];
   } else if constexpr (EPI == EPI_RESIDUAL) {
     if (a.tp.size > 1) {
       // Tensor parallel: every rank partitions the rows across CTAs the same
@@ -383,10 +373,10 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW == kGemvSmallWarps ? 2 : 1) 
       const uint32_t tok = tp_token(a.tp, a.tp_sub);
       const unsigned long long tag = (unsigned long long)tok << 32;
       for (int p = 0; p < a.tp.size; ++p)
-        for (int r = ctid; r < nrows; r += kCons)
+        for (int r = ctid; r < nrows; r += kGemvConsumers)
           st_relaxed_sys_u64(a.tp.recv[p] + slot + (size_t)a.tp.rank * a.hidden + r, tag | __float_as_uint(rowsum[r]));
       const unsigned long long* mine = a.tp.recv[a.tp.rank] + slot;
-      for (int r = ctid; r < nrows; r += kCons) {
+      for (int r = ctid; r < nrows; r += kGemvConsumers) {
         unsigned long long w[kMaxTp];
 #pragma unroll
         for (int p = 0; p < kMaxTp; ++p)
@@ -401,13 +391,13 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW == kGemvSmallWarps ? 2 : 1) 
         a.out[r0 + r] = __float2bfloat16_rn(round_bf16(sum) + __bfloat162float(a.residual[r0 + r]));
       }
     } else {
-      for (int r = ctid; r < nrows; r += kCons) {
+      for (int r = ctid; r < nrows; r += kGemvConsumers) {
         const float p = round_bf16(rowsum[r]);
         a.out[r0 + r] = __float2bfloat16_rn(p + __bfloat162float(a.residual[r0 + r]));
       }
     }
   } else if constexpr (EPI == EPI_SWIGLU) {
-    for (int j = ctid; j < nrows / 2; j += kCons) {
+    for (int j = ctid; j < nrows / 2; j += kGemvConsumers) {
       const float g = round_bf16(rowsum[2 * j]);
       const float u = round_bf16(rowsum[2 * j + 1]);
       const float act = round_bf16(silu_f32(g));
@@ -416,7 +406,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW == kGemvSmallWarps ? 2 : 1) 
   } else {  // EPI_ARGMAX
     float best = -INFINITY;
     int best_i = 0x7fffffff;
-    for (int r = ctid; r < nrows; r += kCons) {
+    for (int r = ctid; r < nrows; r += kGemvConsumers) {
       const bf16 lb = __float2bfloat16_rn(rowsum[r]);
       if (a.logits != nullptr) a.logits[r0 + r] = lb;
       const float v = __bfloat162float(lb);
@@ -430,9 +420,9 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW == kGemvSmallWarps ? 2 : 1) 
     }
     int* misci = reinterpret_cast<int*>(misc);
     if (lane == 0) { misc[16 + warp] = best; misci[32 + warp] = best_i; }
-    named_barrier(kGemvBarrierId, kCons);
+    named_barrier(kGemvBarrierId, kGemvConsumers);
     if (ctid == 0) {
-      for (int w = 0; w < CW; ++w) {
+      for (int w = 0; w < kGemvConsumerWarps; ++w) {
         const float ov = misc[16 + w];
         const int oi = misci[32 + w];
         if (ov > best || (ov == best && oi < best_i)) { best = ov; best_i = oi; }
@@ -443,12 +433,12 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW == kGemvSmallWarps ? 2 : 1) 
       const unsigned ticket = atomicAdd(a.counter, 1u);
       misci[48] = (ticket == (unsigned)(G - 1)) ? 1 : 0;
     }
-    named_barrier(kGemvBarrierId, kCons);
+    named_barrier(kGemvBarrierId, kGemvConsumers);
     if (misci[48]) {
       __threadfence();
       best = -INFINITY;
       best_i = 0x7fffffff;
-      for (int i = ctid; i < G; i += kCons) {
+      for (int i = ctid; i < G; i += kGemvConsumers) {
         const float ov = __ldcg(a.part_val + i);
         const int oi = __ldcg(a.part_idx + i);
         if (ov > best || (ov == best && oi < best_i)) { best = ov; best_i = oi; }
@@ -460,9 +450,9 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW == kGemvSmallWarps ? 2 : 1) 
         if (ov > best || (ov == best && oi < best_i)) { best = ov; best_i = oi; }
       }
       if (lane == 0) { misc[64 + warp] = best; misci[80 + warp] = best_i; }
-      named_barrier(kGemvBarrierId, kCons);
+      named_barrier(kGemvBarrierId, kGemvConsumers);
       if (ctid == 0) {
-        for (int w = 0; w < CW; ++w) {
+        for (int w = 0; w < kGemvConsumerWarps; ++w) {
           const float ov = misc[64 + w];
           const int oi = misci[80 + w];
           if (ov > best || (ov == best && oi < best_i)) { best = ov; best_i = oi; }
@@ -477,7 +467,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW == kGemvSmallWarps ? 2 : 1) 
         *a.counter = 0u;
       }
     }
-    if (ctid == 0) trace_stamp(trace_slot(a.trace), TRACE_EXIT);
+    if (TRACE && ctid == 0) trace_stamp(trace_slot(a.trace), TRACE_EXIT);
     return;
   }
   if (a.pos_inc != nullptr && b == 0 && ctid == 0) {
@@ -485,7 +475,7 @@ __global__ void __launch_bounds__((CW + 1) * 32, CW == kGemvSmallWarps ? 2 : 1) 
     // grid are past pdl_wait, and the next reader runs after this grid ends.
     *a.pos_inc += 1;
   }
-  if (ctid == 0) trace_stamp(trace_slot(a.trace), TRACE_EXIT);
+  if (TRACE && ctid == 0) trace_stamp(trace_slot(a.trace), TRACE_EXIT);
 }
 
 }  // namespace qb

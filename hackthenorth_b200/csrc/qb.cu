@@ -87,7 +87,7 @@ int current_sm_count() {
 // again): correct, only slower.
 constexpr int kMaxDevices = 64;
 struct DeviceCache {
-  bool gemv_attr[5][1] = {};
+  bool gemv_attr[5] = {};
   bool pg_attr[3] = {};
   bool attn_attr[2][2] = {};  // [MT - 1][PRO]
   bool rows_attr[5] = {};
@@ -138,20 +138,9 @@ cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sm
 
 // ---------------------------------------------------------------- GEMV launch
 struct GemvPlan {
-  int grid, stages, max_rows, kc, cw;
+  int grid, stages, max_rows, kc;
   size_t smem;
 };
-
-// Small GEMVs on kGemvSmallWarps consumer warps with the CTA's whole share in
-// flight (gemv.cuh); QB_GEMV_SMALL=0 keeps every GEMV on 16 warps.
-bool small_gemv_enabled() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = std::getenv("QB_GEMV_SMALL");
-    v = (e && e[0] == '0') ? 0 : 1;
-  }
-  return v == 1;
-}
 
 int gemv_kc_pref() {
   static int v = 0;
@@ -179,21 +168,6 @@ bool plan_gemv(int epi, int K, int rows, int sm_count, GemvPlan* p) {
   if (units <= 0) return false;
   p->grid = units < sm_count ? units : sm_count;
   p->max_rows = ((units + p->grid - 1) / p->grid) * rpu;
-  if (small_gemv_enabled()) {
-    // One row piece per stage up to K = 4096 columns, every stage of the CTA in flight.
-    const int cw = kGemvSmallWarps;
-    const int kc = K <= 4096 ? K : 2048;
-    const int stages = ((p->max_rows + cw - 1) / cw) * ((K + kc - 1) / kc);
-    const size_t smem = gemv_smem_bytes(K, stages, p->max_rows, kc, cw);
-    if ((size_t)stages * gemv_stage_bytes(kc, cw) <= kGemvSmallRingBytes && smem <= kGemvSmallSmemMax) {
-      p->cw = cw;
-      p->kc = kc;
-      p->stages = stages;
-      p->smem = smem;
-      return true;
-    }
-  }
-  p->cw = kGemvConsumerWarps;
   const size_t fixed = gemv_smem_bytes(K, 0, p->max_rows, 1024);
   // Wider pieces when K allows and the ring still holds >= 3 of them.
   int kc = (K >= 2048 && gemv_kc_pref() == 2048) ? 2048 : 1024;
@@ -210,25 +184,22 @@ bool plan_gemv(int epi, int K, int rows, int sm_count, GemvPlan* p) {
 
 template <int EPI>
 cudaError_t launch_gemv(GemvArgs a, int sm_count, cudaStream_t st) {
-  bool* attr_done = dev_cache().gemv_attr[EPI];
-  if (!attr_done[0]) {
-    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<EPI, kGemvConsumerWarps>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  bool& attr_done = dev_cache().gemv_attr[EPI];
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(gemv_kernel<EPI, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(gemv_kernel<EPI, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(gemv_kernel<EPI, kGemvSmallWarps>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)kGemvSmallSmemMax);
-    if (e != cudaSuccess) return e;
-    attr_done[0] = true;
+    attr_done = true;
   }
   GemvPlan p;
   if (!plan_gemv(EPI, a.K, a.rows, sm_count, &p)) return cudaErrorInvalidValue;
   a.stages = p.stages;
   a.max_rows = p.max_rows;
   a.kc = p.kc;
-  if (p.cw == kGemvSmallWarps)
-    return launch_ex(gemv_kernel<EPI, kGemvSmallWarps>, dim3(p.grid), dim3(gemv_threads(kGemvSmallWarps)), p.smem,
-                     st, a);
-  return launch_ex(gemv_kernel<EPI, kGemvConsumerWarps>, dim3(p.grid), dim3(kGemvThreads), p.smem, st, a);
+  // the traced instantiation only when this launch records timestamps
+  if (a.trace != nullptr) return launch_ex(gemv_kernel<EPI, true>, dim3(p.grid), dim3(kGemvThreads), p.smem, st, a);
+  return launch_ex(gemv_kernel<EPI, false>, dim3(p.grid), dim3(kGemvThreads), p.smem, st, a);
 }
 
 // The GEMV launched after `a` in the step (its weights, shape and epilogue):
@@ -243,7 +214,6 @@ void set_next_gemv(GemvArgs& a, int epi, const void* w, int K, int rows, int sm_
   a.nx_rpu = gemv_rows_per_unit(epi);
   a.nx_kc = p.kc;
   a.nx_grid = p.grid;
-  a.nx_cw = p.cw;
 }
 
 GemvArgs gemv_args(const void* w, int K, int rows, const void* x, void* out, int* err) {
@@ -364,18 +334,9 @@ cudaError_t launch_attn_t(const CUtensorMap& tk, const CUtensorMap& tv, const At
 // long-context choice.
 constexpr int kDecSizes[3] = {16, 8, 4};
 
-// Consumer warps of the decode attention kernel (= ring slots = stages in
-// flight per CTA): 8, or 12 with QB_DEC_WARPS=12.
-int dec_warps() {
-  static int v = 0;
-  if (v == 0) {
-    const char* e = std::getenv("QB_DEC_WARPS");
-    v = (e && std::strtol(e, nullptr, 10) == 12) ? 12 : 8;
-  }
-  return v;
-}
 typedef void (*DecKernelFn)(const CUtensorMap, const CUtensorMap, const AttnArgs);
-DecKernelFn dec_kernel() { return dec_warps() == 12 ? attn_decode_kernel<12> : attn_decode_kernel<8>; }
+// The traced instantiation records timestamps (qb_set_trace); the other has no trace code.
+DecKernelFn dec_kernel(bool trace = false) { return trace ? attn_decode_kernel<true> : attn_decode_kernel<false>; }
 
 int decode_cluster_size(int hkv, int rows) {
   DeviceCache& dc = dev_cache();
@@ -387,15 +348,17 @@ int decode_cluster_size(int hkv, int rows) {
   const char* e = std::getenv("QB_ATTN_CLUSTER");
   if (e && e[0] == '0') return 0;
   if (rows > kDecRows) return 0;
-  const size_t smem = dec_smem_bytes(dec_warps());
-  if (cudaFuncSetAttribute(dec_kernel(), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return 0;
-  cudaFuncSetAttribute(dec_kernel(), cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  const size_t smem = dec_smem_bytes();
+  for (int t = 0; t < 2; ++t) {
+    if (cudaFuncSetAttribute(dec_kernel(t), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return 0;
+    cudaFuncSetAttribute(dec_kernel(t), cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  }
   for (int i = 0; i < 3; ++i) {
     const int cs = kDecSizes[i];
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(hkv * cs);
-    cfg.blockDim = dim3(dec_threads(dec_warps()));
+    cfg.blockDim = dim3(kDecThreads);
     cfg.dynamicSmemBytes = smem;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -415,13 +378,26 @@ int decode_cluster_size(int hkv, int rows) {
   return dc.dec_cs;
 }
 
+// Capacity (and live keys) from which decode attention runs several clusters
+// per KV head: kDecMultiClusterKeys, or QB_ATTN_MULTI_KEYS.
+int dec_multi_keys() {
+  static int v = 0;
+  if (v == 0) {
+    const char* e = std::getenv("QB_ATTN_MULTI_KEYS");
+    const long x = e ? std::strtol(e, nullptr, 10) : 0;
+    v = (x >= 256 && x <= (1 << 24)) ? (int)x : kDecMultiClusterKeys;
+  }
+  return v;
+}
+
 cudaError_t launch_attn_decode(const CUtensorMap& tk, const CUtensorMap& tv, AttnArgs a, int cs, cudaStream_t st) {
   a.splits = cs;
   a.clusters = 1;
+  a.multi_keys = dec_multi_keys();
   // Long contexts: the cluster size and clusters per KV head that put the
   // most CTAs to work at once (several clusters merge through tickets and
   // partial rows in global memory), e.g. 8 heads x 4 clusters x 4 CTAs.
-  if (a.tickets != nullptr && a.part_splits >= 2 && a.cap >= kDecMultiClusterKeys) {
+  if (a.tickets != nullptr && a.part_splits >= 2 && a.cap >= a.multi_keys) {
     int best = a.Hkv * cs;
     for (int i = 0; i < 3; ++i) {
       const int s = kDecSizes[i];
@@ -444,8 +420,8 @@ cudaError_t launch_attn_decode(const CUtensorMap& tk, const CUtensorMap& tv, Att
   cs = a.splits;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.Hkv * a.clusters * cs);
-  cfg.blockDim = dim3(dec_threads(dec_warps()));
-  cfg.dynamicSmemBytes = dec_smem_bytes(dec_warps());
+  cfg.blockDim = dim3(kDecThreads);
+  cfg.dynamicSmemBytes = dec_smem_bytes();
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -456,7 +432,7 @@ cudaError_t launch_attn_decode(const CUtensorMap& tk, const CUtensorMap& tv, Att
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, dec_kernel(), tk, tv, a);
+  return cudaLaunchKernelEx(&cfg, dec_kernel(a.trace != nullptr), tk, tv, a);
 }
 
 // Verify-pass attention (attn_rows_kernel, R = G * Q <= 24 rows) as one

@@ -85,6 +85,12 @@ class StepTrace:
                    "span": round(end - (prev_end if prev_end is not None else start), 2),
                    "release": None if (wait is None or prev_end is None) else round(wait - prev_end, 2),
                    "first": round(statistics.median(firsts), 2) if firsts else None}
+            # per CTA, each stamp relative to the CTA's start: median and max
+            for k, name in ((WAIT, "wait"), (FIRST, "first"), (LOOP, "loop"), (EXIT, "exit")):
+                offs = [(int(a) - int(b)) / 1e3 for a, b in zip(s[:, k], s[:, ENTRY]) if int(a) > 0]
+                if offs:
+                    rec[f"{name}_med"] = round(statistics.median(offs), 2)
+                    rec[f"{name}_max"] = round(max(offs), 2)
             out.append(rec)
             kind = r["label"].split()[0]
             k = kinds.setdefault(kind, {"launches": 0, "span_us": 0.0, "release_us": 0.0})
