@@ -53,7 +53,9 @@ __device__ __forceinline__ void report_error(int* err, int code) {
 // are not recorded.
 constexpr int kTraceMaxCtas = 256;
 constexpr int kTraceStamps = 8;
-enum TraceStamp : int { TRACE_ENTRY = 0, TRACE_WAIT = 1, TRACE_FIRST = 2, TRACE_LOOP = 3, TRACE_EXIT = 4 };
+enum TraceStamp : int { TRACE_ENTRY = 0, TRACE_WAIT = 1, TRACE_FIRST = 2, TRACE_LOOP = 3, TRACE_EXIT = 4,
+                        // decode attention's merge: in-CTA merge done, cluster wait passed, cluster sync passed
+                        TRACE_MERGED = 5, TRACE_CWAIT = 6, TRACE_CSYNC = 7 };
 __device__ __forceinline__ unsigned long long* trace_slot(unsigned long long* launch_base) {
   return (launch_base != nullptr && blockIdx.x < kTraceMaxCtas) ? launch_base + (size_t)blockIdx.x * kTraceStamps
                                                                  : nullptr;

@@ -414,9 +414,11 @@ __global__ void __launch_bounds__(kDecThreads, 1)
       }
     }
   }
+  if (TRACE && tid == 0) trace_stamp(trace_slot(a.trace), TRACE_MERGED);
 
   // ------------------------------------------------------------ cluster merge
   cluster_wait();  // every CTA of the cluster is running
+  if (TRACE && tid == 0) trace_stamp(trace_slot(a.trace), TRACE_CWAIT);
   if (Se == 1 && Cact == 1) {  // uniform: the single split is the answer
     if (tid < kDecMergeThreads && split == 0 && active && ok) {
 #pragma unroll
@@ -444,6 +446,7 @@ __global__ void __launch_bounds__(kDecThreads, 1)
     }
   }
   cluster_sync_all();
+  if (TRACE && tid == 0) trace_stamp(trace_slot(a.trace), TRACE_CSYNC);
   // Merge dims [split*W, split*W + W) of every row over the cluster's Se
   // splits, in split order (dryft/engine/kernels/attention.py:204-206).
   float cval = 0.f, clse = -INFINITY;

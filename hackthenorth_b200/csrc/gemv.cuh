@@ -193,11 +193,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
       const int nb_total = (a.rows + kGemvConsumerWarps - 1) / kGemvConsumerWarps;
       int c = 0;
       bool more = true;
+      // The next block is claimed while the current one is issued, so the
+      // atomic's round trip overlaps the waits for free ring slots.
+      unsigned pending = 0;
+      if (lane == 0) pending = atomicAdd(a.claim, 1u);
       while (more && ok) {
-        int blk = 0;
-        if (lane == 0) blk = (int)atomicAdd(a.claim, 1u);
-        blk = __shfl_sync(0xffffffffu, blk, 0);
+        int blk = __shfl_sync(0xffffffffu, (int)pending, 0);
         more = blk < nb_total;
+        if (more && lane == 0) pending = atomicAdd(a.claim, 1u);
         const int nst = more ? nkc : 1;
         for (int kc = 0; kc < nst; ++kc, ++c) {
           const int s = c % stages;

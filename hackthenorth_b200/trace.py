@@ -23,7 +23,7 @@ from . import _lib
 
 MAX_CTAS = 256
 STAMPS = 8
-ENTRY, WAIT, FIRST, LOOP, EXIT = range(5)
+ENTRY, WAIT, FIRST, LOOP, EXIT, MERGED, CWAIT, CSYNC = range(8)
 
 
 class StepTrace:
@@ -86,7 +86,8 @@ class StepTrace:
                    "release": None if (wait is None or prev_end is None) else round(wait - prev_end, 2),
                    "first": round(statistics.median(firsts), 2) if firsts else None}
             # per CTA, each stamp relative to the CTA's start: median and max
-            for k, name in ((WAIT, "wait"), (FIRST, "first"), (LOOP, "loop"), (EXIT, "exit")):
+            for k, name in ((WAIT, "wait"), (FIRST, "first"), (LOOP, "loop"), (MERGED, "merged"),
+                            (CWAIT, "cwait"), (CSYNC, "csync"), (EXIT, "exit")):
                 offs = [(int(a) - int(b)) / 1e3 for a, b in zip(s[:, k], s[:, ENTRY]) if int(a) > 0]
                 if offs:
                     rec[f"{name}_med"] = round(statistics.median(offs), 2)
