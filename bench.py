@@ -751,7 +751,7 @@ def run_ours(args):
         raise SystemExit(3)
 
 
-def attention_cases(warmup, peak_gbs):
+def attention_cases(warmup, peak_gbs, only=None):
     """Decode-attention op sweep (GQA 32/8, D 128, bf16 N(0,1), batch 1):
     KV lengths 512..131072, 1 query row and the 5-row causal verify variant.
     Each timed launch reads a different KV buffer (>= 256 MB cycled), so the
@@ -764,6 +764,8 @@ def attention_cases(warmup, peak_gbs):
     cases = []
     for L in (512, 4096, 32768, 131072):
         for queries in (1, 5):
+            if only and (L, queries) not in only:
+                continue
             per_call = 2 * 8 * L * 128 * 2
             nbuf = max(2, min(64, -(-(256 << 20) // per_call)))
             kv = [(torch.randn(8, L, 128, generator=gen, device="cuda").to(torch.bfloat16),
@@ -817,7 +819,10 @@ def run_attention_sweep(args):
     qbuild.build()
     torch.cuda.set_device(0)
     peak_gbs, peak_kind = load_peaks()
-    cases = attention_cases(args.warmup, peak_gbs)
+    only = None
+    if args.att_cases:
+        only = {tuple(int(x) for x in c.split(":")) for c in args.att_cases.split(",")}
+    cases = attention_cases(args.warmup, peak_gbs, only)
     print(json.dumps({"op": "grouped_attention", "metric": "decode attention us and GB/s of K/V reads",
                       "peak_gbs": peak_gbs, "peak_source": peak_kind, "dtype": "bf16",
                       "config": {"q_heads": 32, "kv_heads": 8, "head_dim": 128}, "cases": cases}), flush=True)
@@ -1047,6 +1052,8 @@ def main(argv=None):
                          "(neither is the headline line)")
     ap.add_argument("--layers", type=int, default=0,
                     help="profiling only: override the layer count (the line is marked profile_only)")
+    ap.add_argument("--att-cases", default="",
+                    help="--op attention: only these KV_LEN:QUERIES cases, comma separated (e.g. 4096:5)")
     ap.add_argument("--trace", default="",
                     help="write a per-launch timeline of one decode step (the kernels' %%globaltimer stamps) "
                          "to this JSON path (per rank under torchrun: PATH.rankR)")

@@ -32,7 +32,6 @@ constexpr int kGemvThreads = kGemvConsumers + 32;
 // producer lanes in parallel.
 __host__ __device__ inline int gemv_stage_bytes(int kc) { return kGemvConsumerWarps * kc * 2; }
 constexpr int kGemvBarrierId = 1;  // named barrier of the consumer threads
-constexpr int kGemvStageBlkSlot = 104;  // dynamic blocks: misc words [104, 104 + stages) hold each stage's block
 constexpr int kGemvL2Ahead = 2;    // stages of the next GEMV brought into L2 by each CTA
 
 enum GemvEpilogue : int { EPI_STORE = 0, EPI_RESIDUAL = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3, EPI_PARTIAL = 4 };
@@ -99,8 +98,6 @@ struct GemvArgs {
   const bf16* nx_w;
   int nx_K, nx_rows, nx_rpu, nx_kc, nx_grid;
   unsigned long long* trace;  // this launch's trace records (see common.cuh), or NULL
-  unsigned* claim;            // dynamic row blocks (EPI_STORE / EPI_RESIDUAL on one GPU): [0] next
-                              // 16-row block, [1] CTAs done; both back to 0 when the launch ends
 };
 
 __host__ __device__ inline int gemv_rows_per_unit(int epi) { return epi == EPI_SWIGLU ? 2 : 1; }
@@ -131,14 +128,8 @@ __device__ __forceinline__ float dot8_bf16(const uint4 w, const uint4 x, float a
   return acc;
 }
 
-// DYN: CTAs claim 16-row blocks from a.claim instead of owning a fixed row
-// range, so CTAs that start early (on SMs the previous kernel left first) take
-// more blocks and every CTA finishes at about the same time. Each row is still
-// summed by one warp in one fixed order, so the result does not depend on
-// which CTA took it. Store and residual epilogues only (per-row results).
-template <int EPI, bool TRACE = false, bool DYN = false>
+template <int EPI, bool TRACE = false>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a) {
-  static_assert(!DYN || EPI == EPI_STORE || EPI == EPI_RESIDUAL, "dynamic blocks: per-row epilogues only");
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -185,62 +176,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
     int issued = 0;
     bool ok = true;
     bool waited = false;
-    if constexpr (DYN) {
-      // Claim blocks until none is left; each block is nkc stages. A stage
-      // whose block id is -1 (a plain arrival, no bytes) tells the consumers
-      // that this CTA is done.
-      int* stage_blk = reinterpret_cast<int*>(misc) + kGemvStageBlkSlot;
-      const int nb_total = (a.rows + kGemvConsumerWarps - 1) / kGemvConsumerWarps;
-      int c = 0;
-      bool more = true;
-      // The next block is claimed while the current one is issued, so the
-      // atomic's round trip overlaps the waits for free ring slots.
-      unsigned pending = 0;
-      if (lane == 0) pending = atomicAdd(a.claim, 1u);
-      while (more && ok) {
-        int blk = __shfl_sync(0xffffffffu, (int)pending, 0);
-        more = blk < nb_total;
-        if (more && lane == 0) pending = atomicAdd(a.claim, 1u);
-        const int nst = more ? nkc : 1;
-        for (int kc = 0; kc < nst; ++kc, ++c) {
-          const int s = c % stages;
-          if (c >= stages) {
-            if (!waited) {
-              pdl_wait();
-              pdl_trigger();
-              waited = true;
-            }
-            int good = 1;
-            if (lane == 0) good = mbar_wait(&empty[s], ((c / stages) - 1) & 1, a.err, DEV_TIMEOUT_GEMV_EMPTY) ? 1 : 0;
-            good = __shfl_sync(0xffffffffu, good, 0);
-            if (!good) {
-              ok = false;
-              break;
-            }
-          }
-          if (!more) {
-            if (lane == 0) {
-              reinterpret_cast<volatile int*>(stage_blk)[s] = -1;
-              mbar_arrive(&full[s]);
-            }
-            break;
-          }
-          const int nr = min(kGemvConsumerWarps, a.rows - blk * kGemvConsumerWarps);
-          const int c0 = kc * KC;
-          const uint32_t piece = (uint32_t)min(KC, K - c0) * 2;
-          if (lane == 0) {
-            reinterpret_cast<volatile int*>(stage_blk)[s] = blk;
-            mbar_arrive_expect_tx(&full[s], piece * nr);
-          }
-          __syncwarp();
-          if (lane < nr)
-            bulk_g2s(ring + (size_t)s * stage_bytes + lane * (KC * 2),
-                     a.w + (size_t)(blk * kGemvConsumerWarps + lane) * K + c0, piece, &full[s], policy);
-          issued = c + 1;
-        }
-      }
-    }
-    for (int c = 0; c < (DYN ? 0 : nstage); ++c) {
+    for (int c = 0; c < nstage; ++c) {
       const int s = c % stages;
       if (c >= stages) {
         if (!waited) {
@@ -372,63 +308,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
   float rowacc = 0.f;
   bool ok = true;
   int c = 0;
-  if constexpr (DYN) {
-    // Blocks in the order the producer claimed them; each row's result is
-    // written as soon as its last piece is summed.
-    const int* stage_blk = reinterpret_cast<const int*>(misc) + kGemvStageBlkSlot;
-    int kc = 0;
-    for (;; ++c) {
-      const int s = c % stages;
-      if (!mbar_wait(&full[s], (c / stages) & 1, a.err, DEV_TIMEOUT_GEMV_FULL)) {
-        ok = false;
-        break;
-      }
-      if (TRACE && c == 0 && ctid == 0) trace_stamp(trace_slot(a.trace), TRACE_FIRST);
-      const int blk = reinterpret_cast<const volatile int*>(stage_blk)[s];
-      if (blk < 0) break;  // the CTA's last claim found no block
-      const int row = blk * kGemvConsumerWarps + warp;
-      if (row < a.rows) {
-        const int c0 = kc * KC;
-        const uint8_t* piece = ring + (size_t)s * stage_bytes + warp * (KC * 2) + lane * 16;
-        const bf16* xp = xs + c0 + lane * 8;
-        const int ncols = min(KC, K - c0);
-        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-        int j = 0;
-        for (; j + 1024 <= ncols; j += 1024) {
-          const uint4 w0 = lds128(piece + j * 2);
-          const uint4 w1 = lds128(piece + j * 2 + 512);
-          const uint4 w2 = lds128(piece + j * 2 + 1024);
-          const uint4 w3 = lds128(piece + j * 2 + 1536);
-          const uint4 x0 = lds128(xp + j);
-          const uint4 x1 = lds128(xp + j + 256);
-          const uint4 x2 = lds128(xp + j + 512);
-          const uint4 x3 = lds128(xp + j + 768);
-          a0 = dot8_bf16(w0, x0, a0);
-          a1 = dot8_bf16(w1, x1, a1);
-          a2 = dot8_bf16(w2, x2, a2);
-          a3 = dot8_bf16(w3, x3, a3);
-        }
-        for (; j < ncols; j += 256)
-          if (j + lane * 8 < ncols) a0 = dot8_bf16(lds128(piece + j * 2), lds128(xp + j), a0);
-        rowacc += (a0 + a1) + (a2 + a3);
-        if (kc == nkc - 1) {
-          const float t = warp_sum(rowacc);
-          if (lane == 0) {
-            if constexpr (EPI == EPI_STORE) {
-              a.out[row] = __float2bfloat16_rn(t);
-            } else {
-              a.out[row] = __float2bfloat16_rn(round_bf16(t) + __bfloat162float(a.residual[row]));
-            }
-          }
-          rowacc = 0.f;
-        }
-      }
-      kc = (kc + 1 == nkc) ? 0 : kc + 1;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[s]);
-    }
-  }
-  for (int blk = 0; blk < (DYN ? 0 : nblk) && ok; ++blk) {
+  for (int blk = 0; blk < nblk && ok; ++blk) {
     const int row = blk * kGemvConsumerWarps + warp;
     const bool active = row < nrows;
     for (int kc = 0; kc < nkc; ++kc, ++c) {
@@ -476,22 +356,6 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
   named_barrier(kGemvBarrierId, kGemvConsumers);
   if (reinterpret_cast<volatile int*>(misc)[100] != 0) return;  // uniform across the CTA
   if (TRACE && ctid == 0) trace_stamp(trace_slot(a.trace), TRACE_LOOP);
-  if constexpr (DYN) {
-    // Rows are written. The last CTA to finish puts the claim counters back
-    // to zero for the next launch (every CTA's final, failing claim precedes
-    // its own count here).
-    if (ctid == 0) {
-      __threadfence();
-      const unsigned t = atomicAdd(a.claim + 1, 1u);
-      if (t == (unsigned)(G - 1)) {
-        a.claim[0] = 0u;
-        a.claim[1] = 0u;
-      }
-      if (a.pos_inc != nullptr && b == 0) *a.pos_inc += 1;
-      if (TRACE) trace_stamp(trace_slot(a.trace), TRACE_EXIT);
-    }
-    return;
-  }
 
   // 3. Epilogue.
   if constexpr (EPI == EPI_STORE) {

@@ -55,7 +55,6 @@ constexpr size_t kScrHeadIdx = 5120;       // int[1024]
 constexpr size_t kScrAttnLse = 9216;       // float[16384]
 constexpr size_t kScrAttnO = 9216 + 65536; // float[...] up to the end
 constexpr int kMaxAttnCtas = 512;
-constexpr int kClaimCounters = 960;  // context counters: claim pairs of the qkv, o and down GEMVs
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
@@ -89,7 +88,6 @@ int current_sm_count() {
 constexpr int kMaxDevices = 64;
 struct DeviceCache {
   bool gemv_attr[5] = {};
-  bool gemv_dyn_attr[2] = {};
   bool pg_attr[3] = {};
   bool attn_attr[2][2] = {};  // [MT - 1][PRO]
   bool rows_attr[5] = {};
@@ -199,38 +197,9 @@ cudaError_t launch_gemv(GemvArgs a, int sm_count, cudaStream_t st) {
   a.stages = p.stages;
   a.max_rows = p.max_rows;
   a.kc = p.kc;
-  if constexpr (EPI == EPI_STORE || EPI == EPI_RESIDUAL) {
-    if (a.claim != nullptr && a.tp.size <= 1) {
-      bool& dyn_attr = dev_cache().gemv_dyn_attr[EPI];
-      if (!dyn_attr) {
-        cudaError_t e = cudaFuncSetAttribute(gemv_kernel<EPI, false, true>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        if (e == cudaSuccess)
-          e = cudaFuncSetAttribute(gemv_kernel<EPI, true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   227 * 1024);
-        if (e != cudaSuccess) return e;
-        dyn_attr = true;
-      }
-      if (a.trace != nullptr)
-        return launch_ex(gemv_kernel<EPI, true, true>, dim3(p.grid), dim3(kGemvThreads), p.smem, st, a);
-      return launch_ex(gemv_kernel<EPI, false, true>, dim3(p.grid), dim3(kGemvThreads), p.smem, st, a);
-    }
-  }
-  a.claim = nullptr;
   // the traced instantiation only when this launch records timestamps
   if (a.trace != nullptr) return launch_ex(gemv_kernel<EPI, true>, dim3(p.grid), dim3(kGemvThreads), p.smem, st, a);
   return launch_ex(gemv_kernel<EPI, false>, dim3(p.grid), dim3(kGemvThreads), p.smem, st, a);
-}
-
-// Dynamic row blocks for the decode step's store/residual GEMVs on one GPU
-// (gemv.cuh, DYN): on unless QB_GEMV_DYNAMIC=0.
-bool dynamic_gemv_enabled() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = std::getenv("QB_GEMV_DYNAMIC");
-    v = (e && e[0] == '0') ? 0 : 1;
-  }
-  return v == 1;
 }
 
 // The GEMV launched after `a` in the step (its weights, shape and epilogue):
@@ -686,8 +655,7 @@ WsLayout ws_layout(const qb_ctx* c) {
   WsLayout L;
   size_t o = 0;
   L.err = o; o += 256;
-  L.counters = o; o += 4096;  // [0,64) attention, 64/66 heads, [128,194) step kernel, [512,..) decode clusters,
-                             // [kClaimCounters, +6) dynamic GEMV blocks (qkv, o, down)
+  L.counters = o; o += 4096;  // [0,64) attention, 64/66 heads, [128,194) step kernel, [512,..) decode clusters
   L.head_val = o; o = align_up(o + 4 * 1024, 256);
   L.head_idx = o; o = align_up(o + 4 * 1024, 256);
   L.xa = o; o = align_up(o + (size_t)g.hidden * 2, 256);
@@ -773,7 +741,6 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
   const int nqkv = (g.n_heads + 2 * g.n_kv_heads) * D;
   const bool tp = c->tp_size > 1;
   const bool p2p = tp && c->p2p;
-  const bool dyn = !tp && dynamic_gemv_enabled();
   cudaError_t e;
   ncclResult_t nr;
   if (head) {  // a decode step: its launches are traced from index 0
@@ -809,7 +776,6 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
       consume(a, c->xb, c->xa);
     }
     set_next_gemv(a, EPI_RESIDUAL, w.o, g.n_heads * D, H, c->sm_count);  // across the attention launch
-    if (dyn) a.claim = c->counters + kClaimCounters;
     if (head) a.trace = next_trace(c, "qkv", l);
     if ((e = launch_gemv<EPI_STORE>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "qkv launch");
     // 2. attention with the norm/rope/append prologue
@@ -853,7 +819,6 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
       a = gemv_args(w.o, g.n_heads * D, H, c->attn, c->xb, c->err);
       a.residual = c->xa;
       if (p2p) peer_reduce(a, 2 * l, 0);
-      if (dyn) a.claim = c->counters + kClaimCounters + 2;
       set_next_gemv(a, EPI_SWIGLU, w.gate_up, H, 2 * g.ffn, c->sm_count);
       if (head) a.trace = next_trace(c, "o", l);
       if ((e = launch_gemv<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "o launch");
@@ -885,7 +850,6 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
       a.residual = c->xb;
       if (p2p) peer_reduce(a, 2 * l + 1, 1);
       else if (!head && l == g.n_layers - 1) a.pos_inc = pos;
-      if (dyn) a.claim = c->counters + kClaimCounters + 4;
       next_of_down(a);
       if (head) a.trace = next_trace(c, "down", l);
       if ((e = launch_gemv<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess)
