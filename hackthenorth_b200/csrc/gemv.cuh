@@ -73,6 +73,8 @@ struct GemvArgs {
   const bf16* gain;     // [K] RMSNorm gain, or NULL (no norm)
   float eps;
   const bf16* residual; // EPI_RESIDUAL
+  int res_early;        // EPI_RESIDUAL: the residual was written at least two launches earlier
+                        // (decode steps), so each thread reads its first row before the dependency wait
   bf16* out;            // EPI_STORE/RESIDUAL: [rows]; SWIGLU: [rows/2]
   float* out32;         // EPI_PARTIAL: [rows] fp32 sums (not rounded; reduced across ranks next)
   int row_base;         // EPI_ARGMAX: global index of weight row 0 (vocabulary shard offset)
@@ -237,6 +239,20 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
 
   // ---------------- consumer warps ----------------
   const int ctid = tid;  // 0..kGemvConsumers-1
+  // Inputs that do not depend on the previous launch, read before the wait so
+  // that no dependent global load sits between the input row and the loop or
+  // the epilogue: this thread's RMSNorm gain chunks (weights) and, when the
+  // caller marks the residual as written two launches earlier, its first
+  // residual row.
+  constexpr bool kPreGain = EPI == EPI_STORE || EPI == EPI_SWIGLU || EPI == EPI_ARGMAX;  // the normed projections
+  uint4 gpre0 = make_uint4(0u, 0u, 0u, 0u), gpre1 = make_uint4(0u, 0u, 0u, 0u);
+  if (kPreGain && a.gain != nullptr) {
+    if (ctid * 8 < K) gpre0 = ldg128_nc(a.gain + ctid * 8);
+    if (ctid * 8 + kGemvConsumers * 8 < K) gpre1 = ldg128_nc(a.gain + ctid * 8 + kGemvConsumers * 8);
+  }
+  float res_pre = 0.f;
+  if constexpr (EPI == EPI_RESIDUAL)
+    if (a.res_early && ctid < nrows) res_pre = __bfloat162float(a.residual[r0 + ctid]);
   pdl_wait();
   pdl_trigger();
   if (TRACE && ctid == 0) trace_stamp(trace_slot(a.trace), TRACE_WAIT);
@@ -288,9 +304,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
     for (int w = 0; w < kGemvConsumerWarps; ++w) tot += misc[w];
     // rsqrt(mean(x^2) + eps) as 1/sqrt: correctly rounded sqrt and division.
     const float inv = 1.0f / sqrtf(tot / (float)K + a.eps);
-    for (int i = ctid * 8; i < K; i += kGemvConsumers * 8) {
+    for (int i = ctid * 8, it = 0; i < K; i += kGemvConsumers * 8, ++it) {
       uint4 v = *reinterpret_cast<const uint4*>(xs + i);
-      const uint4 g = ldg128_nc(a.gain + i);
+      const uint4 g = (kPreGain && it == 0) ? gpre0 : ((kPreGain && it == 1) ? gpre1 : ldg128_nc(a.gain + i));
       uint32_t* pv = reinterpret_cast<uint32_t*>(&v);
       const uint32_t* pg = reinterpret_cast<const uint32_t*>(&g);
 #pragma unroll
@@ -388,12 +404,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const GemvArgs a)
             sum += ((uint32_t)(w[p] >> 32) == tok)
                        ? __uint_as_float((uint32_t)w[p])
                        : wait_tagged(mine + (size_t)p * a.hidden + r, tok, a.err, DEV_TIMEOUT_PEER_FLAG);
-        a.out[r0 + r] = __float2bfloat16_rn(round_bf16(sum) + __bfloat162float(a.residual[r0 + r]));
+        const float res = (a.res_early && r == ctid) ? res_pre : __bfloat162float(a.residual[r0 + r]);
+        a.out[r0 + r] = __float2bfloat16_rn(round_bf16(sum) + res);
       }
     } else {
       for (int r = ctid; r < nrows; r += kGemvConsumers) {
         const float p = round_bf16(rowsum[r]);
-        a.out[r0 + r] = __float2bfloat16_rn(p + __bfloat162float(a.residual[r0 + r]));
+        const float res = (a.res_early && r == ctid) ? res_pre : __bfloat162float(a.residual[r0 + r]);
+        a.out[r0 + r] = __float2bfloat16_rn(p + res);
       }
     }
   } else if constexpr (EPI == EPI_SWIGLU) {

@@ -378,6 +378,22 @@ int decode_cluster_size(int hkv, int rows) {
   return dc.dec_cs;
 }
 
+// Decode-step SM partition around attention (bit 0: o-proj, bit 1: QKV).
+// Default (-1): both, when the attention launch holds at most 1/8 of the SMs
+// (one KV head per GPU: tensor parallel 8); QB_PART=0..3 forces the bits.
+// Measured (one B200): with 16 attention CTAs (Qwen3-8B shapes of one of 8
+// tensor-parallel ranks) 956 -> 986 tok/s; with 64 (8 KV heads) slower, 348 ->
+// 325 tok/s at 8B and 1461 -> 1402 at 0.6B: one SM pulls at most ~60 GB/s, so
+// GEMVs on 84 SMs lose bandwidth.
+int gemv_partition() {
+  static int v = -2;
+  if (v == -2) {
+    const char* e = std::getenv("QB_PART");
+    v = e ? (int)(std::strtol(e, nullptr, 10) & 3) : -1;
+  }
+  return v;
+}
+
 // Capacity (and live keys) from which decode attention runs several clusters
 // per KV head: kDecMultiClusterKeys, or QB_ATTN_MULTI_KEYS.
 int dec_multi_keys() {
@@ -390,7 +406,9 @@ int dec_multi_keys() {
   return v;
 }
 
-cudaError_t launch_attn_decode(const CUtensorMap& tk, const CUtensorMap& tv, AttnArgs a, int cs, cudaStream_t st) {
+// The launch shape of decode attention (attn_decode_kernel) for `a`: cluster
+// size (a.splits) and clusters per KV head (a.clusters).
+void dec_shape(AttnArgs& a, int cs) {
   a.splits = cs;
   a.clusters = 1;
   a.multi_keys = dec_multi_keys();
@@ -410,6 +428,21 @@ cudaError_t launch_attn_decode(const CUtensorMap& tk, const CUtensorMap& tv, Att
       }
     }
   }
+}
+
+// CTAs of the decode attention launch for `a` (launch_attn with the prologue,
+// one query row), or 0 when attn_decode_kernel does not apply.
+int dec_ctas(const AttnArgs& a) {
+  if (a.Q != 1) return 0;
+  const int cs = decode_cluster_size(a.Hkv, a.Hq / a.Hkv);
+  if (cs <= 0) return 0;
+  AttnArgs t = a;
+  dec_shape(t, cs);
+  return t.Hkv * t.clusters * t.splits;
+}
+
+cudaError_t launch_attn_decode(const CUtensorMap& tk, const CUtensorMap& tv, AttnArgs a, int cs, cudaStream_t st) {
+  dec_shape(a, cs);
   static bool reported = false;
   if (!reported && std::getenv("QB_VERBOSE")) {
     reported = true;
@@ -760,25 +793,10 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
     a.x_copy = copy;
     a.x32 = c->y32;
   };
+  const int part = gemv_partition();
   for (int l = 0; l < g.n_layers; ++l) {
     const qb_layer_weights& w = c->layers[l];
-    // 1. RMSNorm + QKV (layer 0 gathers the embedding row into xa; under TP
-    //    later layers finish the previous down's reduction: xa = xb + sum)
-    GemvArgs a = gemv_args(w.qkv, H, nqkv, l == 0 ? nullptr : c->xa, c->qkv, c->err);
-    a.gain = static_cast<const bf16*>(w.input_norm);
-    a.eps = g.rms_eps;
-    if (l == 0) {
-      a.embed = c->embed;
-      a.token = tok_in;
-      a.vocab = c->cfg.vocab;
-      a.x_copy = c->xa;
-    } else if (tp && !p2p) {
-      consume(a, c->xb, c->xa);
-    }
-    set_next_gemv(a, EPI_RESIDUAL, w.o, g.n_heads * D, H, c->sm_count);  // across the attention launch
-    if (head) a.trace = next_trace(c, "qkv", l);
-    if ((e = launch_gemv<EPI_STORE>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "qkv launch");
-    // 2. attention with the norm/rope/append prologue
+    // attention of this layer (launched after the QKV GEMV)
     AttnArgs at;
     std::memset(&at, 0, sizeof(at));
     at.qkv = c->qkv;
@@ -803,6 +821,32 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
     at.splits = c->splits;
     at.part_splits = c->splits;
     at.tickets = c->counters + 512;
+    // SM partition around attention (gemv_partition): the QKV and o-proj
+    // GEMVs on the SMs attention does not hold (grid = SMs - attention CTAs),
+    // so attention's CTAs find free SMs while the QKV GEMV streams and every
+    // o-proj CTA starts (and prefetches its weights) during attention.
+    const int attn_n = part != 0 ? dec_ctas(at) : 0;
+    const int bits = part >= 0 ? part : (attn_n > 0 && 8 * attn_n <= c->sm_count ? 3 : 0);
+    const int free_sms = (attn_n > 0 && 2 * attn_n <= c->sm_count) ? c->sm_count - attn_n : c->sm_count;
+    const int qkv_sms = (bits & 2) ? free_sms : c->sm_count;
+    const int o_sms = (bits & 1) ? free_sms : c->sm_count;
+    // 1. RMSNorm + QKV (layer 0 gathers the embedding row into xa; under TP
+    //    later layers finish the previous down's reduction: xa = xb + sum)
+    GemvArgs a = gemv_args(w.qkv, H, nqkv, l == 0 ? nullptr : c->xa, c->qkv, c->err);
+    a.gain = static_cast<const bf16*>(w.input_norm);
+    a.eps = g.rms_eps;
+    if (l == 0) {
+      a.embed = c->embed;
+      a.token = tok_in;
+      a.vocab = c->cfg.vocab;
+      a.x_copy = c->xa;
+    } else if (tp && !p2p) {
+      consume(a, c->xb, c->xa);
+    }
+    set_next_gemv(a, EPI_RESIDUAL, w.o, g.n_heads * D, H, o_sms);  // across the attention launch
+    if (head) a.trace = next_trace(c, "qkv", l);
+    if ((e = launch_gemv<EPI_STORE>(a, qkv_sms, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "qkv launch");
+    // 2. attention with the norm/rope/append prologue
     if (head) at.trace = next_trace(c, "attn", l);
     if ((e = launch_attn(c->tmk[l], c->tmv[l], &c->dmk[l], &c->dmv[l], at, true, st)) != cudaSuccess)
       return cuda_fail(&c->msg, e, "attention launch");
@@ -812,16 +856,17 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
       a.out32 = c->y32;
       set_next_gemv(a, EPI_SWIGLU, w.gate_up, H, 2 * g.ffn, c->sm_count);
       if (head) a.trace = next_trace(c, "o", l);
-      if ((e = launch_gemv<EPI_PARTIAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "o launch");
+      if ((e = launch_gemv<EPI_PARTIAL>(a, o_sms, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "o launch");
       if ((nr = ncclAllReduce(c->y32, c->y32, H, ncclFloat32, ncclSum, c->comm, st)) != ncclSuccess)
         return set_err(&c->msg, QB_ERR_CUDA, std::string("ncclAllReduce: ") + ncclGetErrorString(nr));
     } else {
       a = gemv_args(w.o, g.n_heads * D, H, c->attn, c->xb, c->err);
       a.residual = c->xa;
+      a.res_early = 1;  // xa: written by the previous down (or this layer's QKV gather), 2+ launches back
       if (p2p) peer_reduce(a, 2 * l, 0);
       set_next_gemv(a, EPI_SWIGLU, w.gate_up, H, 2 * g.ffn, c->sm_count);
       if (head) a.trace = next_trace(c, "o", l);
-      if ((e = launch_gemv<EPI_RESIDUAL>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "o launch");
+      if ((e = launch_gemv<EPI_RESIDUAL>(a, o_sms, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "o launch");
     }
     // 4. RMSNorm + gate/up + SwiGLU
     a = gemv_args(w.gate_up, H, 2 * g.ffn, c->xb, c->act, c->err);
@@ -834,7 +879,7 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
       return cuda_fail(&c->msg, e, "gate/up launch");
     // 5. down (+ residual): xa = xb + Down . act
     auto next_of_down = [&](GemvArgs& d) {
-      if (l + 1 < g.n_layers) set_next_gemv(d, EPI_STORE, c->layers[l + 1].qkv, H, nqkv, c->sm_count);
+      if (l + 1 < g.n_layers) set_next_gemv(d, EPI_STORE, c->layers[l + 1].qkv, H, nqkv, qkv_sms);
       else if (head) set_next_gemv(d, EPI_ARGMAX, c->lm_head, H, g.vocab, c->sm_count);
     };
     if (tp && !p2p) {
@@ -848,6 +893,7 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
     } else {
       a = gemv_args(w.down, g.ffn, H, c->act, c->xa, c->err);
       a.residual = c->xb;
+      a.res_early = 1;  // xb: written by this layer's o-proj, two launches back
       if (p2p) peer_reduce(a, 2 * l + 1, 1);
       else if (!head && l == g.n_layers - 1) a.pos_inc = pos;
       next_of_down(a);
