@@ -646,8 +646,6 @@ def run_ours(args):
                    "parallelism": "none" if world == 1 else (
                        f"tp{world} (NCCL all-reduce after o-proj and down)" if os.environ.get("QB_TP_NCCL") == "1"
                        else f"tp{world} (peer-memory reduction fused into the o-proj and down epilogues over NVLink)"),
-                   "decode_path": os.environ.get("QB_STEP_KERNEL") == "1" and world == 1 and "step-kernel"
-                   or "per-sublayer",
                    "l2": "inputs larger than L2 (weights stream %.1f GB per step)" % (cfg.weight_bytes_per_token() / 1e9)},
         "repeats": {"windows": len(windows), "steps_each": args.steps,
                     "tok_s": [round(r, 2) for r in rates], "median_tok_s": round(statistics.median(rates), 2),
@@ -1065,10 +1063,7 @@ def main(argv=None):
                          "prefill_ms) instead of seeded random K/V values")
     ap.add_argument("--batch", type=int, default=1,
                     help="sequences decoded together (1..8, one GPU; the line's value is their total tok/s)")
-    ap.add_argument("--decode-path", choices=("per-sublayer", "step-kernel"), default="per-sublayer",
-                    help="step-kernel: the opt-in persistent one-launch-per-step kernel (single GPU)")
     args = ap.parse_args(argv)
-    os.environ["QB_STEP_KERNEL"] = "1" if args.decode_path == "step-kernel" else "0"
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
     if args.impl == "reference":

@@ -48,7 +48,6 @@ SIGNATURES = {
     "qb_capture_decode": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "qb_replay_decode": (c_int, [c_void_p, c_void_p]),
     "qb_check": (c_int, [c_void_p, c_void_p]),
-    "qb_decode_mode": (c_int, [c_void_p]),
     "qb_set_trace": (c_int, [c_void_p, c_void_p, c_size_t]),
     "qb_trace_labels": (ctypes.c_char_p, [c_void_p]),
     "qb_prefill_scratch_bytes": (c_int, [c_void_p, c_int, c_void_p]),

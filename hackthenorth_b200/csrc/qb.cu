@@ -24,7 +24,6 @@
 
 #include "attention.cuh"
 #include "decode_attention.cuh"
-#include "step_kernel.cuh"
 #include "gemv_rows.cuh"
 #include "verify_attention.cuh"
 #include "prefill_gemm.cuh"
@@ -645,10 +644,6 @@ struct qb_ctx {
   std::vector<CUtensorMap> dmk, dmv;  // 32-row boxes (decode kernel)
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
-  // Persistent step kernel (one cooperative launch per decode step).
-  uint32_t *w_xa = nullptr, *w_xb = nullptr, *w_qkv = nullptr, *w_attn = nullptr, *w_act = nullptr;
-  unsigned long long *w_part_o = nullptr, *w_part_lse = nullptr;
-  unsigned* step_epoch = nullptr;   // tag step counter (in the error block, kept across counter resets)
   // verify pass (k+1 rows)
   bf16 *r_xa = nullptr, *r_xb = nullptr, *r_qkv = nullptr, *r_q = nullptr, *r_attn = nullptr, *r_act = nullptr;
   int64_t* r_pos = nullptr;
@@ -658,12 +653,6 @@ struct qb_ctx {
   float* r_pairs = nullptr;  // tensor parallel verify: [rows][2] + [tp][rows][2]
   cudaGraph_t vgraph = nullptr;
   cudaGraphExec_t vexec = nullptr;
-  bool step_allowed = false;        // QB_STEP_KERNEL=1 at creation turns it on
-  bool step_ready = false;          // descriptors built for the bound weights and state
-  void* step_buf = nullptr;         // device: [2L tensor maps | 5L+1 phases]
-  const StepPhase* step_phases = nullptr;
-  int step_nphases = 0, step_xs = 0, step_rows = 0, step_splits = 1;
-  size_t step_smem = 0;
   // tracing (qb_set_trace): launch i of the decode step records its CTAs'
   // stamps at trace + i * kTraceMaxCtas * kTraceStamps
   unsigned long long* trace = nullptr;
@@ -677,8 +666,6 @@ namespace {
 
 struct WsLayout {
   size_t err, counters, head_val, head_idx, xa, xb, qkv, attn, act, part_lse, part_o, y32, pairs;
-  // persistent step kernel: tagged activation words and split partials
-  size_t w_xa, w_xb, w_qkv, w_attn, w_act, w_part_o, w_part_lse;
   // verify pass: up to kRowsMaxQ rows
   size_t r_xa, r_xb, r_qkv, r_q, r_attn, r_act, r_pos, r_val, r_idx, r_y32, r_pairs, total;
 };
@@ -688,7 +675,7 @@ WsLayout ws_layout(const qb_ctx* c) {
   WsLayout L;
   size_t o = 0;
   L.err = o; o += 256;
-  L.counters = o; o += 4096;  // [0,64) attention, 64/66 heads, [128,194) step kernel, [512,..) decode clusters
+  L.counters = o; o += 4096;  // [0,64) attention, 64/66 heads, [512,..) decode clusters
   L.head_val = o; o = align_up(o + 4 * 1024, 256);
   L.head_idx = o; o = align_up(o + 4 * 1024, 256);
   L.xa = o; o = align_up(o + (size_t)g.hidden * 2, 256);
@@ -702,14 +689,6 @@ WsLayout ws_layout(const qb_ctx* c) {
   L.y32 = o; o = align_up(o + (size_t)g.hidden * 4, 256);
   L.pairs = o; o = align_up(o + (size_t)(2 + 2 * c->tp_size) * 4, 256);
   const int nqkv = (g.n_heads + 2 * g.n_kv_heads) * g.head_dim;
-  L.w_xa = o; o = align_up(o + (size_t)g.hidden * 4, 256);
-  L.w_xb = o; o = align_up(o + (size_t)g.hidden * 4, 256);
-  L.w_qkv = o; o = align_up(o + (size_t)nqkv * 4, 256);
-  L.w_attn = o; o = align_up(o + (size_t)g.n_heads * g.head_dim * 4, 256);
-  L.w_act = o; o = align_up(o + (size_t)g.ffn * 4, 256);
-  const size_t wparts = (size_t)g.n_kv_heads * kStepMaxSplits * kDecRows;
-  L.w_part_lse = o; o = align_up(o + wparts * 8, 256);
-  L.w_part_o = o; o = align_up(o + wparts * kAttnD * 8, 256);
   const size_t R = kRowsMaxQ;
   L.r_xa = o; o = align_up(o + R * g.hidden * 2, 256);
   L.r_xb = o; o = align_up(o + R * g.hidden * 2, 256);
@@ -741,8 +720,6 @@ int validate_config(const qb_config* g, std::string* msg) {
   return QB_OK;
 }
 
-cudaError_t launch_step(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t* pos, void* logits,
-                        cudaStream_t st);
 
 // The trace records of the next launch of the step being built (NULL when
 // tracing is off or the buffer is full), and its label.
@@ -764,11 +741,6 @@ unsigned long long* next_trace(qb_ctx* c, const char* label, int layer) {
 // shards with an 8-byte all-gather.
 int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t* pos, void* logits, bool head,
                     cudaStream_t st) {
-  if (head && c->step_ready) {
-    cudaError_t se = launch_step(c, tok_in, tok_out, pos, logits, st);
-    if (se != cudaSuccess) return cuda_fail(&c->msg, se, "step kernel launch");
-    return QB_OK;
-  }
   const qb_config& g = c->lc;
   const int H = g.hidden, D = g.head_dim;
   const int nqkv = (g.n_heads + 2 * g.n_kv_heads) * D;
@@ -946,193 +918,6 @@ int run_rows_decode(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t*
   return QB_OK;
 }
 
-// Builds the persistent step kernel's phase table for the bound weights and
-// state (single-GPU contexts only), or leaves step_ready false when the kernel
-// does not apply; decode then uses the per-sublayer launches.
-void release_step(qb_ctx* c) {
-  if (c->step_buf) cudaFree(c->step_buf);
-  c->step_buf = nullptr;
-  c->step_phases = nullptr;
-  c->step_ready = false;
-}
-
-void prepare_step(qb_ctx* c) {
-  release_step(c);
-  auto off = [&](const char* why) {
-    if (std::getenv("QB_VERBOSE")) std::fprintf(stderr, "qb: persistent step kernel off: %s\n", why);
-  };
-  if (!c->weights_bound || !c->state_bound) return;
-  if (!c->step_allowed) return off("not requested (QB_STEP_KERNEL=1)");
-  if (c->tp_size != 1) return off("tensor parallel");
-  if (c->batch != 1) return off("batched decode");
-  const qb_config& g = c->lc;
-  const int G = c->sm_count, D = g.head_dim;
-  if (g.n_heads / g.n_kv_heads > kDecRows || g.n_kv_heads > 64 || G > 1024) return off("head layout");
-  if ((g.hidden + G - 1) / G > kStepConsumers) return off("hidden too large");  // residual rows: one thread each
-  const int kmax = std::max({g.hidden, g.n_heads * D, g.ffn});
-  const int xs = (int)std::max<size_t>(kStepCombineBytes, align_up((size_t)kmax * 2, 16));
-  auto per_cta = [&](int rows, int rpu) { return ((rows / rpu + G - 1) / G) * rpu; };
-  const int nqkv = (g.n_heads + 2 * g.n_kv_heads) * D;
-  const int max_rows = std::max({per_cta(nqkv, 1), per_cta(g.hidden, 1), per_cta(2 * g.ffn, 2), per_cta(g.vocab, 1)});
-  const size_t smem = step_smem_bytes(xs, max_rows);
-  if (smem > 227 * 1024) return off("shared memory");
-  if (cudaFuncSetAttribute(step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
-    cudaGetLastError();
-    return off("shared memory attribute");
-  }
-  int per_sm = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, step_kernel, kStepThreads, smem) != cudaSuccess ||
-      per_sm < 1) {
-    cudaGetLastError();
-    return off("occupancy");
-  }
-  const int L = g.n_layers;
-  std::vector<StepPhase> ph;
-  ph.reserve(5 * L + 1);
-  const size_t maps_bytes = align_up((size_t)2 * L * sizeof(CUtensorMap), 256);
-  const size_t total = maps_bytes + (size_t)(5 * L + 1) * sizeof(StepPhase);
-  void* buf = nullptr;
-  if (cudaMalloc(&buf, total) != cudaSuccess) {
-    cudaGetLastError();
-    return off("descriptor allocation");
-  }
-  const CUtensorMap* maps = static_cast<const CUtensorMap*>(buf);
-  for (int l = 0; l < L; ++l) {
-    const qb_layer_weights& w = c->layers[l];
-    const int base = 5 * l;        // phase index of this layer's QKV
-    const int prev_down = base - 1;  // -1 for layer 0: the embedding row
-    StepPhase p;
-    std::memset(&p, 0, sizeof(p));
-    p.kind = PH_STORE;  // RMSNorm + QKV (layer 0: embedding row, kept as the residual stream)
-    p.K = g.hidden;
-    p.rows = nqkv;
-    p.w = static_cast<const bf16*>(w.qkv);
-    p.x_from = l == 0 ? -1 : prev_down;
-    p.x = c->w_xa;
-    p.x_copy = l == 0 ? c->w_xa : nullptr;
-    p.gain = static_cast<const bf16*>(w.input_norm);
-    p.out = c->w_qkv;
-    ph.push_back(p);
-    std::memset(&p, 0, sizeof(p));
-    p.kind = PH_ATTN;  // reads the QKV words of phase base
-    p.x_from = base;
-    p.x = c->w_qkv;
-    p.out = c->w_attn;
-    p.q_norm = static_cast<const bf16*>(w.q_norm);
-    p.k_norm = static_cast<const bf16*>(w.k_norm);
-    const size_t off = (size_t)l * g.n_kv_heads * c->cap * D;
-    p.k_cache = c->kc + off;
-    p.v_cache = c->vc + off;
-    p.tmk = maps + 2 * l;
-    p.tmv = maps + 2 * l + 1;
-    ph.push_back(p);
-    std::memset(&p, 0, sizeof(p));
-    p.kind = PH_RESIDUAL;  // xb = xa + O . attn
-    p.K = g.n_heads * D;
-    p.rows = g.hidden;
-    p.w = static_cast<const bf16*>(w.o);
-    p.x_from = base + 1;
-    p.x = c->w_attn;
-    p.residual = c->w_xa;
-    p.res_from = l == 0 ? 0 : prev_down;
-    p.out = c->w_xb;
-    ph.push_back(p);
-    std::memset(&p, 0, sizeof(p));
-    p.kind = PH_SWIGLU;  // act = SwiGLU(RMSNorm(xb) . Wgu^T)
-    p.K = g.hidden;
-    p.rows = 2 * g.ffn;
-    p.w = static_cast<const bf16*>(w.gate_up);
-    p.x_from = base + 2;
-    p.x = c->w_xb;
-    p.gain = static_cast<const bf16*>(w.post_norm);
-    p.out = c->w_act;
-    ph.push_back(p);
-    std::memset(&p, 0, sizeof(p));
-    p.kind = PH_RESIDUAL;  // xa = xb + Down . act
-    p.K = g.ffn;
-    p.rows = g.hidden;
-    p.w = static_cast<const bf16*>(w.down);
-    p.x_from = base + 3;
-    p.x = c->w_act;
-    p.residual = c->w_xb;
-    p.res_from = base + 2;
-    p.out = c->w_xa;
-    ph.push_back(p);
-  }
-  StepPhase p;
-  std::memset(&p, 0, sizeof(p));
-  p.kind = PH_ARGMAX;
-  p.K = g.hidden;
-  p.rows = g.vocab;
-  p.w = c->lm_head;
-  p.x_from = 5 * L - 1;
-  p.x = c->w_xa;
-  p.gain = c->final_norm;
-  ph.push_back(p);
-  std::vector<CUtensorMap> hm(2 * L);
-  for (int l = 0; l < L; ++l) {
-    hm[2 * l] = c->tmk[l];
-    hm[2 * l + 1] = c->tmv[l];
-  }
-  if (cudaMemcpy(buf, hm.data(), hm.size() * sizeof(CUtensorMap), cudaMemcpyHostToDevice) != cudaSuccess ||
-      cudaMemcpy(static_cast<uint8_t*>(buf) + maps_bytes, ph.data(), ph.size() * sizeof(StepPhase),
-                 cudaMemcpyHostToDevice) != cudaSuccess) {
-    cudaGetLastError();
-    cudaFree(buf);
-    return off("descriptor copy");
-  }
-  c->step_buf = buf;
-  c->step_phases = reinterpret_cast<const StepPhase*>(static_cast<uint8_t*>(buf) + maps_bytes);
-  c->step_nphases = (int)ph.size();
-  c->step_xs = xs;
-  c->step_rows = max_rows;
-  c->step_splits = std::max(1, std::min(kStepMaxSplits, G / g.n_kv_heads));
-  c->step_smem = smem;
-  c->step_ready = true;
-}
-
-// One decode step (every layer + greedy head) as one cooperative launch.
-cudaError_t launch_step(qb_ctx* c, const int64_t* tok_in, int64_t* tok_out, int64_t* pos, void* logits,
-                        cudaStream_t st) {
-  const qb_config& g = c->lc;
-  StepArgs a;
-  std::memset(&a, 0, sizeof(a));
-  a.phases = c->step_phases;
-  a.n_phases = c->step_nphases;
-  a.Hq = g.n_heads;
-  a.Hkv = g.n_kv_heads;
-  a.cap = c->cap;
-  a.vocab = c->cfg.vocab;
-  a.max_splits = c->step_splits;
-  a.xs_bytes = c->step_xs;
-  a.max_rows = c->step_rows;
-  a.eps = g.rms_eps;
-  a.token = tok_in;
-  a.token_out = tok_out;
-  a.pos = pos;
-  a.embed = c->embed;
-  a.cos = c->cos;
-  a.sin = c->sin;
-  a.epoch = c->step_epoch;
-  a.part_o = c->w_part_o;
-  a.part_lse = c->w_part_lse;
-  a.head_ticket = c->counters + 192;
-  a.head_val = c->head_val;
-  a.head_idx = c->head_idx;
-  a.logits = static_cast<bf16*>(logits);
-  a.err = c->err;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(c->sm_count);
-  cfg.blockDim = dim3(kStepThreads);
-  cfg.dynamicSmemBytes = c->step_smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, step_kernel, a);
-}
 
 template <int EPI>
 cudaError_t launch_rows(const RowsArgs& a, int sm_count, cudaStream_t st) {
@@ -1617,11 +1402,6 @@ int qb_create(const qb_config* cfg, int device, int tp_rank, int tp_size, qb_ctx
   c->tp_size = tp_size;
   c->sm_count = sm_count_of(device);
   c->splits = attn_splits_for(lc.n_kv_heads, c->sm_count);
-  // The persistent step kernel is opt-in: on 8B at context 4096 it measures
-  // 3.1 ms per step against 2.88 ms for the per-sublayer launches (its
-  // grid-wide handoffs cost more than kernel boundaries do).
-  const char* sk = std::getenv("QB_STEP_KERNEL");
-  c->step_allowed = (sk && sk[0] == '1');
   *out = c;
   return QB_OK;
 }
@@ -1632,7 +1412,6 @@ int qb_destroy(qb_ctx* c) {
   if (c->graph) cudaGraphDestroy(c->graph);
   if (c->vexec) cudaGraphExecDestroy(c->vexec);
   if (c->vgraph) cudaGraphDestroy(c->vgraph);
-  release_step(c);
   if (c->p2p) {
     cudaSetDevice(c->device);
     for (int r = 0; r < c->tp_size; ++r)
@@ -1661,7 +1440,6 @@ int qb_bind_weights(qb_ctx* c, const qb_layer_weights* layers, int n_layers, con
   c->final_norm = static_cast<const bf16*>(final_norm);
   c->lm_head = static_cast<const bf16*>(lm_head);
   c->weights_bound = true;
-  prepare_step(c);
   return QB_OK;
 }
 
@@ -1701,14 +1479,6 @@ int qb_bind_state(qb_ctx* c, void* k_cache, void* v_cache, int capacity, const v
   c->part_o = reinterpret_cast<float*>(c->ws + L.part_o);
   c->y32 = reinterpret_cast<float*>(c->ws + L.y32);
   c->pairs = reinterpret_cast<float*>(c->ws + L.pairs);
-  c->w_xa = reinterpret_cast<uint32_t*>(c->ws + L.w_xa);
-  c->w_xb = reinterpret_cast<uint32_t*>(c->ws + L.w_xb);
-  c->w_qkv = reinterpret_cast<uint32_t*>(c->ws + L.w_qkv);
-  c->w_attn = reinterpret_cast<uint32_t*>(c->ws + L.w_attn);
-  c->w_act = reinterpret_cast<uint32_t*>(c->ws + L.w_act);
-  c->w_part_o = reinterpret_cast<unsigned long long*>(c->ws + L.w_part_o);
-  c->w_part_lse = reinterpret_cast<unsigned long long*>(c->ws + L.w_part_lse);
-  c->step_epoch = reinterpret_cast<unsigned*>(c->ws + L.err + 64);
   c->r_xa = reinterpret_cast<bf16*>(c->ws + L.r_xa);
   c->r_xb = reinterpret_cast<bf16*>(c->ws + L.r_xb);
   c->r_qkv = reinterpret_cast<bf16*>(c->ws + L.r_qkv);
@@ -1739,7 +1509,6 @@ int qb_bind_state(qb_ctx* c, void* k_cache, void* v_cache, int capacity, const v
   }
   drop_graphs(c);
   c->state_bound = true;
-  prepare_step(c);
   return QB_OK;
 }
 
@@ -1826,7 +1595,6 @@ int qb_set_batch(qb_ctx* c, int batch) {
     c->batch = batch;
     c->state_bound = false;  // the cache layout changed: bind the state again
     drop_graphs(c);
-    release_step(c);
   }
   return QB_OK;
 }
@@ -1894,32 +1662,23 @@ int qb_capture_decode(qb_ctx* c, int64_t* token, int64_t* position, void* logits
     cudaGraphDestroy(c->graph);
     c->graph = nullptr;
   }
-  // First with the persistent step kernel; if its cooperative launch cannot be
-  // captured or instantiated, again with the per-sublayer launches.
-  for (int attempt = 0; attempt < 2; ++attempt) {
-    const bool with_step = c->step_ready;
-    cudaError_t e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
-    if (e != cudaSuccess) return cuda_fail(&c->msg, e, "begin capture");
-    rc = c->batch > 1 ? run_batch_pass(c, token, position, token, logits_out, true, st)
-                      : run_rows_decode(c, token, token, position, logits_out, true, st);
-    cudaGraph_t graph = nullptr;
-    e = cudaStreamEndCapture(st, &graph);
-    if (rc == QB_OK && e == cudaSuccess) {
-      e = cudaGraphInstantiate(&c->exec, graph, 0);
-      if (e == cudaSuccess) {
-        c->graph = graph;
-        return QB_OK;
-      }
+  cudaError_t e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+  if (e != cudaSuccess) return cuda_fail(&c->msg, e, "begin capture");
+  rc = c->batch > 1 ? run_batch_pass(c, token, position, token, logits_out, true, st)
+                    : run_rows_decode(c, token, token, position, logits_out, true, st);
+  cudaGraph_t graph = nullptr;
+  e = cudaStreamEndCapture(st, &graph);
+  if (rc == QB_OK && e == cudaSuccess) {
+    e = cudaGraphInstantiate(&c->exec, graph, 0);
+    if (e == cudaSuccess) {
+      c->graph = graph;
+      return QB_OK;
     }
-    if (graph) cudaGraphDestroy(graph);
-    cudaGetLastError();
-    if (!with_step) {
-      if (rc) return rc;
-      return cuda_fail(&c->msg, e, "decode graph capture");
-    }
-    c->step_ready = false;  // fall back to the per-sublayer launches
   }
-  return set_err(&c->msg, QB_ERR_CUDA, "decode graph capture failed");
+  if (graph) cudaGraphDestroy(graph);
+  cudaGetLastError();
+  if (rc) return rc;
+  return cuda_fail(&c->msg, e, "decode graph capture");
 }
 
 int qb_replay_decode(qb_ctx* c, void* stream) {
@@ -2002,11 +1761,6 @@ int qb_check(qb_ctx* c, void* stream) {
     // mid-count: restore them so the next step starts clean.
     cudaError_t e = cudaMemset(c->counters, 0, 4096);
     if (e != cudaSuccess) return cuda_fail(&c->msg, e, "counter reset");
-    // Words written by the abandoned step carry its tag: move to a new one.
-    unsigned ep = 0;
-    if ((e = cudaMemcpy(&ep, c->step_epoch, sizeof(ep), cudaMemcpyDeviceToHost)) != cudaSuccess ||
-        (ep += 1, (e = cudaMemcpy(c->step_epoch, &ep, sizeof(ep), cudaMemcpyHostToDevice)) != cudaSuccess))
-      return cuda_fail(&c->msg, e, "step epoch advance");
   }
   return rc;
 }
@@ -2025,11 +1779,6 @@ int qb_gemm_bf16(const void* x, const void* w, void* out, const void* residual, 
                                       static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(nullptr, e, "gemm launch");
   return QB_OK;
-}
-
-int qb_decode_mode(const qb_ctx* c) {
-  if (!c) return -1;
-  return c->step_ready ? 1 : 0;
 }
 
 int qb_set_trace(qb_ctx* c, void* buffer, size_t bytes) {

@@ -268,12 +268,6 @@ class DecodeState:
         self.position.add_(len(emitted))
         return emitted
 
-    @property
-    def decode_mode(self) -> str:
-        """``"per-sublayer"`` (default) or ``"step-kernel"`` (one persistent
-        launch per step; ``QB_STEP_KERNEL=1`` when the engine is created)."""
-        return "step-kernel" if _lib.load().qb_decode_mode(self.engine.ctx) == 1 else "per-sublayer"
-
     def _ensure_bound(self):
         if self.engine._bound_state is not self:
             raise RuntimeError("this DecodeState is no longer bound to its engine")

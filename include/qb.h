@@ -173,15 +173,6 @@ int qb_replay_verify(qb_ctx* ctx, void* stream);
  * up, out-of-range token ids). Clears the device error word. */
 int qb_check(qb_ctx* ctx, void* stream);
 
-/* How decode steps of this context run (a diagnostic; the reference has one
- * path): 0 = one launch per sublayer (the default), 1 = one persistent
- * cooperative kernel per step (single GPU, opt-in with QB_STEP_KERNEL=1 in the
- * environment when the context is created; prefill rows and tensor-parallel
- * contexts always use 0). Known after qb_bind_weights and qb_bind_state; a
- * capture that cannot record the cooperative launch switches the context to
- * 0. Returns -1 for NULL. */
-int qb_decode_mode(const qb_ctx* ctx);
-
 /* Tracing (diagnostics; the reference's profiling is external, e.g. the timing
  * harness of dryft/experiments): give the context a device buffer (8-byte
  * aligned, zero-filled by the caller) and every launch of the decode steps

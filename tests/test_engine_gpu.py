@@ -18,28 +18,12 @@ def _bits_to_bf16(a):
     return torch.from_numpy(a.astype(np.int16)).view(torch.bfloat16)
 
 
-def _with_mode(mode, make):
-    """Create an engine with the decode path chosen by QB_STEP_KERNEL (read
-    when the context is created)."""
-    old = os.environ.get("QB_STEP_KERNEL")
-    os.environ["QB_STEP_KERNEL"] = "1" if mode == "step-kernel" else "0"
-    try:
-        return make()
-    finally:
-        if old is None:
-            del os.environ["QB_STEP_KERNEL"]
-        else:
-            os.environ["QB_STEP_KERNEL"] = old
-
-
-@pytest.fixture(scope="module", params=["step-kernel", "per-sublayer"])
-def small_engine(built_lib, request):
+@pytest.fixture(scope="module")
+def small_engine(built_lib):
     from hackthenorth_b200.config import QWEN3_SMALL
     from hackthenorth_b200.engine import Engine
 
-    engine = _with_mode(request.param, lambda: Engine.from_random(QWEN3_SMALL, seed=0))
-    engine.expected_mode = request.param
-    return engine
+    return Engine.from_random(QWEN3_SMALL, seed=0)
 
 
 def _teacher_forced(engine, prompt, tokens, keep_logits=True):
@@ -60,7 +44,6 @@ def test_small_engine_matches_golden_tokens_and_logits(small_engine):
     prompt, gold = g["prompt"].tolist(), g["tokens"].tolist()
     out = [s[0] for s in small_engine.generate([prompt], len(gold))]
     assert out == gold
-    assert small_engine.state.decode_mode == small_engine.expected_mode
     got = _teacher_forced(small_engine, prompt, gold)
     ref = _bits_to_bf16(g["logits_bf16"]).float()
     assert (got - ref).abs().max() <= LOGIT_ATOL
@@ -188,19 +171,17 @@ def test_0p6b_engine_matches_native_greedy_128(built_lib, cpu_threads, golden):
 
 
 @pytest.mark.parametrize("context,capacity", [(200, None), (4096, None), (9000, None), (3000, 16384)])
-def test_step_kernel_and_per_sublayer_launches_match_oracle(built_lib, cpu_threads, context, capacity):
+def test_decode_step_matches_oracle(built_lib, cpu_threads, context, capacity):
     """One Qwen3-8B-shaped layer (full vocabulary) over a seeded N(0, 1) cache
-    prefix: the persistent step kernel and the per-sublayer launches each
-    match the CPU oracle's logits within LOGIT_ATOL (mean difference below
-    0.01) and agree with each other as closely; the greedy token matches the
-    oracle's unless the oracle holds a near tie; the appended K/V rows match
-    within bf16 rounding of the projection.
-    Context 200 runs one attention split per KV head, 4096 about 17 (merged
-    through global memory by the last split in the step kernel, through
-    distributed shared memory in the per-sublayer path). A capacity above 8192
-    gives the per-sublayer path several clusters per KV head (four clusters of
-    four CTAs on a B200), merged across clusters by the last-arriving CTA of
-    each dim slice: context 9000 uses all of them, context 3000 two (8 splits)."""
+    prefix: the decode step's logits match the CPU oracle's within LOGIT_ATOL
+    (mean difference below 0.01); the greedy token matches the oracle's unless
+    the oracle holds a near tie; the appended K/V rows match within bf16
+    rounding of the projection.
+    Context 200 runs one attention split per KV head, 4096 several (merged
+    through distributed shared memory). A capacity above 8192 gives several
+    clusters per KV head (four clusters of four CTAs on a B200), merged across
+    clusters by the last-arriving CTA of each dim slice: context 9000 uses all
+    of them, context 3000 two (8 splits)."""
     import dataclasses
 
     from hackthenorth_b200.config import QWEN3_8B
@@ -218,31 +199,27 @@ def test_step_kernel_and_per_sublayer_launches_match_oracle(built_lib, cpu_threa
     o.values[:, :, :context] = vp
     ref, ref_tok = o.forward_rows([17], context)
     ref = ref[0].float()
-    got = {}
-    for mode in ("step-kernel", "per-sublayer"):
-        engine = _with_mode(mode, lambda: Engine(None, "cuda:0", cfg=cfg, state=state))
-        st = engine.new_state(context, 4, keep_logits=True, capacity=capacity)
-        assert st.decode_mode == mode
-        st.keys[:, :, :context] = kp.to(engine.device)
-        st.values[:, :, :context] = vp.to(engine.device)
-        st.token.fill_(17)
-        st.position.fill_(context)
-        st.step()
-        st.check()
-        got[mode] = st.logits.float().cpu()
-        assert int(st.position.item()) == context + 1
-        torch.testing.assert_close(st.keys[0, :, context].float().cpu(), o.keys[0, :, context].float(),
-                                   atol=0.0625, rtol=0.02)
-        torch.testing.assert_close(st.values[0, :, context].float().cpu(), o.values[0, :, context].float(),
-                                   atol=0.0625, rtol=0.02)
-        top2 = ref.topk(2).values
-        if int(st.token.item()) != int(ref_tok[0]):
-            assert float(top2[0] - top2[1]) <= LOGIT_ATOL
-        del st, engine
-        torch.cuda.empty_cache()
-    for a, b in ((got["step-kernel"], ref), (got["per-sublayer"], ref), (got["step-kernel"], got["per-sublayer"])):
-        d = (a - b).abs()
-        assert d.max() <= LOGIT_ATOL and d.mean() <= 0.01, (float(d.max()), float(d.mean()))
+    engine = Engine(None, "cuda:0", cfg=cfg, state=state)
+    st = engine.new_state(context, 4, keep_logits=True, capacity=capacity)
+    st.keys[:, :, :context] = kp.to(engine.device)
+    st.values[:, :, :context] = vp.to(engine.device)
+    st.token.fill_(17)
+    st.position.fill_(context)
+    st.step()
+    st.check()
+    got = st.logits.float().cpu()
+    assert int(st.position.item()) == context + 1
+    torch.testing.assert_close(st.keys[0, :, context].float().cpu(), o.keys[0, :, context].float(),
+                               atol=0.0625, rtol=0.02)
+    torch.testing.assert_close(st.values[0, :, context].float().cpu(), o.values[0, :, context].float(),
+                               atol=0.0625, rtol=0.02)
+    top2 = ref.topk(2).values
+    if int(st.token.item()) != int(ref_tok[0]):
+        assert float(top2[0] - top2[1]) <= LOGIT_ATOL
+    d = (got - ref).abs()
+    assert d.max() <= LOGIT_ATOL and d.mean() <= 0.01, (float(d.max()), float(d.mean()))
+    del st, engine
+    torch.cuda.empty_cache()
 
 
 def test_4b_shape_prefill_and_decode_match_oracle(built_lib, cpu_threads):
