@@ -28,6 +28,7 @@
 #include "verify_attention.cuh"
 #include "prefill_gemm.cuh"
 #include "prefill_attention.cuh"
+#include "prefill_attention_tc.cuh"
 #include "common.cuh"
 #include "gemv.cuh"
 
@@ -90,6 +91,7 @@ struct DeviceCache {
   bool pg_attr[3] = {};
   bool attn_attr[2][2] = {};  // [MT - 1][PRO]
   bool rows_attr[5] = {};
+  bool ft_attr = false;
   bool fp_attr = false;
   // attn_decode_kernel: cluster size for (hkv, rows) and clusters of 16/8/4 CTAs held at once
   int dec_hkv = -1, dec_rows = -1, dec_cs = 0;
@@ -279,6 +281,31 @@ bool make_rows_map(CUtensorMap* m, const void* base, long long rows, long long c
 }
 
 // D[T][N] = X[T][K] . W[N][K]^T on tcgen05 (prefill_gemm_kernel).
+// 3D map over the prompt rows' queries q[T][Hq][128] (dims innermost): boxes of
+// [rows][G heads][64 dims] (128-byte swizzle) for flash_prefill_tc_kernel.
+bool make_q3_map(CUtensorMap* m, const void* q, int T, int Hq, int G, int rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || (reinterpret_cast<uintptr_t>(q) & 15) != 0) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)kAttnD, (cuuint64_t)Hq, (cuuint64_t)T};
+  cuuint64_t strides[2] = {(cuuint64_t)kAttnD * 2, (cuuint64_t)Hq * kAttnD * 2};
+  cuuint32_t box[3] = {64, (cuuint32_t)G, (cuuint32_t)rows};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Prefill attention on tcgen05 (prefill_attention_tc.cuh); QB_FP_TC=0 keeps
+// the mma.sync flash_prefill_kernel.
+bool fp_tc_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("QB_FP_TC");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 cudaError_t launch_prefill_gemm(int epi, const bf16* x, const bf16* w, bf16* out, const bf16* residual, int T, int N,
                                 int K, int* err, cudaStream_t st) {
   CUtensorMap tx, tw;
@@ -1285,16 +1312,41 @@ int run_prefill_batched(qb_ctx* c, const int64_t* ids, int n, uint8_t* scratch, 
     fa.Hkv = g.n_kv_heads;
     fa.cap = c->cap;
     fa.err = c->err;
-    bool& fp_attr = dev_cache().fp_attr;
-    if (!fp_attr) {
-      if ((e = cudaFuncSetAttribute(flash_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    (int)fp_smem_bytes())) != cudaSuccess)
-        return cuda_fail(&c->msg, e, "prefill attention attribute");
-      fp_attr = true;
+    const int G = g.n_heads / g.n_kv_heads;
+    CUtensorMap tq;
+    if (fp_tc_enabled() && kFtRowsQ % (2 * G) == 0 && make_q3_map(&tq, q, n, g.n_heads, G, kFtRowsQ / G / 2)) {
+      // 256 query rows (256 / G prompt rows x G heads) per CTA on tcgen05
+      bool& ft_attr = dev_cache().ft_attr;
+      if (!ft_attr) {
+        if ((e = cudaFuncSetAttribute(flash_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)ft_smem_bytes())) != cudaSuccess)
+          return cuda_fail(&c->msg, e, "prefill attention attribute");
+        ft_attr = true;
+      }
+      FtArgs ft;
+      ft.out = attn;
+      ft.T = n;
+      ft.p0 = 0;
+      ft.Hq = g.n_heads;
+      ft.Hkv = g.n_kv_heads;
+      ft.cap = c->cap;
+      ft.err = c->err;
+      const int rows = kFtRowsQ / G;
+      if ((e = launch_ex(flash_prefill_tc_kernel, dim3((n + rows - 1) / rows, g.n_kv_heads), dim3(kFtThreads),
+                         ft_smem_bytes(), st, tq, c->tmk[l], c->tmv[l], ft)) != cudaSuccess)
+        return cuda_fail(&c->msg, e, "prefill attention");
+    } else {
+      bool& fp_attr = dev_cache().fp_attr;
+      if (!fp_attr) {
+        if ((e = cudaFuncSetAttribute(flash_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)fp_smem_bytes())) != cudaSuccess)
+          return cuda_fail(&c->msg, e, "prefill attention attribute");
+        fp_attr = true;
+      }
+      if ((e = launch_ex(flash_prefill_kernel, dim3((n + kFpRows - 1) / kFpRows, g.n_heads), dim3(kFpThreads),
+                         fp_smem_bytes(), st, c->tmk[l], c->tmv[l], fa)) != cudaSuccess)
+        return cuda_fail(&c->msg, e, "prefill attention");
     }
-    if ((e = launch_ex(flash_prefill_kernel, dim3((n + kFpRows - 1) / kFpRows, g.n_heads), dim3(kFpThreads),
-                       fp_smem_bytes(), st, c->tmk[l], c->tmv[l], fa)) != cudaSuccess)
-      return cuda_fail(&c->msg, e, "prefill attention");
     if ((e = launch_prefill_gemm(PG_RESIDUAL, attn, static_cast<const bf16*>(w.o), xb, xa, n, H, g.n_heads * D,
                                  c->err, st)) != cudaSuccess)
       return cuda_fail(&c->msg, e, "prefill o");
