@@ -10,7 +10,8 @@
 // rescaled only when a row's maximum grows by more than 8 (P then stays below
 // 2^8), which changes P's rounding point but not its relative precision.
 //
-// CTA = (256 / G prompt rows, KV head g): its 256 query rows (each prompt row
+// CTA = (256 / G prompt rows, KV head g) (1D grid, the longest causal row
+// blocks first): its 256 query rows (each prompt row
 // with the G query heads of g, in two M = 128 tiles) share one stream of g's
 // keys and values, so every K/V byte is fetched once per 256 query rows.
 //  * warp 0, one lane: TMA. Q tiles [prompt rows][G heads][64 dims] x 2 halves
@@ -133,8 +134,12 @@ __global__ void __launch_bounds__(kFtThreads, 1)
   const int lane = threadIdx.x & 31;
   const int G = a.Hq / a.Hkv;
   const int RH = (kFtRowsQ / G) / 2;  // prompt rows per M tile
-  const int g = blockIdx.y;
-  const int r0 = blockIdx.x * 2 * RH;
+  // Grid = row blocks x KV heads, row blocks in descending order (KV head
+  // fastest): the causal blocks with the most keys start first and the short
+  // ones fill the last wave.
+  const int g = blockIdx.x % a.Hkv;
+  const int nrb = gridDim.x / a.Hkv;
+  const int r0 = (nrb - 1 - (int)(blockIdx.x / a.Hkv)) * 2 * RH;
   int nkb[2], pm[2];
 #pragma unroll
   for (int t = 0; t < 2; ++t) {

@@ -1332,7 +1332,7 @@ int run_prefill_batched(qb_ctx* c, const int64_t* ids, int n, uint8_t* scratch, 
       ft.cap = c->cap;
       ft.err = c->err;
       const int rows = kFtRowsQ / G;
-      if ((e = launch_ex(flash_prefill_tc_kernel, dim3((n + rows - 1) / rows, g.n_kv_heads), dim3(kFtThreads),
+      if ((e = launch_ex(flash_prefill_tc_kernel, dim3(((n + rows - 1) / rows) * g.n_kv_heads), dim3(kFtThreads),
                          ft_smem_bytes(), st, tq, c->tmk[l], c->tmv[l], ft)) != cudaSuccess)
         return cuda_fail(&c->msg, e, "prefill attention");
     } else {
