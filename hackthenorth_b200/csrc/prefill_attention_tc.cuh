@@ -94,6 +94,27 @@ __device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
+// 64 consecutive fp32 columns of this warp's 32 TMEM lanes, one load and one wait.
+__device__ __forceinline__ void tc_ld64(uint32_t taddr, float (&v)[64]) {
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, "
+      "%38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, "
+      "%60, %61, %62, %63}, [%64];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]),
+        "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]),
+        "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]),
+        "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]),
+        "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
+}
 __device__ __forceinline__ void tc_st32(uint32_t taddr, const float (&v)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
@@ -302,30 +323,20 @@ __global__ void __launch_bounds__(kFtThreads, 1)
       if (!ok) break;
       tc_fence_after();
       float sv[64];
-      {
-        float h0[32], h1[32];
-        tc_ld32(tmem + lanebase + (uint32_t)(t * kFtKeys), h0);
-        tc_ld32(tmem + lanebase + (uint32_t)(t * kFtKeys + 32), h1);
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          sv[c] = h0[c];
-          sv[32 + c] = h1[c];
-        }
-      }
+      tc_ld64(tmem + lanebase + (uint32_t)(t * kFtKeys), sv);
       // Keys beyond the row's position: only on the tiles that reach past it.
-      float rmax = -INFINITY;
-      if (__all_sync(0xffffffffu, (long long)j * kFtKeys + kFtKeys - 1 <= pos)) {
-#pragma unroll
-        for (int c = 0; c < 64; ++c) rmax = fmaxf(rmax, sv[c]);
-      } else {
+      if (!__all_sync(0xffffffffu, (long long)j * kFtKeys + kFtKeys - 1 <= pos)) {
         const long long lim = pos - (long long)j * kFtKeys + 1;  // keys [0, lim) of the tile are visible
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          sv[c] = c < lim ? sv[c] : -INFINITY;  // also clears NaN of keys past the prompt
-          rmax = fmaxf(rmax, sv[c]);
-        }
+        for (int c = 0; c < 64; ++c) sv[c] = c < lim ? sv[c] : -INFINITY;  // also clears NaN of keys past the prompt
       }
-      rmax *= scale;
+      // row maximum with 8 independent chains
+      float mx[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) mx[e] = sv[e];
+#pragma unroll
+      for (int c = 8; c < 64; ++c) mx[c & 7] = fmaxf(mx[c & 7], sv[c]);
+      const float rmax = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7]))) * scale;
       const float m_new = fmaxf(m_ref, rmax);
       if (j > 0) {
         // O_t and the P_t buffer are free once the previous P.V has completed
@@ -353,7 +364,9 @@ __global__ void __launch_bounds__(kFtThreads, 1)
       // p = 2^(s * scale - m), one FMA and one ex2 per score (masked scores are
       // -inf and give 0; a row with nothing visible yet uses m = 0).
       const float mu = m_ref == -INFINITY ? 0.f : m_ref;
-      float rs = 0.f;
+      float rsum[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) rsum[e] = 0.f;
 #pragma unroll
       for (int ch = 0; ch < 8; ++ch) {
         uint32_t w[4];
@@ -361,12 +374,13 @@ __global__ void __launch_bounds__(kFtThreads, 1)
         for (int e = 0; e < 4; ++e) {
           const float p0 = ex2_approx(fmaf(sv[8 * ch + 2 * e], scale, -mu));
           const float p1 = ex2_approx(fmaf(sv[8 * ch + 2 * e + 1], scale, -mu));
-          rs += p0 + p1;
+          rsum[2 * e] += p0;
+          rsum[2 * e + 1] += p1;
           w[e] = pack_bf16(p0, p1);
         }
         *reinterpret_cast<uint4*>(pt + qrow * 128 + ((ch ^ (qrow & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
-      l += rs;
+      l += ((rsum[0] + rsum[1]) + (rsum[2] + rsum[3])) + ((rsum[4] + rsum[5]) + (rsum[6] + rsum[7]));
       if (j == nk - 1 && (long long)(j + 1) * kFtKeys - 1 > pmax) {
         // Keys past the CTA's last position may hold anything (even NaN):
         // their P is 0, but 0 * NaN is NaN, so clear those V rows first.
