@@ -1,9 +1,9 @@
 // prefill_attention_tc.cuh — causal GQA flash attention for a block of prompt
 // rows on sm_100a's tcgen05 tensor cores (the prefill attention).
 //
-// Same math as flash_prefill_kernel (prefill_attention.cuh; reference: SDPA's
-// causal flash attention for prompt rows, dryft/engine/attention.py:92-98, with
-// the decode path's numerics, dryft/engine/kernels/attention.py:49-57): scores
+// The reference runs prompt attention through SDPA's flash kernel with a
+// causal mask (dryft/engine/attention.py:92-98); this kernel keeps the decode
+// path's numerics (dryft/engine/kernels/attention.py:49-57): scores
 // scaled by 1/sqrt(128) in base 2, masked to keys <= the row's position, fp32
 // softmax statistics, P rounded to bf16 before P.V, fp32 accumulation, one
 // bf16 rounding of O / l. The running maximum is kept lazily: O and l are

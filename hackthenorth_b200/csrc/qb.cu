@@ -92,7 +92,6 @@ struct DeviceCache {
   bool attn_attr[2][2] = {};  // [MT - 1][PRO]
   bool rows_attr[5] = {};
   bool ft_attr = false;
-  bool fp_attr = false;
   // attn_decode_kernel: cluster size for (hkv, rows) and clusters of 16/8/4 CTAs held at once
   int dec_hkv = -1, dec_rows = -1, dec_cs = 0;
   int dec_active[3] = {0, 0, 0};
@@ -293,17 +292,6 @@ bool make_q3_map(CUtensorMap* m, const void* q, int T, int Hq, int G, int rows) 
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-// Prefill attention on tcgen05 (prefill_attention_tc.cuh); QB_FP_TC=0 keeps
-// the mma.sync flash_prefill_kernel.
-bool fp_tc_enabled() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = std::getenv("QB_FP_TC");
-    v = (e && e[0] == '0') ? 0 : 1;
-  }
-  return v == 1;
 }
 
 cudaError_t launch_prefill_gemm(int epi, const bf16* x, const bf16* w, bf16* out, const bf16* residual, int T, int N,
@@ -1303,18 +1291,11 @@ int run_prefill_batched(qb_ctx* c, const int64_t* ids, int n, uint8_t* scratch, 
     const long long warps = (long long)n * (g.n_heads + 2 * g.n_kv_heads);
     if ((e = launch_ex(rope_rows_kernel, dim3((unsigned)((warps + 3) / 4)), dim3(128), 0, st, ra)) != cudaSuccess)
       return cuda_fail(&c->msg, e, "prefill rope");
-    FpArgs fa;
-    fa.q = q;
-    fa.out = attn;
-    fa.T = n;
-    fa.p0 = 0;
-    fa.Hq = g.n_heads;
-    fa.Hkv = g.n_kv_heads;
-    fa.cap = c->cap;
-    fa.err = c->err;
     const int G = g.n_heads / g.n_kv_heads;
     CUtensorMap tq;
-    if (fp_tc_enabled() && kFtRowsQ % (2 * G) == 0 && make_q3_map(&tq, q, n, g.n_heads, G, kFtRowsQ / G / 2)) {
+    if (kFtRowsQ % (2 * G) != 0 || !make_q3_map(&tq, q, n, g.n_heads, G, kFtRowsQ / G / 2))
+      return set_err(&c->msg, QB_ERR_UNSUPPORTED, "prefill attention: query map");
+    {
       // 256 query rows (256 / G prompt rows x G heads) per CTA on tcgen05
       bool& ft_attr = dev_cache().ft_attr;
       if (!ft_attr) {
@@ -1334,17 +1315,6 @@ int run_prefill_batched(qb_ctx* c, const int64_t* ids, int n, uint8_t* scratch, 
       const int rows = kFtRowsQ / G;
       if ((e = launch_ex(flash_prefill_tc_kernel, dim3(((n + rows - 1) / rows) * g.n_kv_heads), dim3(kFtThreads),
                          ft_smem_bytes(), st, tq, c->tmk[l], c->tmv[l], ft)) != cudaSuccess)
-        return cuda_fail(&c->msg, e, "prefill attention");
-    } else {
-      bool& fp_attr = dev_cache().fp_attr;
-      if (!fp_attr) {
-        if ((e = cudaFuncSetAttribute(flash_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)fp_smem_bytes())) != cudaSuccess)
-          return cuda_fail(&c->msg, e, "prefill attention attribute");
-        fp_attr = true;
-      }
-      if ((e = launch_ex(flash_prefill_kernel, dim3((n + kFpRows - 1) / kFpRows, g.n_heads), dim3(kFpThreads),
-                         fp_smem_bytes(), st, c->tmk[l], c->tmv[l], fa)) != cudaSuccess)
         return cuda_fail(&c->msg, e, "prefill attention");
     }
     if ((e = launch_prefill_gemm(PG_RESIDUAL, attn, static_cast<const bf16*>(w.o), xb, xa, n, H, g.n_heads * D,
