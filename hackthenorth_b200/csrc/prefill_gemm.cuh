@@ -39,13 +39,25 @@ constexpr int kPgStageBytes = kPgABytes + kPgBBytes;
 constexpr int kPgThreads = 6 * 32;
 constexpr int kPgTmemCols = 256;
 
-enum PrefillEpi : int { PG_STORE = 0, PG_RESIDUAL = 1, PG_SWIGLU = 2 };
+enum PrefillEpi : int { PG_STORE = 0, PG_RESIDUAL = 1, PG_SWIGLU = 2, PG_QKV_ROPE = 3 };
 
 struct PgArgs {
   int T, N, K;              // rows of X, rows of W, shared K
   bf16* out;                // STORE/RESIDUAL: [T][N]; SWIGLU: [T][N/2]
   const bf16* residual;     // RESIDUAL: [T][N]
   int* err;
+  // PG_QKV_ROPE: the QKV projection of prompt rows at positions p0 + row,
+  // finished per head as the decode path does (q/k RMSNorm + RoPE, K/V to the
+  // cache): q_out [T][Hq][128], caches [Hkv][cap][128] of this layer.
+  const bf16* q_norm;
+  const bf16* k_norm;
+  const bf16* cos;          // [cap][128]
+  const bf16* sin;
+  float eps;
+  bf16* q_out;
+  bf16* k_cache;
+  bf16* v_cache;
+  int Hq, Hkv, cap, p0;
 };
 
 __host__ inline size_t pg_smem_bytes() { return 1024 + (size_t)kPgStages * kPgStageBytes + 256; }  // + barriers, TMEM slot
@@ -89,6 +101,107 @@ __device__ __forceinline__ void tc_ld8(uint32_t taddr, float (&v)[8]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// 32 consecutive fp32 columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tc_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// PG_QKV_ROPE epilogue for one 128-column head of one prompt row: the
+// projection rounded to bf16; q and k heads then RMSNorm'd over the head
+// (bf16(bf16(x * inv) * gain)) and rotated (rotate-half RoPE with the cos/sin
+// row of the position, each product rounded, the sum rounded), exactly the
+// rope_rows_kernel arithmetic (dryft/engine/kernels/fused.py:9-30); q goes to
+// q_out, k and v to the cache at the row's position.
+// The TMEM loads are warp-collective: every lane of the warp calls this for the
+// same head; lanes whose row is past T (valid false) only take part in them.
+__device__ __forceinline__ void pg_qkv_rope_head(const PgArgs& a, int row, bool valid, int head, uint32_t taddr) {
+  float x[128];
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    float v[32];
+    tc_ld32(taddr + (uint32_t)(32 * c), v);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) x[32 * c + i] = round_bf16(v[i]);
+  }
+  if (!valid) return;
+  const int pos = a.p0 + row;
+  if (pos < 0 || pos >= a.cap) {
+    report_error(a.err, DEV_BAD_POSITION);
+    return;
+  }
+  bf16* dst;
+  const bf16* gain = nullptr;
+  if (head < a.Hq) {
+    dst = a.q_out + ((size_t)row * a.Hq + head) * 128;
+    gain = a.q_norm;
+  } else if (head < a.Hq + a.Hkv) {
+    dst = a.k_cache + ((size_t)(head - a.Hq) * a.cap + pos) * 128;
+    gain = a.k_norm;
+  } else {
+    dst = a.v_cache + ((size_t)(head - a.Hq - a.Hkv) * a.cap + pos) * 128;
+  }
+  if (gain != nullptr) {
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 128; ++i) ss = fmaf(x[i], x[i], ss);
+    const float inv = 1.0f / sqrtf(ss / 128.0f + a.eps);  // correctly rounded sqrt and division
+#pragma unroll
+    for (int c8 = 0; c8 < 16; ++c8) {
+      const uint4 gv = ldg128_nc(gain + 8 * c8);
+      const uint32_t* pg = reinterpret_cast<const uint32_t*>(&gv);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        x[8 * c8 + 2 * j] = round_bf16(round_bf16(x[8 * c8 + 2 * j] * inv) * bf_lo(pg[j]));
+        x[8 * c8 + 2 * j + 1] = round_bf16(round_bf16(x[8 * c8 + 2 * j + 1] * inv) * bf_hi(pg[j]));
+      }
+    }
+    const bf16* crow = a.cos + (size_t)pos * 128;
+    const bf16* srow = a.sin + (size_t)pos * 128;
+#pragma unroll
+    for (int c8 = 0; c8 < 8; ++c8) {  // dims d in [8 c8, 8 c8 + 8) and their partners d + 64
+      const uint4 clo = ldg128_nc(crow + 8 * c8), chi = ldg128_nc(crow + 64 + 8 * c8);
+      const uint4 slo = ldg128_nc(srow + 8 * c8), shi = ldg128_nc(srow + 64 + 8 * c8);
+      const uint32_t* pcl = reinterpret_cast<const uint32_t*>(&clo);
+      const uint32_t* pch = reinterpret_cast<const uint32_t*>(&chi);
+      const uint32_t* psl = reinterpret_cast<const uint32_t*>(&slo);
+      const uint32_t* psh = reinterpret_cast<const uint32_t*>(&shi);
+      uint32_t olo[4], ohi[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int d0 = 8 * c8 + 2 * j;
+        const float a0 = x[d0], a1 = x[d0 + 1], b0 = x[d0 + 64], b1 = x[d0 + 65];
+        olo[j] = pack_bf16(round_bf16(a0 * bf_lo(pcl[j])) + round_bf16(-b0 * bf_lo(psl[j])),
+                           round_bf16(a1 * bf_hi(pcl[j])) + round_bf16(-b1 * bf_hi(psl[j])));
+        ohi[j] = pack_bf16(round_bf16(b0 * bf_lo(pch[j])) + round_bf16(a0 * bf_lo(psh[j])),
+                           round_bf16(b1 * bf_hi(pch[j])) + round_bf16(a1 * bf_hi(psh[j])));
+      }
+      *reinterpret_cast<uint4*>(dst + 8 * c8) = make_uint4(olo[0], olo[1], olo[2], olo[3]);
+      *reinterpret_cast<uint4*>(dst + 64 + 8 * c8) = make_uint4(ohi[0], ohi[1], ohi[2], ohi[3]);
+    }
+  } else {
+#pragma unroll
+    for (int c8 = 0; c8 < 16; ++c8) {
+      uint4 o;
+      o.x = pack_bf16(x[8 * c8 + 0], x[8 * c8 + 1]);
+      o.y = pack_bf16(x[8 * c8 + 2], x[8 * c8 + 3]);
+      o.z = pack_bf16(x[8 * c8 + 4], x[8 * c8 + 5]);
+      o.w = pack_bf16(x[8 * c8 + 6], x[8 * c8 + 7]);
+      *reinterpret_cast<uint4*>(dst + 8 * c8) = o;
+    }
+  }
 }
 
 template <int EPI>
@@ -250,11 +363,17 @@ __global__ void __launch_bounds__(kPgThreads, 1)
       tc_fence_after();
       if (!ok) break;
       const uint32_t base = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(ab * kPgTmemCols);
-      for (int c = 0; c < kPgBN; c += 8) {
-        float v[8];
-        tc_ld8(base + (uint32_t)c, v);
-        const int n = n0 + c;
-        if (row < a.T && n < a.N) pg_epilogue_store<EPI>(a, row, n, v);
+      if constexpr (EPI == PG_QKV_ROPE) {
+        // the tile's 256 columns are two whole heads (N is a multiple of 128)
+        for (int hh = 0; hh < kPgBN / 128 && n0 + 128 * hh < a.N; ++hh)
+          pg_qkv_rope_head(a, row, row < a.T, n0 / 128 + hh, base + (uint32_t)(128 * hh));
+      } else {
+        for (int c = 0; c < kPgBN; c += 8) {
+          float v[8];
+          tc_ld8(base + (uint32_t)c, v);
+          const int n = n0 + c;
+          if (row < a.T && n < a.N) pg_epilogue_store<EPI>(a, row, n, v);
+        }
       }
       tc_fence_before();
       __syncwarp();

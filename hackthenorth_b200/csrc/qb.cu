@@ -88,7 +88,7 @@ int current_sm_count() {
 constexpr int kMaxDevices = 64;
 struct DeviceCache {
   bool gemv_attr[5] = {};
-  bool pg_attr[3] = {};
+  bool pg_attr[4] = {};
   bool attn_attr[2][2] = {};  // [MT - 1][PRO]
   bool rows_attr[5] = {};
   bool ft_attr = false;
@@ -295,10 +295,12 @@ bool make_q3_map(CUtensorMap* m, const void* q, int T, int Hq, int G, int rows) 
 }
 
 cudaError_t launch_prefill_gemm(int epi, const bf16* x, const bf16* w, bf16* out, const bf16* residual, int T, int N,
-                                int K, int* err, cudaStream_t st) {
+                                int K, int* err, cudaStream_t st, const PgArgs* rope = nullptr) {
   CUtensorMap tx, tw;
   if (!make_rows_map(&tx, x, T, K, kPgBM) || !make_rows_map(&tw, w, N, K, kPgBN)) return cudaErrorInvalidValue;
   PgArgs a;
+  if (rope != nullptr) a = *rope;
+  else std::memset(&a, 0, sizeof(a));
   a.T = T;
   a.N = N;
   a.K = K;
@@ -308,8 +310,10 @@ cudaError_t launch_prefill_gemm(int epi, const bf16* x, const bf16* w, bf16* out
   const size_t smem = pg_smem_bytes();
   bool* attr = dev_cache().pg_attr;
   void (*k)(const CUtensorMap, const CUtensorMap, const PgArgs) =
-      epi == PG_STORE ? prefill_gemm_kernel<PG_STORE> : epi == PG_RESIDUAL ? prefill_gemm_kernel<PG_RESIDUAL>
-                                                                           : prefill_gemm_kernel<PG_SWIGLU>;
+      epi == PG_STORE      ? prefill_gemm_kernel<PG_STORE>
+      : epi == PG_RESIDUAL ? prefill_gemm_kernel<PG_RESIDUAL>
+      : epi == PG_SWIGLU   ? prefill_gemm_kernel<PG_SWIGLU>
+                           : prefill_gemm_kernel<PG_QKV_ROPE>;
   if (!attr[epi]) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
@@ -1265,32 +1269,25 @@ int run_prefill_batched(qb_ctx* c, const int64_t* ids, int n, uint8_t* scratch, 
     const qb_layer_weights& w = c->layers[l];
     if ((e = norm(xa, static_cast<const bf16*>(w.input_norm), l == 0)) != cudaSuccess)
       return cuda_fail(&c->msg, e, "prefill norm");
-    if ((e = launch_prefill_gemm(PG_STORE, xn, static_cast<const bf16*>(w.qkv), qkv, nullptr, n, nqkv, H, c->err,
-                                 st)) != cudaSuccess)
-      return cuda_fail(&c->msg, e, "prefill qkv");
-    RopeRowsArgs ra;
-    std::memset(&ra, 0, sizeof(ra));
-    ra.qkv = qkv;
-    ra.q_norm = static_cast<const bf16*>(w.q_norm);
-    ra.k_norm = static_cast<const bf16*>(w.k_norm);
-    ra.cos = c->cos;
-    ra.sin = c->sin;
-    ra.eps = g.rms_eps;
-    ra.pos = nullptr;
-    ra.p0 = 0;
-    ra.positions = nullptr;
-    ra.q_out = q;
+    // QKV GEMM with the q/k norm + RoPE + K/V append in its epilogue
+    PgArgs qr;
+    std::memset(&qr, 0, sizeof(qr));
+    qr.q_norm = static_cast<const bf16*>(w.q_norm);
+    qr.k_norm = static_cast<const bf16*>(w.k_norm);
+    qr.cos = c->cos;
+    qr.sin = c->sin;
+    qr.eps = g.rms_eps;
+    qr.q_out = q;
     const size_t layer_off = (size_t)l * g.n_kv_heads * c->cap * D;
-    ra.k_cache = c->kc + layer_off;
-    ra.v_cache = c->vc + layer_off;
-    ra.err = c->err;
-    ra.Q = n;
-    ra.Hq = g.n_heads;
-    ra.Hkv = g.n_kv_heads;
-    ra.cap = c->cap;
-    const long long warps = (long long)n * (g.n_heads + 2 * g.n_kv_heads);
-    if ((e = launch_ex(rope_rows_kernel, dim3((unsigned)((warps + 3) / 4)), dim3(128), 0, st, ra)) != cudaSuccess)
-      return cuda_fail(&c->msg, e, "prefill rope");
+    qr.k_cache = c->kc + layer_off;
+    qr.v_cache = c->vc + layer_off;
+    qr.Hq = g.n_heads;
+    qr.Hkv = g.n_kv_heads;
+    qr.cap = c->cap;
+    qr.p0 = 0;
+    if ((e = launch_prefill_gemm(PG_QKV_ROPE, xn, static_cast<const bf16*>(w.qkv), nullptr, nullptr, n, nqkv, H,
+                                 c->err, st, &qr)) != cudaSuccess)
+      return cuda_fail(&c->msg, e, "prefill qkv");
     const int G = g.n_heads / g.n_kv_heads;
     CUtensorMap tq;
     if (kFtRowsQ % (2 * G) != 0 || !make_q3_map(&tq, q, n, g.n_heads, G, kFtRowsQ / G / 2))
