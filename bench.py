@@ -72,13 +72,22 @@ def load_peaks():
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
+    """nvidia-smi samples of this GPU's SM clock, power and throttle reasons
+    every 50 ms. ``start`` returns once the first sample has arrived; ``mark``
+    is called where the timed region begins and ``stop`` waits for one more
+    sample after it ends, so the record is the samples that bracket the timed
+    region (the last one before it, every one inside, the first one after),
+    however short the region is."""
+
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    INTERVAL_MS = 50
 
     def __init__(self, device_index: int):
         self.proc = None
         self.path = None
+        self.first = 0
         try:
             props = torch.cuda.get_device_properties(device_index)
             ident = str(getattr(props, "uuid", ""))
@@ -86,40 +95,63 @@ class ClockSampler:
         except Exception:
             self.ident = str(device_index)
 
+    def _rows(self):
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                if not line.endswith("\n"):
+                    break  # a sample still being written
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 8:
+                    rows.append(parts)
+        return rows
+
+    def _wait_rows(self, n: int, limit_s: float) -> int:
+        deadline = time.monotonic() + limit_s
+        while True:
+            k = len(self._rows())
+            if k >= n or time.monotonic() > deadline or self.proc.poll() is not None:
+                return k
+            time.sleep(0.01)
+
     def start(self):
         try:
             fd, self.path = tempfile.mkstemp(prefix="qb_clocks_", suffix=".csv")
             os.close(fd)
-            self.fh = open(self.path, "w")
+            self.fh = open(self.path, "w", buffering=1)
             self.proc = subprocess.Popen(["nvidia-smi", "-i", self.ident, f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", str(self.INTERVAL_MS)],
                                          stdout=self.fh, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
-        time.sleep(0.3)
+            return
+        self._wait_rows(1, 10.0)
+        self.mark()
+
+    def mark(self):
+        """The timed region starts now: keep the newest sample and all later ones."""
+        if self.proc is not None:
+            self.first = max(len(self._rows()) - 1, 0)
 
     def stop(self):
         if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        self._wait_rows(len(self._rows()) + 1, 2.0)  # one sample taken after the region
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
         self.fh.close()
-        rows = []
-        with open(self.path) as f:
-            for line in f:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) >= 8:
-                    rows.append(parts)
+        rows = self._rows()[self.first:]
         os.unlink(self.path)
         sm = [float(r[0]) for r in rows if r[0].replace(".", "").isdigit()]
         mx = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
         reasons = sorted({n for r in rows for n, v in zip(names, r[4:8]) if v.lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows),
+                "reasons": reasons if rows else ["unsampled"], "samples": len(rows),
+                "interval_ms": self.INTERVAL_MS,
                 "power_w_max": max((float(r[2]) for r in rows if r[2].replace(".", "").isdigit()), default=None)}
 
 
@@ -547,14 +579,15 @@ def run_ours(args):
     warm_state(state, args.warmup, first_token, ctx)
     stream = torch.cuda.current_stream()
 
+    # Clocks are sampled across the first window and the repeats (the same K
+    # steps timed again in further windows; the line's value is the first
+    # window, as the contract asks, and the spread shows how stable it is).
     clocks = ClockSampler(local)
     clocks.start()
+    clocks.mark()
     t_dev = timed_steps(state, args.steps, first_token, ctx, world)
-    clk = clocks.stop()
-    # Repeats: the same K steps timed again in further windows (the line's
-    # value is the first window, as the contract asks; the spread shows how
-    # stable it is).
     windows = [t_dev] + [timed_steps(state, args.steps, first_token, ctx, world) for _ in range(args.repeats)]
+    clk = clocks.stop()
     rates = [B * args.steps / t for t in windows]
 
     # e2e: the same steps with host buffers (pinned H2D of the token, replay,
