@@ -559,19 +559,22 @@ def run_ours(args):
     total_steps = args.warmup + args.steps
     state = engine.new_state(ctx, total_steps + 2, capacity=ctx + 2 * total_steps + 8, batch=B)
     prefill_ms = None
-    if args.real_prefill and world == 1:
-        # the configuration's random prompt (seed 1) prefilled as dense blocks,
-        # timed with CUDA events after one untimed prefill of the same prompt
+    if args.real_prefill:
+        # the configuration's random prompt (seed 1) prefilled as dense blocks
+        # (tensor parallel under torchrun), timed with CUDA events after one
+        # untimed prefill of the same prompt; the max over ranks
         prompt = torch.randint(0, cfg.vocab, (ctx,), generator=torch.Generator().manual_seed(1)).to(dev)
         state.prefill(prompt)
         state.check()
+        torch.cuda.synchronize()
+        barrier(world)
         p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         p0.record()
         state.prefill(prompt)
         p1.record()
         torch.cuda.synchronize()
         state.check()
-        prefill_ms = p0.elapsed_time(p1)
+        prefill_ms = max_over_ranks(p0.elapsed_time(p1), world)
         first_token = state.read_token()[0]
     else:
         seeded_kv(state, cfg, ctx, dev)

@@ -51,6 +51,7 @@ SIGNATURES = {
     "qb_set_trace": (c_int, [c_void_p, c_void_p, c_size_t]),
     "qb_trace_labels": (ctypes.c_char_p, [c_void_p]),
     "qb_prefill_scratch_bytes": (c_int, [c_void_p, c_int, c_void_p]),
+    "qb_bind_prefill_weights": (c_int, [c_void_p, ctypes.POINTER(c_void_p), ctypes.POINTER(c_void_p), c_int]),
     "qb_prefill_batched": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_void_p, c_void_p, c_void_p,
                                    c_void_p]),
     "qb_gemm_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_void_p,

@@ -1,7 +1,10 @@
 // prefill_gemm.cuh — dense bf16 GEMM for prompt prefill on sm_100a's 5th-gen
 // tensor cores: D[T][N] = X[T][K] . W[N][K]^T with fp32 accumulation in tensor
 // memory (TMEM) and one bf16 rounding, plus the projection epilogues of the
-// decode path (store, + residual, SwiGLU over gate/up-interleaved rows).
+// decode path (store, + residual, SwiGLU over gate/up-interleaved rows, the
+// QKV heads' norm + RoPE + cache append); a tensor-parallel rank computes a
+// block of output columns over the whole input (unshard_cols_kernel lays the
+// all-gathered blocks out as whole rows).
 //
 // This is the prefill counterpart of the reference's dense projections
 // (dryft/engine/attention.py:92-98 uses torch linear for prompt rows; the
@@ -44,7 +47,8 @@ enum PrefillEpi : int { PG_STORE = 0, PG_RESIDUAL = 1, PG_SWIGLU = 2, PG_QKV_ROP
 struct PgArgs {
   int T, N, K;              // rows of X, rows of W, shared K
   bf16* out;                // STORE/RESIDUAL: [T][N]; SWIGLU: [T][N/2]
-  const bf16* residual;     // RESIDUAL: [T][N]
+  const bf16* residual;     // RESIDUAL: [T][res_stride] (res_stride 0: N)
+  int res_stride;
   int* err;
   // PG_QKV_ROPE: the QKV projection of prompt rows at positions p0 + row,
   // finished per head as the decode path does (q/k RMSNorm + RoPE, K/V to the
@@ -214,7 +218,7 @@ __device__ __forceinline__ void pg_epilogue_store(const PgArgs& a, int row, int 
     o.w = pack_bf16(v[6], v[7]);
     *reinterpret_cast<uint4*>(a.out + (size_t)row * a.N + n) = o;
   } else if constexpr (EPI == PG_RESIDUAL) {
-    const uint4 r = *reinterpret_cast<const uint4*>(a.residual + (size_t)row * a.N + n);
+    const uint4 r = *reinterpret_cast<const uint4*>(a.residual + (size_t)row * (a.res_stride ? a.res_stride : a.N) + n);
     const uint32_t* pr = reinterpret_cast<const uint32_t*>(&r);
     uint4 o;
     uint32_t* po = reinterpret_cast<uint32_t*>(&o);
@@ -387,6 +391,19 @@ __global__ void __launch_bounds__(kPgThreads, 1)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kPgTmemCols)
                  : "memory");
   }
+}
+
+// dst[t][r*C + c] = src[r][t][c]: the rank-major result of an NCCL all-gather
+// of every tensor-parallel rank's column block [T][C], laid out as whole rows
+// [T][n*C]. C is a multiple of 8 (one 16-byte vector per thread).
+__global__ void unshard_cols_kernel(const bf16* __restrict__ src, bf16* __restrict__ dst, int T, int C, int n) {
+  pdl_wait();
+  const long long W = (long long)C * n;
+  const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (i >= (long long)T * W) return;
+  const long long t = i / W, col = i - t * W;
+  const long long r = col / C, c = col - r * C;
+  *reinterpret_cast<uint4*>(dst + i) = *reinterpret_cast<const uint4*>(src + (r * T + t) * C + c);
 }
 
 }  // namespace qb

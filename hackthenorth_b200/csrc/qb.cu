@@ -294,12 +294,13 @@ bool make_q3_map(CUtensorMap* m, const void* q, int T, int Hq, int G, int rows) 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// extra: the fields of the QKV_ROPE epilogue and the residual stride (the rest are set here).
 cudaError_t launch_prefill_gemm(int epi, const bf16* x, const bf16* w, bf16* out, const bf16* residual, int T, int N,
-                                int K, int* err, cudaStream_t st, const PgArgs* rope = nullptr) {
+                                int K, int* err, cudaStream_t st, const PgArgs* extra = nullptr) {
   CUtensorMap tx, tw;
   if (!make_rows_map(&tx, x, T, K, kPgBM) || !make_rows_map(&tw, w, N, K, kPgBN)) return cudaErrorInvalidValue;
   PgArgs a;
-  if (rope != nullptr) a = *rope;
+  if (extra != nullptr) a = *extra;
   else std::memset(&a, 0, sizeof(a));
   a.T = T;
   a.N = N;
@@ -639,6 +640,8 @@ struct qb_ctx {
   float* pairs = nullptr;  // [2] this rank's {max, index}; then [2 * tp_size] gathered
   int sm_count = 148;
   std::vector<qb_layer_weights> layers;
+  // tensor-parallel block prefill: rows [r*H/n, (r+1)*H/n) of o and down
+  std::vector<const bf16*> o_rows, down_rows;
   const bf16* embed = nullptr;
   const bf16* final_norm = nullptr;
   const bf16* lm_head = nullptr;
@@ -1213,21 +1216,26 @@ int run_batch_pass(qb_ctx* c, const int64_t* ids, int64_t* pos, int64_t* tok_out
 // Batched prefill scratch: per prompt row xa, xb, xn [H]; qkv; q, attn [Hq*D];
 // act [F] (bf16).
 struct PrefillLayout {
-  size_t xa, xb, xn, qkv, q, attn, act, total;
+  // tensor parallel only: gath (all-gather results, rank-major), full (rows
+  // made whole), outl (this rank's [T][H/n] output columns)
+  size_t xa, xb, xn, q, attn, act, gath, full, outl, total;
 };
 PrefillLayout prefill_layout(const qb_ctx* c, int n) {
   const qb_config& g = c->lc;
   const size_t T = (size_t)n;
-  const size_t nqkv = (size_t)(g.n_heads + 2 * g.n_kv_heads) * g.head_dim;
   PrefillLayout L;
   size_t o = 0;
   L.xa = o; o = align_up(o + T * g.hidden * 2, 256);
   L.xb = o; o = align_up(o + T * g.hidden * 2, 256);
   L.xn = o; o = align_up(o + T * g.hidden * 2, 256);
-  L.qkv = o; o = align_up(o + T * nqkv * 2, 256);
   L.q = o; o = align_up(o + T * g.n_heads * g.head_dim * 2, 256);
   L.attn = o; o = align_up(o + T * g.n_heads * g.head_dim * 2, 256);
   L.act = o; o = align_up(o + T * g.ffn * 2, 256);
+  const bool tp = c->tp_size > 1;
+  const size_t wide = std::max<size_t>((size_t)c->cfg.n_heads * g.head_dim, std::max<size_t>(c->cfg.ffn, g.hidden));
+  L.gath = o; o = align_up(o + (tp ? T * wide * 2 : 0), 256);
+  L.full = o; o = align_up(o + (tp ? T * wide * 2 : 0), 256);
+  L.outl = o; o = align_up(o + (tp ? T * (g.hidden / c->tp_size) * 2 : 0), 256);
   L.total = o;
   return L;
 }
@@ -1236,20 +1244,65 @@ PrefillLayout prefill_layout(const qb_ctx* c, int n) {
 // blocks (tcgen05 GEMMs, causal flash attention), K/V appended; the last row
 // through the LM head; *position = n (DecodeState.prefill,
 // dryft/engine/decode.py:157-166, dryft/engine/prefill.py:6-26).
+// Tensor parallel: each rank runs its heads and FFN slice (QKV + RoPE, flash
+// attention, gate/up + SwiGLU); the o-proj and down projections run
+// column-parallel: the attention output and the SwiGLU activations of every
+// rank are all-gathered (NCCL) into whole rows, each rank computes output
+// columns [r*H/n, (r+1)*H/n) over the whole input with the same GEMM and
+// residual epilogue, and those blocks are all-gathered into the next
+// residual. Every value is then computed as on one GPU, so the K/V rows and
+// the first token equal the single-GPU prefill's; the last row's head is the
+// vocabulary-sharded argmax of the decode step.
 int run_prefill_batched(qb_ctx* c, const int64_t* ids, int n, uint8_t* scratch, int64_t* tok_out, int64_t* pos,
                         void* logits, cudaStream_t st) {
   const qb_config& g = c->lc;
   const int H = g.hidden, D = g.head_dim;
   const int nqkv = (g.n_heads + 2 * g.n_kv_heads) * D;
+  const int tp = c->tp_size;
+  const int Hr = H / tp;  // output columns of this rank under tensor parallelism
   const PrefillLayout P = prefill_layout(c, n);
   bf16* xa = reinterpret_cast<bf16*>(scratch + P.xa);
   bf16* xb = reinterpret_cast<bf16*>(scratch + P.xb);
   bf16* xn = reinterpret_cast<bf16*>(scratch + P.xn);
-  bf16* qkv = reinterpret_cast<bf16*>(scratch + P.qkv);
   bf16* q = reinterpret_cast<bf16*>(scratch + P.q);
   bf16* attn = reinterpret_cast<bf16*>(scratch + P.attn);
   bf16* act = reinterpret_cast<bf16*>(scratch + P.act);
+  bf16* gath = reinterpret_cast<bf16*>(scratch + P.gath);
+  bf16* full = reinterpret_cast<bf16*>(scratch + P.full);
+  bf16* outl = reinterpret_cast<bf16*>(scratch + P.outl);
   cudaError_t e;
+  ncclResult_t nr;
+  // every rank's column block src [n][C] -> dst [n][tp * C]
+  auto gather_cols = [&](const bf16* src, int C, bf16* dst, const char* what) -> int {
+    if ((nr = ncclAllGather(src, gath, (size_t)n * C, ncclBfloat16, c->comm, st)) != ncclSuccess)
+      return set_err(&c->msg, QB_ERR_CUDA, std::string("ncclAllGather: ") + ncclGetErrorString(nr));
+    const long long vecs = (long long)n * C * tp / 8;
+    if ((e = launch_ex(unshard_cols_kernel, dim3((unsigned)((vecs + 255) / 256)), dim3(256), 0, st,
+                       (const bf16*)gath, dst, n, C, tp)) != cudaSuccess)
+      return cuda_fail(&c->msg, e, what);
+    return QB_OK;
+  };
+  // out[n][H] = x . W^T + res: on one GPU x [n][K] and W whole; tensor
+  // parallel x is this rank's [n][K/tp] slice, w_rows this rank's output rows
+  auto project_residual = [&](const bf16* x, const void* w, const bf16* w_rows, int K, const bf16* res, bf16* out,
+                              const char* what) -> int {
+    if (tp == 1) {
+      if ((e = launch_prefill_gemm(PG_RESIDUAL, x, static_cast<const bf16*>(w), out, res, n, H, K, c->err, st)) !=
+          cudaSuccess)
+        return cuda_fail(&c->msg, e, what);
+      return QB_OK;
+    }
+    int rc2;
+    if ((rc2 = gather_cols(x, K / tp, full, what)) != QB_OK) return rc2;
+    PgArgs ra;
+    std::memset(&ra, 0, sizeof(ra));
+    ra.res_stride = H;
+    if ((e = launch_prefill_gemm(PG_RESIDUAL, full, w_rows, outl, res + (size_t)c->tp_rank * Hr, n, Hr, K, c->err,
+                                 st, &ra)) != cudaSuccess)
+      return cuda_fail(&c->msg, e, what);
+    return gather_cols(outl, Hr, out, what);
+  };
+  int rc;
   auto norm = [&](const bf16* x, const bf16* gain, bool gather) {
     NormRowsArgs na;
     std::memset(&na, 0, sizeof(na));
@@ -1314,19 +1367,21 @@ int run_prefill_batched(qb_ctx* c, const int64_t* ids, int n, uint8_t* scratch, 
                          ft_smem_bytes(), st, tq, c->tmk[l], c->tmv[l], ft)) != cudaSuccess)
         return cuda_fail(&c->msg, e, "prefill attention");
     }
-    if ((e = launch_prefill_gemm(PG_RESIDUAL, attn, static_cast<const bf16*>(w.o), xb, xa, n, H, g.n_heads * D,
-                                 c->err, st)) != cudaSuccess)
-      return cuda_fail(&c->msg, e, "prefill o");
+    if ((rc = project_residual(attn, w.o, tp > 1 ? c->o_rows[l] : nullptr, c->cfg.n_heads * D, xa, xb,
+                               "prefill o")) != QB_OK)
+      return rc;
     if ((e = norm(xb, static_cast<const bf16*>(w.post_norm), false)) != cudaSuccess)
       return cuda_fail(&c->msg, e, "prefill norm");
     if ((e = launch_prefill_gemm(PG_SWIGLU, xn, static_cast<const bf16*>(w.gate_up), act, nullptr, n, 2 * g.ffn, H,
                                  c->err, st)) != cudaSuccess)
       return cuda_fail(&c->msg, e, "prefill gate/up");
-    if ((e = launch_prefill_gemm(PG_RESIDUAL, act, static_cast<const bf16*>(w.down), xa, xb, n, H, g.ffn, c->err,
-                                 st)) != cudaSuccess)
-      return cuda_fail(&c->msg, e, "prefill down");
+    if ((rc = project_residual(act, w.down, tp > 1 ? c->down_rows[l] : nullptr, c->cfg.ffn, xb, xa,
+                               "prefill down")) != QB_OK)
+      return rc;
   }
-  // The last row through the final norm, the LM head and the argmax.
+  // The last row through the final norm, the LM head and the argmax (under
+  // tensor parallelism: this rank's vocabulary rows, then the (max, index)
+  // pairs of every rank and the lowest index among the largest values).
   GemvArgs a = gemv_args(c->lm_head, H, g.vocab, xa + (size_t)(n - 1) * H, nullptr, c->err);
   a.gain = c->final_norm;
   a.eps = g.rms_eps;
@@ -1335,7 +1390,19 @@ int run_prefill_batched(qb_ctx* c, const int64_t* ids, int n, uint8_t* scratch, 
   a.part_idx = c->head_idx;
   a.counter = c->counters + 64;
   a.token_out = tok_out;
+  if (tp > 1) {
+    a.token_out = nullptr;
+    a.row_base = c->tp_rank * g.vocab;
+    a.pair_out = c->pairs;
+  }
   if ((e = launch_gemv<EPI_ARGMAX>(a, c->sm_count, st)) != cudaSuccess) return cuda_fail(&c->msg, e, "prefill head");
+  if (tp > 1) {
+    if ((nr = ncclAllGather(c->pairs, c->pairs + 2, 2, ncclFloat32, c->comm, st)) != ncclSuccess)
+      return set_err(&c->msg, QB_ERR_CUDA, std::string("ncclAllGather: ") + ncclGetErrorString(nr));
+    // no peer-reduction words were written, so the epoch stays as it is
+    tp_pick_kernel<<<1, 32, 0, st>>>(c->pairs + 2, c->tp_size, tok_out, nullptr, nullptr, nullptr, 0, 0, c->err);
+    if ((e = cudaGetLastError()) != cudaSuccess) return cuda_fail(&c->msg, e, "prefill pick");
+  }
   if ((e = launch_ex(set_i64_kernel, dim3(1), dim3(1), 0, st, pos, (long long)n)) != cudaSuccess)
     return cuda_fail(&c->msg, e, "prefill position");
   return QB_OK;
@@ -1459,6 +1526,22 @@ int qb_bind_weights(qb_ctx* c, const qb_layer_weights* layers, int n_layers, con
   c->final_norm = static_cast<const bf16*>(final_norm);
   c->lm_head = static_cast<const bf16*>(lm_head);
   c->weights_bound = true;
+  return QB_OK;
+}
+
+int qb_bind_prefill_weights(qb_ctx* c, const void* const* o_rows, const void* const* down_rows, int n_layers) {
+  if (!c) return set_err(nullptr, QB_ERR_ARG, "ctx is NULL");
+  if (!o_rows || !down_rows || n_layers != c->cfg.n_layers)
+    return set_err(&c->msg, QB_ERR_ARG, "o_rows/down_rows tables do not match n_layers");
+  for (int l = 0; l < n_layers; ++l)
+    if (!ptr_ok(o_rows[l]) || !ptr_ok(down_rows[l]))
+      return set_err(&c->msg, QB_ERR_ARG, "prefill weight pointers must be 16-byte aligned and non-NULL");
+  c->o_rows.resize(n_layers);
+  c->down_rows.resize(n_layers);
+  for (int l = 0; l < n_layers; ++l) {
+    c->o_rows[l] = static_cast<const bf16*>(o_rows[l]);
+    c->down_rows[l] = static_cast<const bf16*>(down_rows[l]);
+  }
   return QB_OK;
 }
 
@@ -1661,8 +1744,13 @@ int qb_prefill_batched(qb_ctx* c, const int64_t* ids, int n, void* scratch, size
   if (rc) return rc;
   if (!ids || !token || !position || n <= 0) return set_err(&c->msg, QB_ERR_ARG, "bad prefill arguments");
   if (n > c->cap) return set_err(&c->msg, QB_ERR_CAPACITY, "prompt longer than the KV capacity");
-  if (c->tp_size != 1) return set_err(&c->msg, QB_ERR_UNSUPPORTED, "batched prefill runs on one GPU");
   if (c->batch != 1) return set_err(&c->msg, QB_ERR_UNSUPPORTED, "block prefill takes one sequence (qb_prefill: batched contexts)");
+  if (c->tp_size > 1) {
+    if ((int)c->o_rows.size() != c->cfg.n_layers)
+      return set_err(&c->msg, QB_ERR_ARG, "tensor-parallel block prefill needs qb_bind_prefill_weights");
+    if (c->cfg.hidden % c->tp_size || (c->cfg.hidden / c->tp_size) % 8)
+      return set_err(&c->msg, QB_ERR_UNSUPPORTED, "tensor-parallel block prefill needs hidden / tp_size a multiple of 8");
+  }
   if (!ptr_ok(scratch) || scratch_bytes < prefill_layout(c, n).total)
     return set_err(&c->msg, QB_ERR_ARG, "scratch smaller than qb_prefill_scratch_bytes(n) or unaligned");
   return run_prefill_batched(c, ids, n, static_cast<uint8_t*>(scratch), token, position, logits_out,

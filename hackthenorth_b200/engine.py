@@ -147,7 +147,8 @@ class DecodeState:
         """Write K/V for the prompt, emit the first token into ``self.token``
         and set ``position = len(prompt)``. ``batched`` forces (True) or
         forbids (False) the dense-block path; by default it is used for
-        prompts of ``BATCHED_PREFILL_MIN`` rows or more on one GPU. With
+        prompts of ``BATCHED_PREFILL_MIN`` rows or more (under tensor
+        parallelism too: every rank calls it with the same prompt). With
         ``batch`` B > 1, ``ids`` is ``[B, P]`` (equal prompt lengths) and the
         prompts run as P teacher-forced batched passes."""
         if self.batch > 1:
@@ -165,7 +166,7 @@ class DecodeState:
         self._ensure_bound()
         L = _lib.load()
         if batched is None:
-            batched = n >= self.BATCHED_PREFILL_MIN and self.engine.tp_size == 1
+            batched = n >= self.BATCHED_PREFILL_MIN
         if batched:
             need = _lib.c_size_t()
             _lib.check(L.qb_prefill_scratch_bytes(self.engine.ctx, n, _lib.ctypes.byref(need)), self.engine.ctx)
@@ -317,6 +318,11 @@ class Engine:
         w = self.weights
         _lib.check(L.qb_bind_weights(ctx, table, cfg.n_layers, w.embed.data_ptr(), w.final_norm.data_ptr(),
                                      w.lm_head.data_ptr()), ctx)
+        if tp_size > 1:
+            # the block prefill's column-parallel o-proj and down (row shards)
+            o_rows = (_lib.c_void_p * cfg.n_layers)(*[lw["o_rows"].data_ptr() for lw in w.layers])
+            down_rows = (_lib.c_void_p * cfg.n_layers)(*[lw["down_rows"].data_ptr() for lw in w.layers])
+            _lib.check(L.qb_bind_prefill_weights(ctx, o_rows, down_rows, cfg.n_layers), ctx)
         self._weight_table = table
         self.state: Optional[DecodeState] = None
         self._bound_state = None

@@ -106,7 +106,10 @@ class PackedWeights:
     KV heads [r*Hkv/n, (r+1)*Hkv/n) with their query heads (q/k/v rows of qkv,
     the matching input columns of o), FFN columns [r*F/n, (r+1)*F/n) (gate/up
     rows, down input columns) and vocabulary rows [r*V/n, (r+1)*V/n) of the
-    head; the embedding and the norm gains stay whole.
+    head; the embedding and the norm gains stay whole. The block prefill's
+    column-parallel projections also keep output rows [r*H/n, (r+1)*H/n) of o
+    and down over every input column (``o_rows``, ``down_rows``: 2 (H/n)(Hq*D +
+    F) bytes per layer more).
     """
 
     def __init__(self, cfg: ModelConfig, state: Dict[str, torch.Tensor], device="cuda:0",
@@ -151,6 +154,10 @@ class PackedWeights:
                 "gu": dev_bf16(interleave_gate_up(gate[fs], up[fs])),
                 "down": dev_bf16(down[:, fs]) if n > 1 else get(p + "mlp.down_proj.weight"),
             })
+            if n > 1:
+                hs = slice(r * (cfg.hidden // n), (r + 1) * (cfg.hidden // n))
+                self.layers[-1]["o_rows"] = dev_bf16(o[hs])
+                self.layers[-1]["down_rows"] = dev_bf16(down[hs])
 
     def nbytes(self) -> int:
         seen, total = set(), 0

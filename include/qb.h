@@ -82,7 +82,8 @@ int qb_create(const qb_config* cfg, int device, int tp_rank, int tp_size, qb_ctx
 int qb_nccl_unique_id(void* out, size_t bytes);
 
 /* Join the tensor-parallel group: one NCCL communicator per context, used for
- * an fp32 all-reduce of [H] after every o-proj and down projection and an
+ * an fp32 all-reduce of [H] after every o-proj and down projection (when the
+ * peer-memory reduction is off), the all-gathers of the block prefill and an
  * 8-byte all-gather of each rank's greedy candidate. No-op when tp_size == 1. */
 int qb_tp_init(qb_ctx* ctx, const void* unique_id);
 int qb_destroy(qb_ctx* ctx);
@@ -141,8 +142,23 @@ int qb_prefill(qb_ctx* ctx, const int64_t* ids, int n, int64_t* token, int64_t* 
  * (dryft/engine/attention.py:92-98, dryft/engine/prefill.py:6-26). Same
  * contract as qb_prefill (K/V for positions 0..n-1, first token to *token,
  * *position = n); scratch: a device buffer of qb_prefill_scratch_bytes(n)
- * bytes (prompt-row activations). Single GPU (tp_size 1). */
+ * bytes (prompt-row activations, plus the all-gather buffers under tensor
+ * parallelism). Under tensor parallelism every rank calls it with the same
+ * ids on its own stream, after qb_bind_prefill_weights: each rank runs its
+ * heads and FFN slice; the o-proj and down projections run column-parallel
+ * (the attention output and SwiGLU activations all-gathered into whole rows,
+ * each rank's [n][hidden/tp_size] output columns all-gathered into the next
+ * residual: four NCCL all-gathers per layer, then one 8-byte all-gather for
+ * the head), so the K/V rows and the first token equal the single-GPU
+ * prefill's; logits_out is this rank's [V/tp_size] shard. One sequence
+ * (batch 1). hidden / tp_size must be a multiple of 8. */
 int qb_prefill_scratch_bytes(const qb_ctx* ctx, int n, size_t* bytes);
+/* The row shards of the tensor-parallel block prefill's column-parallel
+ * projections, per layer: o_rows[l] = rows [r*H/n, (r+1)*H/n) of o
+ * ([H/n][Hq*D], every input column) and down_rows[l] = the same rows of down
+ * ([H/n][F]). Borrowed (no copy); required before qb_prefill_batched when
+ * tp_size > 1, unused otherwise. */
+int qb_bind_prefill_weights(qb_ctx* ctx, const void* const* o_rows, const void* const* down_rows, int n_layers);
 int qb_prefill_batched(qb_ctx* ctx, const int64_t* ids, int n, void* scratch, size_t scratch_bytes,
                        int64_t* token, int64_t* position, void* logits_out, void* stream);
 

@@ -36,7 +36,7 @@ def _ulps(got, ref):
 
 
 @pytest.mark.parametrize("T,N,K", [(128, 256, 64), (128, 256, 4096), (200, 512, 1024), (1000, 6144, 4096),
-                                   (4096, 1024, 12288), (37, 2048, 512)])
+                                   (4096, 1024, 12288), (37, 2048, 512), (64, 128, 1024)])
 def test_gemm_matches_fp32_reference(built_lib, T, N, K):
     g = torch.Generator(device=DEV).manual_seed(T * 7 + N + K)
     x = torch.randn(T, K, generator=g, device=DEV).to(BF16)

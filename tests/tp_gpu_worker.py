@@ -5,7 +5,12 @@ rank 0 writes the tokens to the path given on the command line.
 With a third argument ``verify``: the speculative stream (verify passes with a
 seeded synthetic draft of the golden continuation) and one 5-row verify pass
 (predictions, the full logits gathered from the vocabulary shards, the rows'
-K/V gathered from the head shards), written by rank 0 as .npz."""
+K/V gathered from the head shards), written by rank 0 as .npz.
+
+With ``prefill``: a seeded 300-row prompt through the tensor-parallel block
+prefill (first token, last-row logits gathered from the vocabulary shards,
+every prompt row's K/V gathered from the head shards) and the first token of
+the same prompt run row by row, written by rank 0 as .npz."""
 import json
 import os
 import sys
@@ -43,8 +48,11 @@ def main():
     state = random_state_dict(cfg, 0)  # CPU draw, identical on every rank and in the golden vectors
     engine = Engine(None, f"cuda:{local}", cfg=cfg, state=state, tp_rank=dist.get_rank(),
                     tp_size=dist.get_world_size(), unique_id=uid)
-    if mode == "verify":
-        verify_case(engine, cfg, prompt, g["tokens"].tolist(), out_path)
+    if mode in ("verify", "prefill"):
+        if mode == "verify":
+            verify_case(engine, cfg, prompt, g["tokens"].tolist(), out_path)
+        else:
+            prefill_case(engine, cfg, out_path)
         del engine
         torch.cuda.synchronize()
         dist.destroy_process_group()
@@ -66,6 +74,31 @@ def _gather(t, dim):
     parts = [torch.empty_like(t) for _ in range(dist.get_world_size())]
     dist.all_gather(parts, t.contiguous())
     return torch.cat(parts, dim=dim)
+
+
+PREFILL_ROWS = 300
+
+
+def prefill_case(engine, cfg, out_path):
+    dev = engine.device
+    T = PREFILL_ROWS
+    prompt = torch.randint(0, cfg.vocab, (T,), generator=torch.Generator().manual_seed(T))
+    st = engine.new_state(T, 4, keep_logits=True)
+    st.prefill(prompt.to(dev), batched=True)
+    st.check()
+    token = st.read_token()[0]
+    position = int(st.position.item())
+    logits = _gather(st.logits.reshape(1, -1), 1)[0]
+    keys = _gather(st.keys[:, :, :T], 1)
+    values = _gather(st.values[:, :, :T], 1)
+    rows = engine.new_state(T, 4)
+    rows.prefill(prompt.to(dev), batched=False)
+    rows.check()
+    token_rows = rows.read_token()[0]
+    if dist.get_rank() == 0:
+        np.savez(out_path, prompt=prompt.numpy(), token=token, token_rows=token_rows, position=position,
+                 logits=logits.float().cpu().numpy(), keys=keys.float().cpu().numpy(),
+                 values=values.float().cpu().numpy())
 
 
 def verify_case(engine, cfg, prompt, gold, out_path):
