@@ -19,6 +19,12 @@
 //    projection's long rows) each slot also carries the same 2048 columns of
 //    the input rows, copied after griddepcontrol.wait (the slot's full barrier
 //    then takes two arrivals) and normalised in the slot when a gain is given;
+//  * resident rows of at most two pieces (K <= 4096) go one step further: each
+//    warp loads the B fragments of its columns of every piece into registers
+//    once (32 registers), and the shared memory that held the rows becomes a
+//    third ring slot, so two 64 KB stages are in flight while one is consumed
+//    (the producer fills that slot for the first time once all consumer warps
+//    have arrived on a barrier after their fragment loads);
 //  * consumer warp w takes columns [128w, 128w+128) of the piece: 8 k-steps of
 //    mma.sync m16n8k16 with A = 16 weight rows (ldmatrix) and B = the Q input
 //    rows transposed (ldmatrix of the row-major rows), accumulating a 16 x 8
@@ -38,6 +44,7 @@ constexpr int kRowsKC = 2048;
 constexpr int kRowsPitch = kRowsKC * 2 + 16;  // padded row piece
 constexpr int kRowsStageBytes = (16 + 8) * kRowsPitch;
 constexpr int kRowsStages = 2;
+constexpr int kRowsRegStages = 3;  // register-fragment mode: the resident rows' space is the third slot
 constexpr int kRowsMaxQ = 8;
 constexpr int kRowsBarrierId = 1;
 constexpr int kRowsResidentBytes = kRowsMaxQ * (4096 + 8) * 2;  // resident input rows
@@ -47,8 +54,13 @@ constexpr int kRowsRingBytes = kRowsStages * kRowsStageBytes > kRowsStages * 16 
                                    ? kRowsStages * kRowsStageBytes
                                    : kRowsStages * 16 * kRowsPitch + kRowsResidentBytes;
 
+static_assert(kRowsRegStages * 16 * kRowsPitch <= kRowsRingBytes, "three 16-row slots fit the ring");
+static_assert(kRowsResidentBytes <= 16 * kRowsPitch, "the resident rows fit one 16-row slot");
+
 // Input rows resident in shared memory (else carried by every slot).
 __host__ __device__ inline bool rows_resident(int Q, int K) { return (size_t)Q * (K + 8) * 2 <= kRowsResidentBytes; }
+// Resident rows whose B fragments stay in registers (at most two pieces).
+__host__ __device__ inline bool rows_in_regs(int Q, int K) { return rows_resident(Q, K) && K <= 2 * kRowsKC; }
 
 struct RowsArgs {
   const bf16* w;            // [rows][K]
@@ -88,25 +100,47 @@ __device__ __forceinline__ size_t rows_tp_slot(const RowsArgs& a, int sender, in
          (((size_t)a.tp_parity * a.tp.size + sender) * kRowsMaxQ + q) * a.hidden;
 }
 
-// ring, two reduction buffers, row factors, barriers, scratch.
+// ring, two reduction buffers, row factors, barriers (full, empty, the
+// fragments-loaded barrier), scratch.
 __host__ inline size_t rows_smem_bytes() {
-  return 16 + (size_t)kRowsRingBytes + 2 * 16 * 16 * 8 * 4 + kRowsMaxQ * 4 + 2 * kRowsStages * 8 + 256 * 4;
+  return 16 + (size_t)kRowsRingBytes + 2 * 16 * 16 * 8 * 4 + kRowsMaxQ * 4 + (2 * kRowsRegStages + 1) * 8 + 256 * 4;
+}
+
+// One 2048-column piece of a 16-row block for warp w's columns [128w, 128w+128):
+// 8 k-steps, A = 16 weight rows from the slot, B = the input-row fragments.
+__device__ __forceinline__ void rows_piece_mma(float (&acc)[4], const uint8_t* slot, int warp, int lane,
+                                               const uint32_t (&bq)[4][4]) {
+#pragma unroll
+  for (int k2 = 0; k2 < 4; ++k2) {
+    const int col = warp * 128 + k2 * 32;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint32_t af[4];
+      const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
+      ldsm_x4(af, slot + row * kRowsPitch + (col + h * 16 + (lane >> 4) * 8) * 2);
+      mma_bf16_16816(acc, af, bq[k2][2 * h], bq[k2][2 * h + 1]);
+    }
+  }
 }
 
 template <int EPI>
 __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const RowsArgs a) {
   extern __shared__ __align__(16) uint8_t smem_rows[];
   const bool resident = rows_resident(a.Q, a.K);
+  const bool regs = rows_in_regs(a.Q, a.K);  // B fragments in registers, three ring slots
+  const int NS = regs ? kRowsRegStages : kRowsStages;
   const int stage_bytes = resident ? 16 * kRowsPitch : kRowsStageBytes;
   const int xpitch = (a.K + 8) * 2;  // resident row pitch (bytes)
   uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_rows) + 15) & ~uintptr_t(15));
-  uint8_t* xres = ring + kRowsStages * 16 * kRowsPitch;  // resident rows [Q][K + 8] (resident mode)
+  // resident rows [Q][K + 8] (resident mode); in register mode the third slot
+  uint8_t* xres = ring + kRowsStages * 16 * kRowsPitch;
   float* red = reinterpret_cast<float*>(ring + kRowsRingBytes);
   // red: two buffers [16 warps][16 rows][8], alternating by block
   float* inv = red + 2 * 16 * 16 * 8;  // [8]
   uint64_t* full = reinterpret_cast<uint64_t*>(inv + kRowsMaxQ);
-  uint64_t* empty = full + kRowsStages;
-  float* misc = reinterpret_cast<float*>(empty + kRowsStages);  // 256 floats
+  uint64_t* empty = full + kRowsRegStages;
+  uint64_t* xfree = empty + kRowsRegStages;  // register mode: every consumer warp holds its fragments
+  float* misc = reinterpret_cast<float*>(xfree + 1);  // 256 floats
   volatile int* flags = reinterpret_cast<volatile int*>(misc + 240);
 
   const int tid = threadIdx.x;
@@ -127,10 +161,11 @@ __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const RowsAr
   const int nstage = nblk * nkc;
 
   if (tid == 0) {
-    for (int s = 0; s < kRowsStages; ++s) {
+    for (int s = 0; s < kRowsRegStages; ++s) {
       mbar_init(&full[s], resident ? 1 : 2);  // weights (+ the slot's input rows)
       mbar_init(&empty[s], kRowsWarps);
     }
+    mbar_init(xfree, kRowsWarps);
     fence_mbar_init();
     flags[0] = 0;
     flags[1] = 0;
@@ -141,7 +176,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const RowsAr
     // ---------------- producer warp: lanes 0..15 weight rows, 16..16+Q-1 input rows
     const uint64_t policy = policy_evict_first();
     auto issue_w = [&](int c) {
-      const int s = c % kRowsStages, blk = c / nkc, kc = c - blk * nkc;
+      const int s = c % NS, blk = c / nkc, kc = c - blk * nkc;
       const int nr = min(16, nrows - blk * 16);
       const int c0 = kc * kRowsKC;
       const uint32_t piece = (uint32_t)min(kRowsKC, K - c0) * 2;
@@ -154,7 +189,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const RowsAr
     const bf16* xrow = nullptr;  // this lane's input row (lanes 16..16+Q-1)
     auto issue_x = [&](int c) {
       if (resident) return;
-      const int s = c % kRowsStages, kc = c % nkc;
+      const int s = c % NS, kc = c % nkc;
       const int c0 = kc * kRowsKC;
       const uint32_t piece = (uint32_t)min(kRowsKC, K - c0) * 2;
       if (lane == 0) mbar_arrive_expect_tx(&full[s], piece * Q);
@@ -162,8 +197,10 @@ __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const RowsAr
       if (lane >= 16 && lane < 16 + Q)
         bulk_g2s(ring + (size_t)s * kRowsStageBytes + lane * kRowsPitch, xrow + c0, piece, &full[s], policy);
     };
+    // weights are immutable: the first two stages go before the wait (in
+    // register mode the third slot still holds the input rows then)
     const int pre = min(nstage, kRowsStages);
-    for (int c = 0; c < pre; ++c) issue_w(c);  // weights are immutable: before the wait
+    for (int c = 0; c < pre; ++c) issue_w(c);
     pdl_wait();
     pdl_trigger();
     if (lane >= 16 && lane < 16 + Q) {
@@ -183,9 +220,13 @@ __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const RowsAr
     int issued = pre;
     bool ok = true;
     for (int c = pre; c < nstage; ++c) {
-      const int s = c % kRowsStages;
+      const int s = c % NS;
       int good = 1;
-      if (lane == 0) good = mbar_wait(&empty[s], ((c / kRowsStages) - 1) & 1, a.err, DEV_TIMEOUT_GEMV_EMPTY) ? 1 : 0;
+      if (lane == 0)
+        good = (c < NS ? mbar_wait(xfree, 0, a.err, DEV_TIMEOUT_GEMV_EMPTY)  // first fill of the rows' slot
+                       : mbar_wait(&empty[s], ((c / NS) - 1) & 1, a.err, DEV_TIMEOUT_GEMV_EMPTY))
+                   ? 1
+                   : 0;
       good = __shfl_sync(0xffffffffu, good, 0);
       if (!good) {
         ok = false;
@@ -197,8 +238,7 @@ __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const RowsAr
     }
     if (lane == 0) {
       // Keep shared memory alive until the copies in flight land.
-      for (int c = (issued > kRowsStages ? issued - kRowsStages : 0); c < issued; ++c)
-        mbar_wait(&full[c % kRowsStages], (c / kRowsStages) & 1, nullptr, 0);
+      for (int c = (issued > NS ? issued - NS : 0); c < issued; ++c) mbar_wait(&full[c % NS], (c / NS) & 1, nullptr, 0);
     }
     (void)ok;
     return;
@@ -262,6 +302,25 @@ __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const RowsAr
     }
   }
 
+  // Register mode: this warp's B fragments of every piece (rows >= Q repeat
+  // row Q-1, as below), then the rows' slot is handed to the producer.
+  uint32_t bqr[2][4][4];
+  if (regs) {
+    const int qrow = min(lane & 7, Q - 1);
+#pragma unroll
+    for (int kc = 0; kc < 2; ++kc)
+#pragma unroll
+      for (int k2 = 0; k2 < 4; ++k2) {
+        const int col = kc * kRowsKC + warp * 128 + k2 * 32;
+        if (kc < nkc && warp * 128 < min(kRowsKC, K - kc * kRowsKC))
+          ldsm_x4(bqr[kc][k2], xres + qrow * xpitch + (col + (lane >> 3) * 8) * 2);
+        else
+          bqr[kc][k2][0] = bqr[kc][k2][1] = bqr[kc][k2][2] = bqr[kc][k2][3] = 0u;
+      }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(xfree);
+  }
+
   // Running argmax per input row (thread t of the first 128 owns row t & 7).
   float best = -INFINITY;
   int best_i = 0x7fffffff;
@@ -271,8 +330,8 @@ __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const RowsAr
   for (int blk = 0; blk < nblk && ok; ++blk) {
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
     for (int kc = 0; kc < nkc; ++kc, ++c) {
-      const int s = c % kRowsStages;
-      if (!mbar_wait(&full[s], (c / kRowsStages) & 1, a.err, DEV_TIMEOUT_GEMV_FULL)) flags[0] = 1;
+      const int s = c % NS;
+      if (!mbar_wait(&full[s], (c / NS) & 1, a.err, DEV_TIMEOUT_GEMV_FULL)) flags[0] = 1;
       uint8_t* slot = ring + (size_t)s * stage_bytes;
       const int c0 = kc * kRowsKC;
       // B operand rows: the resident rows at column c0, or the slot's copy
@@ -301,7 +360,12 @@ __global__ void __launch_bounds__(kRowsThreads, 1) gemv_rows_kernel(const RowsAr
         }
         named_barrier(kRowsBarrierId, kRowsWarps * 32);
       }
-      if (warp * 128 < ncols && flags[0] == 0) {
+      if (regs && warp * 128 < ncols && flags[0] == 0) {
+        if (kc == 0)
+          rows_piece_mma(acc, slot, warp, lane, bqr[0]);
+        else
+          rows_piece_mma(acc, slot, warp, lane, bqr[1]);
+      } else if (warp * 128 < ncols && flags[0] == 0) {
         // ldmatrix reads 8 input rows; rows >= Q repeat row Q-1 (their output
         // columns are never used), so no address leaves the Q stored rows.
         const int qrow = min(lane & 7, Q - 1);
