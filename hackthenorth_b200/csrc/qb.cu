@@ -53,7 +53,8 @@ constexpr size_t kScrCounters = 256;       // unsigned[192]
 constexpr size_t kScrHeadVal = 1024;       // float[1024]
 constexpr size_t kScrHeadIdx = 5120;       // int[1024]
 constexpr size_t kScrAttnLse = 9216;       // float[16384]
-constexpr size_t kScrAttnO = 9216 + 65536; // float[...] up to the end
+constexpr size_t kScrAttnO = 9216 + 65536; // float[...] up to the tickets
+constexpr size_t kScrTickets = kOpScratchBytes - 4096;  // unsigned[64 heads x 16]: rows-kernel cluster merges
 constexpr int kMaxAttnCtas = 512;
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -2041,11 +2042,20 @@ static int op_attention(const void* qkv, const void* q, const void* q_norm, cons
   a.cap = cap;
   a.splits = splits;
   cudaError_t e;
-  // Short caches without the prologue: the cluster kernel of the verify pass
-  // (DSMEM merge, no global round trip); long caches keep the split kernel,
+  // Without the prologue the cluster kernel of the verify pass runs short
+  // caches (one cluster per KV head, DSMEM merge, no global round trip) and,
+  // above 16 rows per KV head, long caches too, as several clusters per KV
+  // head that merge through the partial rows and the tickets at the end of
+  // the scratch (the split kernel's 17..32-row variant streams at a fraction
+  // of the copy rate). Long caches of at most 16 rows keep the split kernel,
   // whose grid covers every SM.
-  const int rcs = (!pro && rows <= kVaMaxRows && cap < kOpRowsMaxCap) ? rows_cluster_size(hkv) : 0;
-  if (rcs > 0)
+  const int rcs = (!pro && rows <= kVaMaxRows && (cap < kOpRowsMaxCap || rows > 16)) ? rows_cluster_size(hkv) : 0;
+  if (rcs > 0 && cap >= kOpRowsMaxCap) {
+    a.part_splits = splits;  // partial rows per KV head: splits x kVaMaxRows
+    a.tickets = reinterpret_cast<unsigned*>(s + kScrTickets);
+    rows_attn_shape(a, rcs);
+  }
+  if (rcs > 0 && (cap < kOpRowsMaxCap || a.clusters > 1))
     e = launch_attn_rows(dk, dv, a, rcs, static_cast<cudaStream_t>(stream));
   else
     e = launch_attn(tk, tv, &dk, &dv, a, pro, static_cast<cudaStream_t>(stream));
