@@ -180,6 +180,10 @@ __global__ void __launch_bounds__(kVaThreads, 1)
         }
         __syncwarp();
       }
+      // Scores and softmax of every n-tile first (P^T fragments kept), then
+      // P.V with each V fragment read once for all n-tiles; every output
+      // accumulator still adds the two key m-tiles in the same order.
+      uint32_t pb[NT][2][2];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         uint32_t qb[8][2];
@@ -247,23 +251,23 @@ __global__ void __launch_bounds__(kVaThreads, 1)
           o[j][nt][2] *= corr[0];
           o[j][nt][3] *= corr[1];
         }
-        uint32_t pb[2][2];
 #pragma unroll
         for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-          for (int h = 0; h < 2; ++h) pb[mt][h] = movmatrix_trans(pack_bf16(p[mt][h][0], p[mt][h][1]));
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
-#pragma unroll
-          for (int dt = 0; dt < 8; ++dt) {
-            const int mi = lane >> 3;
-            const int key = mt * 16 + (lane & 7) + (mi >> 1) * 8;
-            const int ch = ((dt & 3) << 1) + (mi & 1);
-            uint32_t va[4];
-            ldsm_x4_t(va, stage + (2 + (dt >> 2)) * kDecSubTile + swz(key, ch));
-            mma_bf16_16816(o[dt][nt], va, pb[mt][0], pb[mt][1]);
-          }
+          for (int h = 0; h < 2; ++h) pb[nt][mt][h] = movmatrix_trans(pack_bf16(p[mt][h][0], p[mt][h][1]));
       }
+#pragma unroll
+      for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+        for (int dt = 0; dt < 8; ++dt) {
+          const int mi = lane >> 3;
+          const int key = mt * 16 + (lane & 7) + (mi >> 1) * 8;
+          const int ch = ((dt & 3) << 1) + (mi & 1);
+          uint32_t va[4];
+          ldsm_x4_t(va, stage + (2 + (dt >> 2)) * kDecSubTile + swz(key, ch));
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) mma_bf16_16816(o[dt][nt], va, pb[nt][mt][0], pb[nt][mt][1]);
+        }
       __syncwarp();
       if (lane == 0 && c + kVaStages < nst) {
         fence_proxy_async_smem();  // this warp's reads of the slot precede the refill
