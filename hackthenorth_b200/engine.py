@@ -357,7 +357,9 @@ class Engine:
 
         As in the reference, one sequence speculates by default: a
         ``PromptLookup`` over the prompt and the emitted tokens proposes
-        ``draft_width(max_new_tokens)`` tokens (up to 7), one verify pass
+        ``draft_width(max_new_tokens)`` tokens (up to 7; at most 5 when the
+        model has 4 query heads per KV head, so that the verify pass stays on
+        the rows attention kernel: ``fast_verify_drafts``), one verify pass
         checks them, and the accepted prefix plus one target token is emitted;
         without a proposal it takes a plain decode step. The emitted sequence
         is the plain greedy one (verification only accepts tokens the target
@@ -379,9 +381,10 @@ class Engine:
         if not prompts[0]:
             raise ValueError("the prompt must hold at least one token")
         if draft_tokens is None:
-            from .speculate import draft_width
+            from .speculate import draft_width, fast_verify_drafts
 
-            draft_tokens = draft_width(max_new_tokens) if B == 1 else 0
+            width = min(draft_width(max_new_tokens), fast_verify_drafts(self.cfg.n_heads, self.cfg.n_kv_heads))
+            draft_tokens = width if B == 1 else 0
         if draft_tokens > 0:
             yield from self._generate_speculative(prompts, max_new_tokens, draft_tokens, drafter)
             return

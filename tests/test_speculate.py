@@ -67,6 +67,17 @@ def test_backoff_matches_naive_history_search_after_every_append(width):
         lookup.append(tok)
 
 
+def test_default_width_keeps_the_verify_pass_on_the_rows_attention_kernel():
+    from hackthenorth_b200.speculate import fast_verify_drafts
+
+    assert fast_verify_drafts(32, 8) == 5     # Qwen3-4B / 8B: 6 rows x 4 heads = 24 rows per KV head
+    assert fast_verify_drafts(16, 8) == 11    # Qwen3-0.6B: the reference's 7 fit
+    assert fast_verify_drafts(64, 8) == 2
+    assert fast_verify_drafts(32, 1) == 0     # a group of 32 leaves no room for drafts
+    assert min(draft_width(100), fast_verify_drafts(16, 8)) == 7
+    assert min(draft_width(100), fast_verify_drafts(32, 8)) == 5
+
+
 def test_draft_width_caps_short_requests():
     assert [draft_width(n) for n in (1, 2, 3, 9, 100)] == [0, 0, 1, 7, 7]
     assert draft_width(100, 4) == 4

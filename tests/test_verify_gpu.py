@@ -122,6 +122,24 @@ def test_speculative_generate_equals_plain_greedy(built_lib):
         assert len(list(engine.generate([rep], n, draft_tokens=4))) == n
 
 
+def test_default_speculation_width_with_four_query_heads_per_kv_head(built_lib):
+    """With 4 query heads per KV head (the 4B and 8B shapes) the default
+    prompt-lookup speculation proposes at most 5 tokens, so every verify pass
+    holds at most 6 rows (24 rows per KV head, the rows attention kernel), and
+    the emitted stream is the plain greedy one."""
+    from hackthenorth_b200.config import QWEN3_SMALL
+    from hackthenorth_b200.engine import Engine
+
+    cfg = dataclasses.replace(QWEN3_SMALL, name="qwen3-small-g4", n_kv_heads=2)
+    engine = Engine.from_random(cfg, seed=0)
+    g = torch.Generator().manual_seed(5)
+    rep = (torch.randint(0, cfg.vocab, (6,), generator=g).tolist() * 5)[:30]
+    plain = [s[0] for s in engine.generate([rep], 24, draft_tokens=0)]
+    default = [s[0] for s in engine.generate([rep], 24)]
+    assert default == plain
+    assert 2 <= engine.state._verify_n <= 6
+
+
 def test_verify_rejects_bad_arguments(built_lib):
     from hackthenorth_b200 import _lib
     from hackthenorth_b200.config import QWEN3_SMALL
