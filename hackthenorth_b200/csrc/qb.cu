@@ -2050,13 +2050,14 @@ static int op_attention(const void* qkv, const void* q, const void* q_norm, cons
   // of the copy rate). Long caches of at most 16 rows keep the split kernel,
   // whose grid covers every SM.
   const int rcs = (!pro && rows <= kVaMaxRows && (cap < kOpRowsMaxCap || rows > 16)) ? rows_cluster_size(hkv) : 0;
+  AttnArgs ra = a;  // the rows kernel's shape (the split kernel keeps `splits`)
   if (rcs > 0 && cap >= kOpRowsMaxCap) {
-    a.part_splits = splits;  // partial rows per KV head: splits x kVaMaxRows
-    a.tickets = reinterpret_cast<unsigned*>(s + kScrTickets);
-    rows_attn_shape(a, rcs);
+    ra.part_splits = splits;  // partial rows per KV head: splits x kVaMaxRows
+    ra.tickets = reinterpret_cast<unsigned*>(s + kScrTickets);
+    rows_attn_shape(ra, rcs);
   }
-  if (rcs > 0 && (cap < kOpRowsMaxCap || a.clusters > 1))
-    e = launch_attn_rows(dk, dv, a, rcs, static_cast<cudaStream_t>(stream));
+  if (rcs > 0 && (cap < kOpRowsMaxCap || ra.clusters > 1))
+    e = launch_attn_rows(dk, dv, ra, rcs, static_cast<cudaStream_t>(stream));
   else
     e = launch_attn(tk, tv, &dk, &dv, a, pro, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(nullptr, e, "attention launch");

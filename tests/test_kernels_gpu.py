@@ -199,12 +199,15 @@ def test_grouped_attention_long_contexts_match_fp32(cap, queries):
 
 
 @pytest.mark.parametrize("hq,hkv,cap,queries,last", [(32, 8, 20000, 6, 19999), (16, 2, 30000, 3, 25000),
-                                                     (8, 1, 17000, 3, 16990), (32, 8, 16384, 5, 9000)])
+                                                     (8, 1, 17000, 3, 16990), (32, 8, 16384, 5, 9000),
+                                                     (48, 12, 20000, 5, 19999)])
 def test_grouped_attention_long_caches_many_rows_match_fp32(hq, hkv, cap, queries, last):
     """Long caches with 17..24 query rows per KV head run the rows kernel as
     several clusters per KV head, merged through the op scratch's partial rows
     and tickets (8, 2 and 1 KV heads; 24 rows; live keys well below the
-    capacity): within 1e-2 relative of fp32 attention, slots past the last
+    capacity; 12 KV heads, where no shape of several clusters may beat one
+    cluster per head and the split kernel then runs with the op's split
+    count): within 1e-2 relative of fp32 attention, slots past the last
     position (NaN here) never read, and a second call agrees (the merge
     tickets are left at zero)."""
     from hackthenorth_b200 import ops
