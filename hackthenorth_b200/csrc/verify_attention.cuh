@@ -162,6 +162,24 @@ __global__ void __launch_bounds__(kVaThreads, 1)
       l[nt][0] = l[nt][1] = 0.f;
     }
     const float scale = 0.12751743082459868f;  // log2(e) / sqrt(128)
+    // Query fragments: up to two n-tiles stay in registers for the whole key
+    // loop; three are read from shared memory per stage (the registers hold
+    // the 96 output accumulators then).
+    constexpr int NQH = NT <= 2 ? NT : 1;
+    uint32_t qh[NQH][8][2];
+    if constexpr (NT <= 2) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t r4[4];
+          ldsm_x4(r4, qs + (nt * 8 + (lane & 7)) * kAttnD + j * 32 + (lane >> 3) * 8);
+          qh[nt][2 * j][0] = r4[0];
+          qh[nt][2 * j][1] = r4[1];
+          qh[nt][2 * j + 1][0] = r4[2];
+          qh[nt][2 * j + 1][1] = r4[3];
+        }
+    }
     const int s = warp;
     uint8_t* stage = ring + s * kDecStageBytes;
     for (int c = warp; c < nst; c += kVaWarps) {
@@ -187,14 +205,22 @@ __global__ void __launch_bounds__(kVaThreads, 1)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         uint32_t qb[8][2];
+        if constexpr (NT <= 2) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint32_t r4[4];
-          ldsm_x4(r4, qs + (nt * 8 + (lane & 7)) * kAttnD + j * 32 + (lane >> 3) * 8);
-          qb[2 * j][0] = r4[0];
-          qb[2 * j][1] = r4[1];
-          qb[2 * j + 1][0] = r4[2];
-          qb[2 * j + 1][1] = r4[3];
+          for (int j = 0; j < 8; ++j) {
+            qb[j][0] = qh[nt][j][0];
+            qb[j][1] = qh[nt][j][1];
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t r4[4];
+            ldsm_x4(r4, qs + (nt * 8 + (lane & 7)) * kAttnD + j * 32 + (lane >> 3) * 8);
+            qb[2 * j][0] = r4[0];
+            qb[2 * j][1] = r4[1];
+            qb[2 * j + 1][0] = r4[2];
+            qb[2 * j + 1][1] = r4[3];
+          }
         }
         float sc[2][2][4];
 #pragma unroll
